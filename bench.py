@@ -1,0 +1,251 @@
+"""Flagship benchmark: training samples/s of the ~1B nuVLA-style model.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl native|reference]
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
+
+Prints ONE JSON line on rank 0. ``value`` is whole-job samples/s from CUDA-event
+time of exactly K optimizer steps (each = grad-accum micro-steps of batch B per
+GPU, DDP with no_sync accumulation, AdamW with clip 1.0), max over ranks, with
+device-resident synthetic inputs that are far larger than L2 (the activations
+of one micro-step alone are tens of GB). ``e2e`` is the same metric through the
+public ``Trainer.step`` API with each step's inputs copied from pinned host
+memory and the loss read back to the host, every step.
+
+``--impl reference`` runs the reference implementation installed (unmodified)
+in baseline/_ref through its own modules, torch DDP and fused AdamW under bf16
+autocast (baseline/ref_arm.py), timed the same way.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+BASELINE_SAMPLES_PER_S = 158.05  # reference train samples/s (optimised preset, 1x H100 NVL, 77.3M)
+METRIC = "train samples/sec (device-timed, max over ranks)"
+
+
+def parse(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--model-config", default="1b")
+    ap.add_argument("--batch-size", type=int, default=8)
+    ap.add_argument("--grad-accum", type=int, default=4)
+    ap.add_argument("--bucket-mb", type=float, default=100.0)
+    ap.add_argument("--comm", default="auto")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--json-out", default=None)
+    return ap.parse_args(argv)
+
+
+# ----------------------------------------------------------------------
+class ClockSampler:
+    """Samples SM clock / power / throttle reasons with nvidia-smi while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_ids: list[str]):
+        self.ids = gpu_ids
+        self.rows: list[list[str]] = []
+        self.proc = None
+        self.th = None
+
+    def start(self):
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+        if self.ids:
+            cmd += ["-i", ",".join(self.ids)]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:  # noqa: BLE001 - no nvidia-smi: no clock record
+            self.proc = None
+            return
+        self.th = threading.Thread(target=self._read, daemon=True)
+        self.th.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:  # noqa: BLE001
+            self.proc.kill()
+        if self.th:
+            self.th.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        load = [s for s in sm if mx and s > 0.3 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def visible_gpu_ids() -> list[str]:
+    v = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if v:
+        return [x.strip() for x in v.split(",") if x.strip()]
+    return [str(i) for i in range(torch.cuda.device_count())]
+
+
+def timed_steps(fn, k: int, device) -> float:
+    """CUDA-event time (ms) of k calls of fn, barrier + synchronize on both sides."""
+    if dist.is_initialized():
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(k):
+        fn()
+    e1.record()
+    torch.cuda.synchronize(device)
+    if dist.is_initialized():
+        dist.barrier()
+    return e0.elapsed_time(e1)
+
+
+def max_ranks(v: float, device) -> float:
+    if not dist.is_initialized():
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------
+def run_native(args) -> dict:
+    sys.path.insert(0, ROOT)
+    from nuvla_forge_b200 import _native as nat
+    from nuvla_forge_b200.data import SampleSpec, SyntheticBatchSource
+    from nuvla_forge_b200.models import NuVLAConfig
+    from nuvla_forge_b200.parallel.dist import setup_distributed
+    from nuvla_forge_b200.train import Trainer
+
+    info = setup_distributed()
+    dev = info.device
+    if not nat.HAS_NATIVE:
+        raise RuntimeError("native library not loaded on a GPU box")
+    cfg = NuVLAConfig.preset(args.model_config)
+    trainer = Trainer(cfg, info, bucket_mb=args.bucket_mb, comm=args.comm, grad_accum=args.grad_accum,
+                      no_sync_accum=True, bf16=True)
+    spec = SampleSpec.for_model(cfg)
+    src = SyntheticBatchSource(spec, args.batch_size, seed=7, rank=info.rank, world=info.world)
+    host_iter = iter(src)
+    A = args.grad_accum
+    # device-resident micro-batches for the device-timed region (distinct per step)
+    n_dev = A * 2
+    dev_batches = [trainer.to_device(next(host_iter)) for _ in range(n_dev)]
+    torch.cuda.synchronize(dev)
+    counter = {"i": 0}
+
+    def dev_step():
+        i = counter["i"]
+        mb = [dev_batches[(i * A + j) % n_dev] for j in range(A)]
+        counter["i"] += 1
+        trainer.step(mb)
+
+    for _ in range(args.warmup):
+        dev_step()
+    torch.cuda.synchronize(dev)
+    trainer.check_health()
+
+    sampler = ClockSampler(visible_gpu_ids()) if info.is_main else None
+    if sampler:
+        sampler.start()
+    nat.reset_launch_count()
+    ms = timed_steps(dev_step, args.steps, dev)
+    launches = nat.launch_count()
+    clocks = sampler.stop() if sampler else None
+    trainer.check_health()
+    ms_step = max_ranks(ms / args.steps, dev)
+    gb = args.batch_size * A * info.world
+    value = gb / (ms_step / 1e3)
+
+    e2e = None
+    if not args.no_e2e:
+        host_batches = [[next(host_iter) for _ in range(A)] for _ in range(args.steps + 1)]
+        bytes_in = sum(v.numel() * v.element_size() for b in host_batches[0] for k, v in b.items()
+                       if isinstance(v, torch.Tensor))
+        # one untimed e2e step (warm the copy path)
+        float(trainer.step(host_batches[-1]).item())
+        it = {"i": 0}
+
+        def e2e_step():
+            loss = trainer.step(host_batches[it["i"]])
+            it["i"] += 1
+            float(loss.item())   # device -> host read of the step's result
+
+        ms_e2e = timed_steps(e2e_step, args.steps, dev)
+        ms_e2e = max_ranks(ms_e2e / args.steps, dev)
+        e2e = {"value": gb / (ms_e2e / 1e3), "unit": "samples/s", "ms_per_step": ms_e2e,
+               "h2d_bytes_per_step": int(bytes_in), "d2h_bytes_per_step": 4,
+               "api": "nuvla_forge_b200.train.Trainer.step"}
+    peak = torch.cuda.max_memory_allocated(dev) / 2**20
+    out = {
+        "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": info.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": value / BASELINE_SAMPLES_PER_S, "dtype": "bf16",
+        "data": "synthetic (uint8 6 views x 2 frames 448px, uniform tokens, unicycle waypoints); random init",
+        "config": {"model": f"nuVLA-{args.model_config} ({trainer.num_parameters() / 1e9:.2f}B params: ViT d1024x24 "
+                            "p14 pooled 256/img, backbone d2048x16 GQA16/8 ffn5632, DiT d1024x12)"
+                   if args.model_config == "1b" else f"nuVLA-{args.model_config}",
+                   "global_batch": gb, "micro_batch_per_gpu": args.batch_size, "grad_accum": A,
+                   "seq_len": cfg.n_images * cfg.pooled_tokens + cfg.text_len,
+                   "parallelism": f"dp{info.world}", "comm": getattr(trainer.model, "comm", "?"),
+                   "bucket_mb": args.bucket_mb,
+                   "l2": "inputs larger than L2 (58 MB uint8 per micro-batch, tens of GB of activations)"},
+        "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "peak_mem_mib": peak, "impl": "native",
+    }
+    if info.world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return out if info.is_main else None
+
+
+def main(argv=None):
+    args = parse(argv)
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    if args.impl == "reference":
+        sys.path.insert(0, os.path.join(ROOT, "baseline"))
+        from ref_arm import run_reference
+        out = run_reference(args)
+    else:
+        out = run_native(args)
+    if out is not None:
+        line = json.dumps(out)
+        print(line, flush=True)
+        if args.json_out:
+            with open(args.json_out, "w") as f:
+                f.write(line + "\n")
+
+
+if __name__ == "__main__":
+    main()

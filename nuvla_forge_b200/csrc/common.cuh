@@ -1,0 +1,163 @@
+// Shared device helpers for the nuvla_forge_b200 kernels (sm_100a only).
+//
+// Everything in this library is exported through a C ABI (extern "C") so the
+// Python side can call it through ctypes without compiling against torch
+// headers. Every entry point returns a cudaError_t (0 == success) and takes the
+// CUDA stream it must launch on; none of them allocates memory: scratch space is
+// always passed in by the caller.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#define NFB_API extern "C" __attribute__((visibility("default")))
+
+#ifndef NFB_CHECK_LAUNCH
+#define NFB_CHECK_LAUNCH() return (int)cudaGetLastError()
+#endif
+
+namespace nfb {
+
+// dtype codes shared with Python (nuvla_forge_b200/_native.py).
+enum DType : int { kF32 = 0, kBF16 = 1, kF16 = 2 };
+
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+
+// 16-byte vector of T (8 x bf16/fp16 or 4 x fp32).
+template <typename T> struct Vec16 {
+  static constexpr int N = 16 / sizeof(T);
+  union { uint4 u; T v[N]; };
+};
+
+template <typename T>
+__device__ __forceinline__ void load16(const T* p, float* out) {
+  Vec16<T> r;
+  r.u = *reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < Vec16<T>::N; ++i) out[i] = to_f32(r.v[i]);
+}
+
+template <typename T>
+__device__ __forceinline__ void store16(T* p, const float* in) {
+  Vec16<T> r;
+#pragma unroll
+  for (int i = 0; i < Vec16<T>::N; ++i) r.v[i] = from_f32<T>(in[i]);
+  *reinterpret_cast<uint4*>(p) = r.u;
+}
+
+// Streaming (evict-first) variants for data that is touched exactly once.
+template <typename T>
+__device__ __forceinline__ void load16_stream(const T* p, float* out) {
+  Vec16<T> r;
+  r.u = __ldcs(reinterpret_cast<const uint4*>(p));
+#pragma unroll
+  for (int i = 0; i < Vec16<T>::N; ++i) out[i] = to_f32(r.v[i]);
+}
+
+template <typename T>
+__device__ __forceinline__ void store16_stream(T* p, const float* in) {
+  Vec16<T> r;
+#pragma unroll
+  for (int i = 0; i < Vec16<T>::N; ++i) r.v[i] = from_f32<T>(in[i]);
+  __stcs(reinterpret_cast<uint4*>(p), r.u);
+}
+
+// 8 consecutive elements of T (one 16-byte vector for 2-byte types, two for fp32).
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float* out) {
+  if constexpr (sizeof(T) == 2) load16<T>(p, out);
+  else { load16<T>(p, out); load16<T>(p + 4, out + 4); }
+}
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float* in) {
+  if constexpr (sizeof(T) == 2) store16<T>(p, in);
+  else { store16<T>(p, in); store16<T>(p + 4, in + 4); }
+}
+template <typename T>
+__device__ __forceinline__ void load8_stream(const T* p, float* out) {
+  if constexpr (sizeof(T) == 2) load16_stream<T>(p, out);
+  else { load16_stream<T>(p, out); load16_stream<T>(p + 4, out + 4); }
+}
+// Round 8 floats through T (so later math sees exactly what was stored).
+template <typename T>
+__device__ __forceinline__ void round8(float* v) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = to_f32(from_f32<T>(v[j]));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float sigmoidf_fast(float x) {
+  return __fdividef(1.0f, 1.0f + __expf(-x));
+}
+
+// Nanosecond global timer, used to bound every spin-wait in the library.
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// System-scope release store / acquire load on 32-bit flags living in memory
+// that other GPUs read and write through NVLink peer mappings.
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Error codes written into a caller-provided device status word when a bounded
+// wait gives up. The host reads the word after the step and raises.
+enum Status : uint32_t {
+  kOk = 0,
+  kTimeoutBarrier = 1,
+  kTimeoutFlag = 2,
+  kBadArgument = 3,
+};
+
+__device__ __forceinline__ void set_status(uint32_t* status, uint32_t code, uint32_t where) {
+  if (status) {
+    atomicCAS(status, 0u, (code << 24) | (where & 0xFFFFFFu));
+  }
+}
+
+// Spin until *flag >= target (wrap-safe comparison of epochs), at most
+// timeout_ns. Returns true on success.
+__device__ __forceinline__ bool wait_flag_geq(const uint32_t* flag, uint32_t target, uint64_t timeout_ns) {
+  uint64_t t0 = globaltimer_ns();
+  while (true) {
+    uint32_t v = ld_acquire_sys(flag);
+    if ((int32_t)(v - target) >= 0) return true;
+    if (globaltimer_ns() - t0 > timeout_ns) return false;
+    __nanosleep(64);
+  }
+}
+
+}  // namespace nfb

@@ -1,0 +1,144 @@
+// On-device image preparation: uint8 camera frames -> normalised bf16.
+//
+// Parity: nuvla_forge/data/loader.py:186-196 (normalise_images), which runs
+// four eager elementwise kernels plus two small host->device constructions per
+// call. Two kernels here:
+//
+// * nfb_image_normalize: [.., 3, H, W] uint8 -> same layout in bf16/fp16/fp32,
+//   out = (v / 255 - mean[c]) / std[c]; one pass, one launch.
+// * nfb_image_patchify: [n_img, H, W, 3] uint8 (HWC, as the loader produces
+//   it, so the host never transposes) -> [n_img, (H/p)*(W/p), Kpad] bf16 patch
+//   rows in (c, ky, kx) order, i.e. exactly the rows that multiply a
+//   Conv2d-shaped [D, 3, p, p] patch-embedding weight. Columns K..Kpad are
+//   zero so the patch GEMM's K stays a multiple of 8. One CTA owns one strip
+//   of p image rows: the strip is contiguous in HWC, so it is read once with
+//   16-byte loads into shared memory and the strip's patches are written out
+//   contiguously.
+#include "common.cuh"
+
+namespace nfb {
+
+struct NormConst { float scale[3]; float bias[3]; };
+
+template <typename TO>
+__global__ void image_normalize_kernel(const uint8_t* __restrict__ in, TO* __restrict__ out,
+                                       int64_t n, int64_t hw, NormConst k) {
+  // 16 bytes per thread per step
+  const int64_t nvec = n / 16;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += (int64_t)gridDim.x * blockDim.x) {
+    uint4 u = __ldcs(reinterpret_cast<const uint4*>(in) + i);
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(&u);
+    float o[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int64_t e = i * 16 + j;
+      const int c = (int)((e / hw) % 3);
+      o[j] = (float)b[j] * k.scale[c] + k.bias[c];
+    }
+    constexpr int PER = 16 / sizeof(TO);
+#pragma unroll
+    for (int j = 0; j < 16; j += PER) store16<TO>(out + i * 16 + j, o + j);
+  }
+  // tail
+  for (int64_t e = nvec * 16 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)((e / hw) % 3);
+    out[e] = from_f32<TO>((float)in[e] * k.scale[c] + k.bias[c]);
+  }
+}
+
+template <typename TO>
+__global__ void __launch_bounds__(256) image_patchify_kernel(const uint8_t* __restrict__ in, TO* __restrict__ out,
+                                                             int H, int W, int p, int kpad, NormConst k) {
+  extern __shared__ __align__(16) uint8_t strip[];
+  const int rows_of_patches = H / p;
+  const int64_t img = blockIdx.x / rows_of_patches;
+  const int py = blockIdx.x % rows_of_patches;
+  const int64_t strip_bytes = (int64_t)p * W * 3;
+  const uint8_t* src = in + img * (int64_t)H * W * 3 + (int64_t)py * strip_bytes;
+  if ((reinterpret_cast<uintptr_t>(src) & 15) == 0 && (strip_bytes & 15) == 0) {
+    for (int64_t i = threadIdx.x; i < strip_bytes / 16; i += blockDim.x)
+      reinterpret_cast<uint4*>(strip)[i] = __ldcs(reinterpret_cast<const uint4*>(src) + i);
+  } else {
+    for (int64_t i = threadIdx.x; i < strip_bytes; i += blockDim.x) strip[i] = src[i];
+  }
+  __syncthreads();
+  const int pw = W / p;
+  const int K = 3 * p * p;
+  const int pp = p * p;
+  TO* dst = out + (img * rows_of_patches + py) * (int64_t)pw * kpad;
+  constexpr int PER = 16 / sizeof(TO);
+  const int vec_per_patch = kpad / PER;
+  for (int v = threadIdx.x; v < pw * vec_per_patch; v += blockDim.x) {
+    const int px = v / vec_per_patch;
+    const int k0 = (v % vec_per_patch) * PER;
+    float o[PER];
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int kk = k0 + j;
+      if (kk < K) {
+        const int c = kk / pp;
+        const int rem = kk - c * pp;
+        const int ky = rem / p;
+        const int kx = rem - ky * p;
+        const float val = (float)strip[(ky * W + px * p + kx) * 3 + c];
+        o[j] = val * k.scale[c] + k.bias[c];
+      } else {
+        o[j] = 0.f;
+      }
+    }
+    store16<TO>(dst + (int64_t)px * kpad + k0, o);
+  }
+}
+
+static NormConst make_const(const float* mean, const float* std) {
+  NormConst k;
+  for (int c = 0; c < 3; ++c) {
+    k.scale[c] = 1.0f / (255.0f * std[c]);
+    k.bias[c] = -mean[c] / std[c];
+  }
+  return k;
+}
+
+}  // namespace nfb
+
+using namespace nfb;
+
+// in: uint8 [..., 3, H, W] contiguous, n elements; out dtype 0 f32, 1 bf16, 2 f16.
+NFB_API int nfb_image_normalize(int out_dtype, const void* in, void* out, int64_t n, int64_t hw,
+                                const float* mean, const float* std, void* stream) {
+  if (n == 0) return 0;
+  if ((reinterpret_cast<uintptr_t>(in) & 15) || (reinterpret_cast<uintptr_t>(out) & 15)) return (int)cudaErrorInvalidValue;
+  NormConst k = make_const(mean, std);
+  cudaStream_t st = (cudaStream_t)stream;
+  int64_t blocks = (n / 16 + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (blocks < 1) blocks = 1;
+  const uint8_t* src = (const uint8_t*)in;
+  if (out_dtype == kBF16) image_normalize_kernel<__nv_bfloat16><<<(int)blocks, 256, 0, st>>>(src, (__nv_bfloat16*)out, n, hw, k);
+  else if (out_dtype == kF16) image_normalize_kernel<__half><<<(int)blocks, 256, 0, st>>>(src, (__half*)out, n, hw, k);
+  else if (out_dtype == kF32) image_normalize_kernel<float><<<(int)blocks, 256, 0, st>>>(src, (float*)out, n, hw, k);
+  else return (int)cudaErrorInvalidValue;
+  return (int)cudaGetLastError();
+}
+
+// in: uint8 [n_img, H, W, 3]; out: [n_img, (H/p)*(W/p), kpad]; kpad % 8 == 0, kpad >= 3*p*p.
+NFB_API int nfb_image_patchify(int out_dtype, const void* in, void* out, int64_t n_img, int H, int W, int p,
+                               int kpad, const float* mean, const float* std, void* stream) {
+  if (n_img == 0) return 0;
+  if (H % p || W % p || kpad < 3 * p * p || kpad % 8) return (int)cudaErrorInvalidValue;
+  NormConst k = make_const(mean, std);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t grid = n_img * (H / p);
+  const size_t smem = ((size_t)p * W * 3 + 15) / 16 * 16;
+  if (smem > 200 * 1024) return (int)cudaErrorInvalidValue;
+  if (out_dtype == kBF16) {
+    if (smem > 48 * 1024) cudaFuncSetAttribute(image_patchify_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    image_patchify_kernel<__nv_bfloat16><<<(unsigned)grid, 256, smem, st>>>((const uint8_t*)in, (__nv_bfloat16*)out, H, W, p, kpad, k);
+  } else if (out_dtype == kF16) {
+    if (smem > 48 * 1024) cudaFuncSetAttribute(image_patchify_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    image_patchify_kernel<__half><<<(unsigned)grid, 256, smem, st>>>((const uint8_t*)in, (__half*)out, H, W, p, kpad, k);
+  } else {
+    return (int)cudaErrorInvalidValue;
+  }
+  return (int)cudaGetLastError();
+}

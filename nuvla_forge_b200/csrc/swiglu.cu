@@ -1,0 +1,135 @@
+// Fused SwiGLU forward and backward (parity: nuvla_forge/kernels/swiglu.py:35-63).
+//
+//   forward:  out = silu(a) * b
+//   backward: da = dout * b * s * (1 + a * (1 - s)),  db = dout * a * s,  s = sigmoid(a)
+//
+// Bandwidth bound, so the kernels move 16-byte vectors and use streaming
+// cache hints for tensors that are read or written exactly once. a and b may
+// be row-strided views (for example the two column halves of one fused
+// gate/up projection); out, da and db have their own row strides so the
+// backward can write straight into the halves of one fused gradient buffer.
+#include "common.cuh"
+
+namespace nfb {
+
+struct SwigluArgs {
+  const void* a; const void* b; const void* dout;
+  void* out; void* da; void* db;
+  int64_t M, N;                     // rows, columns (N % 8 == 0)
+  int64_t sa, sb, sdo, so, sda, sdb; // row strides (elements)
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) swiglu_fwd_kernel(SwigluArgs p) {
+  const int64_t cpr = p.N / 8;  // 8-wide chunks per row
+  const int64_t total = p.M * cpr;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / cpr, c = (i - r * cpr) * 8;
+    float av[8], bv[8], o[8];
+    load8_stream<T>(reinterpret_cast<const T*>(p.a) + r * p.sa + c, av);
+    load8_stream<T>(reinterpret_cast<const T*>(p.b) + r * p.sb + c, bv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = av[j] * sigmoidf_fast(av[j]) * bv[j];
+    store8<T>(reinterpret_cast<T*>(p.out) + r * p.so + c, o);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) swiglu_bwd_kernel(SwigluArgs p) {
+  const int64_t cpr = p.N / 8;
+  const int64_t total = p.M * cpr;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / cpr, c = (i - r * cpr) * 8;
+    float av[8], bv[8], dv[8], da[8], db[8];
+    load8_stream<T>(reinterpret_cast<const T*>(p.a) + r * p.sa + c, av);
+    load8_stream<T>(reinterpret_cast<const T*>(p.b) + r * p.sb + c, bv);
+    load8_stream<T>(reinterpret_cast<const T*>(p.dout) + r * p.sdo + c, dv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float s = sigmoidf_fast(av[j]);
+      const float silu = av[j] * s;
+      da[j] = dv[j] * bv[j] * s * (1.f + av[j] * (1.f - s));
+      db[j] = dv[j] * silu;
+    }
+    store8<T>(reinterpret_cast<T*>(p.da) + r * p.sda + c, da);
+    store8<T>(reinterpret_cast<T*>(p.db) + r * p.sdb + c, db);
+  }
+}
+
+// Scalar tail kernels for shapes whose columns are not a multiple of 8.
+template <typename T>
+__global__ void swiglu_fwd_scalar(const T* a, const T* b, T* out, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float x = to_f32(a[i]), y = to_f32(b[i]);
+    out[i] = from_f32<T>(x * sigmoidf_fast(x) * y);
+  }
+}
+template <typename T>
+__global__ void swiglu_bwd_scalar(const T* dout, const T* a, const T* b, T* da, T* db, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float x = to_f32(a[i]), y = to_f32(b[i]), d = to_f32(dout[i]);
+    float s = sigmoidf_fast(x);
+    da[i] = from_f32<T>(d * y * s * (1.f + x * (1.f - s)));
+    db[i] = from_f32<T>(d * x * s);
+  }
+}
+
+static int elementwise_grid(int64_t work, int threads) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int64_t blocks = (work + threads - 1) / threads;
+  int64_t cap = (int64_t)sms * 8;  // grid-stride beyond 8 CTAs of 256 per SM
+  if (blocks > cap) blocks = cap;
+  return (int)(blocks < 1 ? 1 : blocks);
+}
+
+}  // namespace nfb
+
+using namespace nfb;
+
+NFB_API int nfb_swiglu_fwd(int dtype, const void* a, const void* b, void* out,
+                           int64_t M, int64_t N, int64_t sa, int64_t sb, int64_t so, void* stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  if (M * N == 0) return 0;
+  SwigluArgs p{a, b, nullptr, out, nullptr, nullptr, M, N, sa, sb, 0, so, 0, 0};
+  if (N % 8 == 0) {
+    int grid = elementwise_grid(M * N / 8, 256);
+    if (dtype == kF32) swiglu_fwd_kernel<float><<<grid, 256, 0, st>>>(p);
+    else if (dtype == kBF16) swiglu_fwd_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
+    else if (dtype == kF16) swiglu_fwd_kernel<__half><<<grid, 256, 0, st>>>(p);
+    else return (int)cudaErrorInvalidValue;
+  } else {
+    // scalar path requires dense rows
+    if (sa != N || sb != N || so != N) return (int)cudaErrorInvalidValue;
+    int grid = elementwise_grid(M * N, 256);
+    if (dtype == kBF16) swiglu_fwd_scalar<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)a, (const __nv_bfloat16*)b, (__nv_bfloat16*)out, M * N);
+    else if (dtype == kF16) swiglu_fwd_scalar<__half><<<grid, 256, 0, st>>>((const __half*)a, (const __half*)b, (__half*)out, M * N);
+    else if (dtype == kF32) swiglu_fwd_scalar<float><<<grid, 256, 0, st>>>((const float*)a, (const float*)b, (float*)out, M * N);
+    else return (int)cudaErrorInvalidValue;
+  }
+  return (int)cudaGetLastError();
+}
+
+NFB_API int nfb_swiglu_bwd(int dtype, const void* dout, const void* a, const void* b, void* da, void* db,
+                           int64_t M, int64_t N, int64_t sdo, int64_t sa, int64_t sb, int64_t sda, int64_t sdb,
+                           void* stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  if (M * N == 0) return 0;
+  SwigluArgs p{a, b, dout, nullptr, da, db, M, N, sa, sb, sdo, 0, sda, sdb};
+  if (N % 8 == 0) {
+    int grid = elementwise_grid(M * N / 8, 256);
+    if (dtype == kF32) swiglu_bwd_kernel<float><<<grid, 256, 0, st>>>(p);
+    else if (dtype == kBF16) swiglu_bwd_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
+    else if (dtype == kF16) swiglu_bwd_kernel<__half><<<grid, 256, 0, st>>>(p);
+    else return (int)cudaErrorInvalidValue;
+  } else {
+    if (sa != N || sb != N || sdo != N || sda != N || sdb != N) return (int)cudaErrorInvalidValue;
+    int grid = elementwise_grid(M * N, 256);
+    if (dtype == kBF16) swiglu_bwd_scalar<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)dout, (const __nv_bfloat16*)a, (const __nv_bfloat16*)b, (__nv_bfloat16*)da, (__nv_bfloat16*)db, M * N);
+    else if (dtype == kF16) swiglu_bwd_scalar<__half><<<grid, 256, 0, st>>>((const __half*)dout, (const __half*)a, (const __half*)b, (__half*)da, (__half*)db, M * N);
+    else if (dtype == kF32) swiglu_bwd_scalar<float><<<grid, 256, 0, st>>>((const float*)dout, (const float*)a, (const float*)b, (float*)da, (float*)db, M * N);
+    else return (int)cudaErrorInvalidValue;
+  }
+  return (int)cudaGetLastError();
+}

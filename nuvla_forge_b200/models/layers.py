@@ -1,0 +1,187 @@
+"""Transformer building blocks shared by the vision encoder, the backbone and the DiT.
+
+Parameter names follow the reference so ``state_dict`` keys match
+(nuvla_forge/model/dit.py:34-110, nuvla_forge/model/nuvla.py:47-59):
+``norm1/norm2.weight``, ``attn.qkv.weight``, ``attn.proj.weight``,
+``mlp.w_gate.weight``, ``mlp.w_up.weight``, ``mlp.w_down.weight``.
+
+Compute differs from the reference where it saves memory traffic, never in
+the function computed:
+
+* Residual adds are fused into the output-projection GEMM epilogue
+  (``addmm(x, o, W.T)``: cuBLAS reads the residual as its C operand), and the
+  following RMSNorm is one native kernel.
+* The SwiGLU gate and up projections are one GEMM over a packed [2F, D]
+  weight whose backward is one input-gradient GEMM; ``state_dict`` still
+  exposes ``w_gate.weight`` and ``w_up.weight`` (split on save, joined on load).
+* Attention runs on the projection-native [B, S, H, D] layout (no permutes)
+  and supports grouped-query attention (``kv_heads < heads``) and a causal
+  mask, which the BASELINE backbone configs need.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from ..ops import attention as attention_op
+from ..ops import rmsnorm as rmsnorm_op
+from ..ops import swiglu_packed
+from ..ops.reference import swiglu_ref
+
+
+def _linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None,
+            residual: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x @ w.T (+ b) (+ residual), with the residual read by the GEMM itself."""
+    if residual is None:
+        return F.linear(x, w, b)
+    shape = residual.shape
+    x2 = x.reshape(-1, x.shape[-1])
+    r2 = residual.reshape(-1, shape[-1])
+    if b is not None:
+        r2 = r2 + b
+    return torch.addmm(r2, x2, w.t()).view(shape)
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, dim: int, eps: float = 1e-6, fused: bool = True):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(dim))
+        self.eps = eps
+        self.fused = fused
+
+    def forward(self, x, scale=None, shift=None, tokens_per_sample=None):
+        return rmsnorm_op(x, self.weight, self.eps, scale=scale, shift=shift,
+                          tokens_per_sample=tokens_per_sample, force_reference=not self.fused)
+
+
+def modulate(x, shift, scale):
+    return x * (1 + scale.unsqueeze(1)) + shift.unsqueeze(1)
+
+
+class TimestepEmbedder(nn.Module):
+    """Sinusoidal diffusion-time embedding projected to the model width.
+
+    Parity: nuvla_forge/model/dit.py:49-68 (freq_dim 256, Linear-SiLU-Linear).
+    """
+
+    def __init__(self, dim: int, freq_dim: int = 256):
+        super().__init__()
+        self.freq_dim = freq_dim
+        self.mlp = nn.Sequential(nn.Linear(freq_dim, dim), nn.SiLU(), nn.Linear(dim, dim))
+
+    def forward(self, t):
+        half = self.freq_dim // 2
+        k = torch.arange(half, dtype=torch.float32, device=t.device)
+        freqs = torch.exp(k * (-math.log(10000.0) / half))
+        ang = t.to(torch.float32)[:, None] * freqs[None, :]
+        emb = torch.cat([torch.cos(ang), torch.sin(ang)], dim=-1)
+        return self.mlp(emb.to(self.mlp[0].weight.dtype))
+
+
+class Attention(nn.Module):
+    """Multi-head / grouped-query attention with a fused qkv projection.
+
+    Self-attention uses ``qkv`` [(H + 2*Hkv) * Dh, D]. Cross-attention into a
+    context of the same width slices the same weight (as the reference does,
+    nuvla_forge/model/dit.py:84-90); for a context of a different width the
+    module owns ``q`` [D, D] and ``kv`` [2 * Hkv * Dh, Dctx] instead.
+    """
+
+    def __init__(self, dim: int, n_heads: int, kv_heads: int | None = None, causal: bool = False,
+                 ctx_dim: int | None = None, fused: bool = True):
+        super().__init__()
+        self.dim = dim
+        self.n_heads = n_heads
+        self.kv_heads = kv_heads or n_heads
+        self.head_dim = dim // n_heads
+        self.causal = causal
+        self.fused = fused
+        kvd = self.kv_heads * self.head_dim
+        self.split_ctx = ctx_dim is not None and ctx_dim != dim
+        if self.split_ctx:
+            self.q = nn.Linear(dim, dim, bias=False)
+            self.kv = nn.Linear(ctx_dim, 2 * kvd, bias=False)
+        else:
+            self.qkv = nn.Linear(dim, dim + 2 * kvd, bias=False)
+        self.proj = nn.Linear(dim, dim, bias=False)
+
+    def forward(self, x, context=None, residual=None):
+        b, t, c = x.shape
+        H, Hk, Dh = self.n_heads, self.kv_heads, self.head_dim
+        if context is None:
+            qkv = F.linear(x, self.qkv.weight).view(b, t, H + 2 * Hk, Dh)
+            q, k, v = qkv.split([H, Hk, Hk], dim=2)
+        else:
+            s = context.shape[1]
+            if self.split_ctx:
+                q = F.linear(x, self.q.weight).view(b, t, H, Dh)
+                kv = F.linear(context, self.kv.weight).view(b, s, 2 * Hk, Dh)
+            else:
+                q = F.linear(x, self.qkv.weight[:c]).view(b, t, H, Dh)
+                kv = F.linear(context, self.qkv.weight[c:]).view(b, s, 2 * Hk, Dh)
+            k, v = kv.split([Hk, Hk], dim=2)
+        o = attention_op(q, k, v, causal=self.causal and context is None, force_reference=not self.fused)
+        o = o.reshape(b, t, c)
+        return _linear(o, self.proj.weight, residual=residual)
+
+
+class SwiGLUMLP(nn.Module):
+    """w_down(silu(w_gate x) * w_up x) with the gate/up weights packed in one tensor."""
+
+    def __init__(self, dim: int, hidden: int, fused: bool = True):
+        super().__init__()
+        self.hidden = hidden
+        self.fused = fused
+        self.w_gate_up = nn.Parameter(torch.empty(2 * hidden, dim))
+        self.w_down = nn.Linear(hidden, dim, bias=False)
+        bound = 1.0 / math.sqrt(dim)
+        nn.init.uniform_(self.w_gate_up, -bound, bound)
+        self._register_state_dict_hook(SwiGLUMLP._split_on_save)
+        self._register_load_state_dict_pre_hook(SwiGLUMLP._join_on_load)
+
+    @staticmethod
+    def _split_on_save(module, state_dict, prefix, local_metadata):
+        key = prefix + "w_gate_up"
+        if key in state_dict:
+            w = state_dict.pop(key)
+            state_dict[prefix + "w_gate.weight"] = w[: module.hidden]
+            state_dict[prefix + "w_up.weight"] = w[module.hidden:]
+        return state_dict
+
+    @staticmethod
+    def _join_on_load(state_dict, prefix, *args, **kwargs):
+        g, u = prefix + "w_gate.weight", prefix + "w_up.weight"
+        if g in state_dict and u in state_dict:
+            state_dict[prefix + "w_gate_up"] = torch.cat([state_dict.pop(g), state_dict.pop(u)], dim=0)
+
+    def forward(self, x, residual=None):
+        ab = F.linear(x, self.w_gate_up)
+        if self.fused:
+            act = swiglu_packed(ab)
+        else:
+            act = swiglu_ref(ab[..., : self.hidden], ab[..., self.hidden:])
+        return _linear(act, self.w_down.weight, residual=residual)
+
+
+class TransformerBlock(nn.Module):
+    """Pre-norm block: x + attn(norm1(x)), then + mlp(norm2(x)).
+
+    Parity: nuvla_forge/model/nuvla.py:47-59 (RMSNorm, fused-qkv attention,
+    SwiGLU with hidden 4*dim by default).
+    """
+
+    def __init__(self, dim: int, heads: int, fused: bool = True, kv_heads: int | None = None,
+                 ffn: int | None = None, causal: bool = False):
+        super().__init__()
+        self.norm1 = RMSNorm(dim, fused=fused)
+        self.attn = Attention(dim, heads, kv_heads=kv_heads, causal=causal, fused=fused)
+        self.norm2 = RMSNorm(dim, fused=fused)
+        self.mlp = SwiGLUMLP(dim, ffn or dim * 4, fused=fused)
+
+    def forward(self, x):
+        x = self.attn(self.norm1(x), residual=x)
+        return self.mlp(self.norm2(x), residual=x)

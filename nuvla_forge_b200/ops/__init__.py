@@ -1,0 +1,25 @@
+"""Ops: the model's hot operations, native sm_100a kernels with PyTorch references.
+
+Public names mirror the reference's kernel package (nuvla_forge/kernels/__init__.py:8-18)
+plus the ops the reference left to PyTorch.
+"""
+
+from .._native import HAS_NATIVE
+from .attention import attention
+from .chunked_ce import chunked_cross_entropy
+from .image import normalise_images, patchify_images
+from .norm import add_rmsnorm, fused_adaln_residual_rmsnorm, rmsnorm
+from .swiglu import fused_swiglu, swiglu_packed
+
+__all__ = [
+    "HAS_NATIVE",
+    "add_rmsnorm",
+    "attention",
+    "chunked_cross_entropy",
+    "fused_adaln_residual_rmsnorm",
+    "fused_swiglu",
+    "normalise_images",
+    "patchify_images",
+    "rmsnorm",
+    "swiglu_packed",
+]
