@@ -149,14 +149,33 @@ def run_reference(args):
         local, rank, world = 0, 0, 1
         torch.cuda.set_device(0)
     dev = torch.device(f"cuda:{local}")
-    torch.manual_seed(1234 + rank)
     torch.backends.cuda.matmul.allow_tf32 = True
     torch.backends.cudnn.allow_tf32 = True
-    model, s = build_reference_model(args.model_config)
-    model = model.to(dev)
-    if world > 1:
-        model = DDP(model, device_ids=[local], bucket_cap_mb=args.bucket_mb, gradient_as_bucket_view=True)
-    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, weight_decay=0.01, fused=True)
+    state = {}
+
+    def build(grad_ckpt: bool):
+        torch.manual_seed(1234 + rank)
+        model, s = build_reference_model(args.model_config)
+        if grad_ckpt:
+            # the reference's own remedy for activation memory (nuvla_forge/train.py:139-152):
+            # recompute the vision encoder blocks in backward
+            from torch.utils.checkpoint import checkpoint
+
+            for blk in model.encoder.blocks:
+                inner = blk.forward
+
+                def fwd(*a, _inner=inner, **kw):
+                    return checkpoint(_inner, *a, use_reentrant=False, **kw)
+
+                blk.forward = fwd
+        model = model.to(dev)
+        if world > 1:
+            model = DDP(model, device_ids=[local], bucket_cap_mb=args.bucket_mb, gradient_as_bucket_view=True)
+        opt = torch.optim.AdamW(model.parameters(), lr=3e-4, weight_decay=0.01, fused=True)
+        state.update(model=model, opt=opt, s=s, grad_ckpt=grad_ckpt)
+
+    build(False)
+    s = state["s"]
     A, B = args.grad_accum, args.batch_size
     gen = torch.Generator().manual_seed(7 + rank)
 
@@ -171,6 +190,7 @@ def run_reference(args):
                 {"images": imgs, "trajectory": traj, "text_tokens": toks, "text_targets": tg}.items()}
 
     def step(micro):
+        model, opt = state["model"], state["opt"]
         for m, b in enumerate(micro):
             b = {k: v.to(dev, non_blocking=True) for k, v in b.items()}
             images = normalise_images(b["images"], dtype=torch.bfloat16)
@@ -194,7 +214,26 @@ def run_reference(args):
         step([dev_batches[(i * A + j) % n_dev] for j in range(A)])
 
     t0 = time.time()
-    for _ in range(args.warmup):
+    try:
+        dev_step()
+        oom = 0.0
+    except torch.OutOfMemoryError:
+        oom = 1.0
+    # every rank must agree before rebuilding (collective order stays identical)
+    if world > 1:
+        flag = torch.tensor([oom], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+        oom = float(flag.item())
+    if oom:
+        state.clear()
+        import gc
+
+        gc.collect()
+        torch.cuda.empty_cache()
+        torch.cuda.reset_peak_memory_stats(dev)
+        build(True)
+        dev_step()
+    for _ in range(max(0, args.warmup - 1)):
         dev_step()
     torch.cuda.synchronize(dev)
     sampler = ClockSampler(visible_gpu_ids()) if rank == 0 else None
@@ -227,6 +266,7 @@ def run_reference(args):
         "config": {"model": f"nuVLA-{args.model_config} from reference modules", "global_batch": gb,
                    "micro_batch_per_gpu": B, "grad_accum": A, "parallelism": f"dp{world}",
                    "bucket_mb": args.bucket_mb, "has_triton": HAS_TRITON,
+                   "grad_checkpoint_encoder": state["grad_ckpt"],
                    "l2": "inputs larger than L2"},
         "clocks": clocks, "e2e": e2e, "gpu_launches": None,
         "peak_mem_mib": torch.cuda.max_memory_allocated(dev) / 2**20, "setup_s": time.time() - t0,

@@ -19,7 +19,7 @@ __device__ __forceinline__ MS ms_merge(MS a, MS b) {
   return {m, a.s * __expf(a.m - m) + b.s * __expf(b.m - m)};
 }
 
-template <typename T>
+template <typename T, bool VEC>
 __global__ void __launch_bounds__(512) ce_rows_kernel(T* logits, int64_t ld, const int64_t* targets,
                                                       int64_t V, int64_t ignore_index, const float* count,
                                                       float* loss_rows) {
@@ -29,7 +29,7 @@ __global__ void __launch_bounds__(512) ce_rows_kernel(T* logits, int64_t ld, con
   T* base = logits + row * ld;
   const int64_t tgt = targets[row];
   const float inv = 1.f / fmaxf(*count, 1.f);
-  const int64_t nv = V / 8;
+  const int64_t nv = VEC ? V / 8 : 0;  // rows not 16-byte aligned take the scalar loops only
   if (tgt == ignore_index) {
     float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int64_t i = threadIdx.x; i < nv; i += blockDim.x) store8<T>(base + i * 8, z);
@@ -104,11 +104,18 @@ using namespace nfb;
 NFB_API int nfb_ce_rows(int dtype, void* logits, int64_t ld, const int64_t* targets, int64_t rows, int64_t V,
                         int64_t ignore_index, const float* count, float* loss_rows, void* stream) {
   if (rows == 0) return 0;
-  if ((reinterpret_cast<uintptr_t>(logits) & 15) || (ld % 8)) return (int)cudaErrorInvalidValue;
   cudaStream_t st = (cudaStream_t)stream;
-  if (dtype == kBF16) ce_rows_kernel<__nv_bfloat16><<<(unsigned)rows, 512, 0, st>>>((__nv_bfloat16*)logits, ld, targets, V, ignore_index, count, loss_rows);
-  else if (dtype == kF32) ce_rows_kernel<float><<<(unsigned)rows, 512, 0, st>>>((float*)logits, ld, targets, V, ignore_index, count, loss_rows);
-  else return (int)cudaErrorInvalidValue;
+  const int64_t es = dtype == kF32 ? 4 : 2;
+  const bool vec = ((reinterpret_cast<uintptr_t>(logits) & 15) == 0) && ((ld * es) % 16 == 0);
+  if (dtype == kBF16) {
+    if (vec) ce_rows_kernel<__nv_bfloat16, true><<<(unsigned)rows, 512, 0, st>>>((__nv_bfloat16*)logits, ld, targets, V, ignore_index, count, loss_rows);
+    else ce_rows_kernel<__nv_bfloat16, false><<<(unsigned)rows, 512, 0, st>>>((__nv_bfloat16*)logits, ld, targets, V, ignore_index, count, loss_rows);
+  } else if (dtype == kF32) {
+    if (vec) ce_rows_kernel<float, true><<<(unsigned)rows, 512, 0, st>>>((float*)logits, ld, targets, V, ignore_index, count, loss_rows);
+    else ce_rows_kernel<float, false><<<(unsigned)rows, 512, 0, st>>>((float*)logits, ld, targets, V, ignore_index, count, loss_rows);
+  } else {
+    return (int)cudaErrorInvalidValue;
+  }
   return (int)cudaGetLastError();
 }
 

@@ -1,0 +1,62 @@
+"""Spawn helpers for multi-process CPU (gloo) tests."""
+
+import datetime
+import os
+import socket
+import traceback
+
+import torch.multiprocessing as mp
+
+
+def free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _entry(rank, world, port, fn, q, args, timeout_s):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=timeout_s))
+        res = fn(rank, world, *args)
+        q.put((rank, "ok", res))
+    except BaseException as exc:  # noqa: BLE001 - report to the parent
+        q.put((rank, "err", f"{type(exc).__name__}: {exc}\n{traceback.format_exc()}"))
+    finally:
+        try:
+            if dist.is_initialized():
+                dist.destroy_process_group()
+        except Exception:  # noqa: BLE001
+            pass
+
+
+def run_ranks(fn, world: int = 2, args=(), timeout_s: float = 60.0, join_s: float = 120.0) -> dict:
+    """Run fn(rank, world, *args) on `world` gloo ranks; returns {rank: (status, result)}."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_entry, args=(r, world, port, fn, q, args, timeout_s)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = {}
+    import queue
+    import time
+
+    deadline = time.time() + join_s
+    while len(out) < world and time.time() < deadline:
+        try:
+            r, st, res = q.get(timeout=1.0)
+            out[r] = (st, res)
+        except queue.Empty:
+            if all(not p.is_alive() for p in procs) and q.empty():
+                break
+    for p in procs:
+        p.join(timeout=5)
+        if p.is_alive():
+            p.kill()
+            p.join()
+    return out
