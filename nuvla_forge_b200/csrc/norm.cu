@@ -451,3 +451,127 @@ NFB_API int nfb_norm_bwd(int dtype, int gate_mode, int mod,
 }
 
 NFB_API int nfb_num_sms() { return num_sms(); }
+
+// ===========================================================================
+// Allocation-free variant of the norm backward (nfb_norm_bwd_noalloc).
+//
+// This entry point has no counterpart in the reference implementation.
+//
+// Who it is for: callers that cannot allocate device memory at the point
+// where they run the backward. Examples are a host framework that owns every
+// device allocation through a fixed memory plan made before the first step
+// (its accounting forbids raw allocations later), and plugin or callback
+// code inside another engine whose contract says the call must not allocate,
+// because a device allocation can block on work already queued on the GPU.
+// nfb_norm_bwd needs the caller to pass scratch buffers (per-CTA partial
+// rows, per-sample rows and ticket counters); this variant instead uses one
+// file-scope device array of fixed size, so the caller passes only the
+// inputs and outputs.
+//
+// Limit: the scratch holds kNoAllocScratchFloats floats (4 MiB). A call needs
+// B*N floats for per-sample rows plus 3*N*B*P floats of CTA partials, with
+// P >= 1 CTAs per sample, and B+1 ticket slots (B <= kNoAllocMaxSamples).
+// Larger problems are rejected with cudaErrorInvalidValue and a message
+// readable through nfb_noalloc_last_error(); the number of CTAs per sample is
+// lowered (never below 1) to fit the scratch, which changes only the
+// summation grouping, not the result beyond rounding.
+//
+// Every GPU that loads this library holds the array until the process exits.
+// The first call on each device looks up the array's device address with
+// cudaGetSymbolAddress while that device is current and caches it; make that
+// first call before any stream capture. All calls on a device share the
+// array: it keeps the previous call's contents, the ticket counters are
+// cleared with cudaMemsetAsync on the call's stream at the start of every
+// call, and calls whose executions overlap on the GPU (for example on two
+// streams without ordering between them) race on the scratch and give wrong
+// results. The call makes no cudaMalloc/cudaFree and no allocating library
+// call.
+// ===========================================================================
+#include <mutex>
+#include <stdio.h>
+
+namespace nfb {
+
+constexpr int64_t kNoAllocScratchFloats = 1 << 20;  // 4 MiB of fp32
+constexpr int64_t kNoAllocMaxSamples = 1023;        // ticket slots = samples + 1
+constexpr int64_t kNoAllocTicketWords = kNoAllocMaxSamples + 1;
+constexpr int kNoAllocMaxDevices = 64;
+
+// [0, kNoAllocScratchFloats): partials then per-sample rows; then the tickets.
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats + kNoAllocTicketWords];
+
+static float* g_noalloc_ptr[kNoAllocMaxDevices] = {nullptr};
+static std::mutex g_noalloc_mu;
+static thread_local char g_noalloc_msg[256] = "";
+
+static int noalloc_fail(int rc, const char* msg) {
+  snprintf(g_noalloc_msg, sizeof(g_noalloc_msg), "%s", msg);
+  return rc;
+}
+
+// Device address of the scratch array for the current device (looked up once per device).
+static int noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return noalloc_fail((int)e, "cudaGetDevice failed");
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return noalloc_fail((int)cudaErrorInvalidDevice, "device ordinal too large");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) return noalloc_fail((int)e, "cudaGetSymbolAddress(g_noalloc_scratch) failed");
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+
+}  // namespace nfb
+
+// Message describing why the last nfb_norm_bwd_noalloc call on this host thread failed ("" if none).
+NFB_API const char* nfb_noalloc_last_error() { return nfb::g_noalloc_msg; }
+
+// Capacity of the allocation-free scratch, in fp32 elements.
+NFB_API int64_t nfb_noalloc_scratch_floats() { return nfb::kNoAllocScratchFloats; }
+
+// Same contract and outputs as nfb_norm_bwd, without the partials/dwb/tickets/P arguments.
+NFB_API int nfb_norm_bwd_noalloc(int dtype, int gate_mode, int mod,
+                                 const void* dh_up, const void* dout, const void* h, const void* y,
+                                 const void* gate, const void* weight, const void* scale, const float* rstd,
+                                 void* dx, void* dy, void* dgate, void* dscale, void* dshift, void* dweight,
+                                 int64_t M, int64_t N, int64_t T,
+                                 int64_t s_dhup, int64_t s_dout, int64_t s_h, int64_t s_y, int64_t s_dx,
+                                 int64_t s_dy, int64_t sg, int64_t ss, int w_f32, void* stream) {
+  using namespace nfb;
+  g_noalloc_msg[0] = '\0';
+  if (N <= 0 || N > 8192 || (N % 8) != 0 || T <= 0 || M % T != 0)
+    return noalloc_fail((int)cudaErrorInvalidValue, "invalid shape: need 0 < N <= 8192, N % 8 == 0, M % T == 0");
+  if (M == 0) return 0;
+  const int64_t B = M / T;
+  if (B > kNoAllocMaxSamples)
+    return noalloc_fail((int)cudaErrorInvalidValue, "too many samples for the allocation-free scratch (max 1023)");
+  const int64_t rows_floats = B * N;
+  if (rows_floats + 3 * N * B > kNoAllocScratchFloats)
+    return noalloc_fail((int)cudaErrorInvalidValue,
+                        "problem too large for the allocation-free scratch: need B*N + 3*N*B floats <= 1048576");
+  int64_t P = nfb_norm_bwd_P(M, N, B);
+  const int64_t p_fit = (kNoAllocScratchFloats - rows_floats) / (3 * N * B);
+  if (P > p_fit) P = p_fit;
+  float* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc != 0) return rc;
+  float* partials = scratch;
+  float* dwb = scratch + B * P * 3 * N;
+  uint32_t* tickets = reinterpret_cast<uint32_t*>(scratch + kNoAllocScratchFloats);
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e = cudaMemsetAsync(tickets, 0, (size_t)(B + 1) * sizeof(uint32_t), st);
+  if (e != cudaSuccess) return noalloc_fail((int)e, "cudaMemsetAsync of the ticket counters failed");
+  NormBwdArgs a{dh_up, dout, h, y, gate, weight, scale, rstd, dx, dy, dgate, dscale, dshift, dweight,
+                partials, dwb, tickets, M, N, T, B, P, s_dhup, s_dout, s_h, s_y, s_dx, s_dy, sg, ss, w_f32};
+  if (dtype == kF32) rc = dispatch_bwd<float>(a, gate_mode, mod, st);
+  else if (dtype == kBF16) rc = dispatch_bwd<__nv_bfloat16>(a, gate_mode, mod, st);
+  else if (dtype == kF16) rc = dispatch_bwd<__half>(a, gate_mode, mod, st);
+  else return noalloc_fail((int)cudaErrorInvalidValue, "unsupported dtype code");
+  if (rc != 0) return noalloc_fail(rc, "kernel launch failed");
+  return 0;
+}
