@@ -1,0 +1,284 @@
+// Cross entropy on the tcgen05 GEMM: the [M, V] logits exist only in TMEM.
+//
+// Parity: nuvla_forge/kernels/chunked_ce.py:120-208 computes the same mean CE and
+// its gradients during forward, but materialises an fp32 [chunk, V] logit tile
+// per chunk and syncs the host for the valid-token count. Here:
+//
+//   pass 1 (nfb_ce_tc_stats): logits tile = h[128 rows] x W[256 vocab]^T in TMEM;
+//          the epilogue reduces each row's 256 logits to an online-softmax
+//          partial (max, sum exp) per vocab tile and picks out the target logit.
+//   merge  (nfb_ce_tc_merge): per row, merge the partials into the log-sum-exp
+//          and the row's loss / count (count read from device memory).
+//   pass 2 (nfb_ce_tc_grad): recompute the logits tile in TMEM; the epilogue
+//          writes dlogits = (softmax - onehot) / count as bf16 for the two
+//          gradient GEMMs (d_hidden = dl W, d_W += dl^T h), which the caller
+//          runs per row chunk so only a [chunk, V] bf16 buffer ever exists.
+//
+// nfb_tc_gemm_bf16 exposes the same core as a plain C = A B^T GEMM (bf16 or
+// fp32 output), used by the tests to check the core against cuBLAS.
+#include <cudaTypedefs.h>
+
+#include "tc_gemm.cuh"
+
+namespace nfb {
+namespace tc {
+
+// ---------------------------------------------------------------------------
+// Host: tensor maps through the driver entry point (no libcuda link needed).
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+static int get_encode() {
+  if (g_encode) return 0;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr) return (int)cudaErrorNotSupported;
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return 0;
+}
+
+// 2-D bf16 row-major [rows, cols] with row stride `ld` elements; box = box_rows x 64 columns, 128B swizzle.
+static int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  int rc = get_encode();
+  if (rc) return rc;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * 2) % 16) || cols % 8) return (int)cudaErrorInvalidValue;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
+}
+
+static int sm_count() {
+  int dev = 0, n = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+static GemmShape make_shape(int M, int N, int K) {
+  GemmShape s;
+  s.M = M; s.N = N; s.K = K;
+  s.m_tiles = (M + BM - 1) / BM;
+  s.n_tiles = (N + BN - 1) / BN;
+  s.k_tiles = (K + BK - 1) / BK;
+  s.group = 8;
+  return s;
+}
+
+template <class Epi>
+__global__ void __launch_bounds__(kThreads, 1) tc_kernel(const __grid_constant__ CUtensorMap ta,
+                                                        const __grid_constant__ CUtensorMap tb, GemmShape sh,
+                                                        Epi epi, uint32_t* status) {
+  Epi e = epi;
+  gemm_body(&ta, &tb, sh, e, status);
+}
+
+template <class Epi>
+static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const Epi& epi,
+                  uint32_t* status, cudaStream_t st) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  CUtensorMap ta, tb;
+  int rc = make_tmap(&ta, A, M, K, lda, BM);
+  if (rc) return rc;
+  rc = make_tmap(&tb, B, N, K, ldb, BN);
+  if (rc) return rc;
+  GemmShape sh = make_shape(M, N, K);
+  cudaError_t e = cudaFuncSetAttribute(tc_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+  if (e != cudaSuccess) return (int)e;
+  const int tiles = sh.m_tiles * sh.n_tiles;
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  tc_kernel<Epi><<<grid, kThreads, kSmemBytes, st>>>(ta, tb, sh, epi, status);
+  return (int)cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Epilogues (one TMEM lane = one output row per thread)
+// ---------------------------------------------------------------------------
+struct StoreEpi {
+  void* C;
+  int64_t ldc;
+  int out_f32;
+  int vec_ok;  // rows 16-byte aligned
+
+  __device__ void row(int m0, int n0, int r, uint32_t taddr, const GemmShape& sh) {
+    const int m = m0 + r;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      float v[32];
+      tmem_ld32(taddr + c, v);
+      if (m >= sh.M) continue;
+      const int n = n0 + c;
+      if (out_f32) {
+        float* dst = reinterpret_cast<float*>(C) + (int64_t)m * ldc + n;
+        if (vec_ok && n + 32 <= sh.N) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) if (n + j < sh.N) dst[j] = v[j];
+        }
+      } else {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(C) + (int64_t)m * ldc + n;
+        if (vec_ok && n + 32 <= sh.N) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) store16<__nv_bfloat16>(dst + j, v + j);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) if (n + j < sh.N) dst[j] = __float2bfloat16_rn(v[j]);
+        }
+      }
+    }
+  }
+};
+
+struct CeStatsEpi {
+  const int64_t* targets;
+  float* pmax;   // [M, n_tiles]
+  float* psum;   // [M, n_tiles]
+  float* tlogit; // [M]
+
+  __device__ void row(int m0, int n0, int r, uint32_t taddr, const GemmShape& sh) {
+    const int m = m0 + r;
+    const int64_t tgt = m < sh.M ? targets[m] : -1;
+    float mx = -INFINITY, sum = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      float v[32];
+      tmem_ld32(taddr + c, v);
+      const int n = n0 + c;
+      float cm = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) if (n + j < sh.N) cm = fmaxf(cm, v[j]);
+      if (cm > mx) {
+        sum = (mx == -INFINITY) ? 0.f : sum * __expf(mx - cm);
+        mx = cm;
+      }
+      if (mx != -INFINITY) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) if (n + j < sh.N) sum += __expf(v[j] - mx);
+      }
+      if (tgt >= n && tgt < n + 32) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) if (tgt == n + j) tlogit[m] = v[j];
+      }
+    }
+    if (m < sh.M) {
+      const int64_t idx = (int64_t)m * sh.n_tiles + n0 / BN;
+      pmax[idx] = mx;
+      psum[idx] = sum;
+    }
+  }
+};
+
+struct CeGradEpi {
+  const int64_t* targets;
+  const float* lse;
+  const float* count;
+  __nv_bfloat16* dl;
+  int64_t ldd;
+  int64_t ignore_index;
+  int vec_ok;
+
+  __device__ void row(int m0, int n0, int r, uint32_t taddr, const GemmShape& sh) {
+    const int m = m0 + r;
+    const int64_t tgt = m < sh.M ? targets[m] : ignore_index;
+    const bool valid = m < sh.M && tgt != ignore_index;
+    const float inv = 1.f / fmaxf(*count, 1.f);
+    const float l = valid ? lse[m] : 0.f;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      float v[32];
+      tmem_ld32(taddr + c, v);
+      if (m >= sh.M) continue;
+      const int n = n0 + c;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float p = valid ? __expf(v[j] - l) * inv : 0.f;
+        if (valid && tgt == n + j) p -= inv;
+        v[j] = p;
+      }
+      __nv_bfloat16* dst = dl + (int64_t)m * ldd + n;
+      if (vec_ok && n + 32 <= sh.N) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) store16<__nv_bfloat16>(dst + j, v + j);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) if (n + j < sh.N) dst[j] = __float2bfloat16_rn(v[j]);
+      }
+    }
+  }
+};
+
+__global__ void ce_merge_kernel(const float* pmax, const float* psum, const float* tlogit, const int64_t* targets,
+                                const float* count, int M, int n_tiles, int64_t ignore_index, float* lse_out,
+                                float* loss_rows) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= M) return;
+  float mx = -INFINITY, s = 0.f;
+  for (int t = 0; t < n_tiles; ++t) {
+    const float pm = pmax[(int64_t)m * n_tiles + t];
+    const float ps = psum[(int64_t)m * n_tiles + t];
+    if (pm == -INFINITY) continue;
+    if (pm > mx) {
+      s = (mx == -INFINITY) ? 0.f : s * __expf(mx - pm);
+      mx = pm;
+    }
+    s += ps * __expf(pm - mx);
+  }
+  const float lse = mx + __logf(s);
+  lse_out[m] = lse;
+  const int64_t tgt = targets[m];
+  const float inv = 1.f / fmaxf(*count, 1.f);
+  loss_rows[m] = (tgt == ignore_index) ? 0.f : (lse - tlogit[m]) * inv;
+}
+
+}  // namespace tc
+}  // namespace nfb
+
+using namespace nfb;
+using namespace nfb::tc;
+
+// C[M, N] = A[M, K] @ B[N, K]^T, A/B bf16 with row strides lda/ldb; C bf16 (out_f32=0) or fp32.
+NFB_API int nfb_tc_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, int64_t lda, int64_t ldb,
+                             int64_t ldc, int out_f32, uint32_t* status, void* stream) {
+  StoreEpi epi;
+  epi.C = C; epi.ldc = ldc; epi.out_f32 = out_f32;
+  const int es = out_f32 ? 4 : 2;
+  epi.vec_ok = ((reinterpret_cast<uintptr_t>(C) & 15) == 0) && ((ldc * es) % 16 == 0);
+  return launch(A, lda, B, ldb, M, N, K, epi, status, (cudaStream_t)stream);
+}
+
+NFB_API int nfb_ce_tc_tiles(int V) { return (V + BN - 1) / BN; }
+
+// Pass 1: online-softmax partials per (row, vocab tile) and the target logit.
+NFB_API int nfb_ce_tc_stats(const void* hidden, int64_t ldh, const void* weight, int64_t ldw, const int64_t* targets,
+                            int M, int V, int H, float* pmax, float* psum, float* tlogit, uint32_t* status,
+                            void* stream) {
+  CeStatsEpi epi{targets, pmax, psum, tlogit};
+  return launch(hidden, ldh, weight, ldw, M, V, H, epi, status, (cudaStream_t)stream);
+}
+
+NFB_API int nfb_ce_tc_merge(const float* pmax, const float* psum, const float* tlogit, const int64_t* targets,
+                            const float* count, int M, int V, int64_t ignore_index, float* lse, float* loss_rows,
+                            void* stream) {
+  if (M <= 0) return 0;
+  ce_merge_kernel<<<(M + 255) / 256, 256, 0, (cudaStream_t)stream>>>(pmax, psum, tlogit, targets, count, M,
+                                                                     (V + BN - 1) / BN, ignore_index, lse, loss_rows);
+  return (int)cudaGetLastError();
+}
+
+// Pass 2: dl[M, V] = (softmax - onehot) / count in bf16, recomputing the logits in TMEM.
+NFB_API int nfb_ce_tc_grad(const void* hidden, int64_t ldh, const void* weight, int64_t ldw, const int64_t* targets,
+                           const float* lse, const float* count, int64_t ignore_index, int M, int V, int H, void* dl,
+                           int64_t ldd, uint32_t* status, void* stream) {
+  CeGradEpi epi;
+  epi.targets = targets; epi.lse = lse; epi.count = count; epi.dl = (__nv_bfloat16*)dl; epi.ldd = ldd;
+  epi.ignore_index = ignore_index;
+  epi.vec_ok = ((reinterpret_cast<uintptr_t>(dl) & 15) == 0) && ((ldd * 2) % 16 == 0);
+  return launch(hidden, ldh, weight, ldw, M, V, H, epi, status, (cudaStream_t)stream);
+}

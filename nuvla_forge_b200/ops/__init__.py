@@ -5,6 +5,7 @@ plus the ops the reference left to PyTorch.
 """
 
 from .._native import HAS_NATIVE
+from . import ce_tc  # noqa: F401  (registers the tcgen05 cross-entropy path)
 from .attention import attention
 from .chunked_ce import chunked_cross_entropy
 from .image import normalise_images, patchify_images

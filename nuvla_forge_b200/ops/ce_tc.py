@@ -1,0 +1,116 @@
+"""Cross entropy on the tcgen05 GEMM (native csrc/ce_tc.cu).
+
+The [M, V] logits live only in tensor memory: pass 1 turns each 128x256 logit
+tile into per-row online-softmax partials, a merge kernel produces the
+log-sum-exp and the per-row losses, and pass 2 recomputes the tile and writes
+``(softmax - onehot) / count`` in bf16 for one row chunk at a time, which the
+two gradient GEMMs (cuBLAS) consume. Like the reference
+(nuvla_forge/kernels/chunked_ce.py:120-182) the gradients are produced during
+forward and backward only scales them; unlike it, no fp32 logit tile exists and
+nothing synchronises the host.
+"""
+
+from __future__ import annotations
+
+import os
+
+import torch
+
+from .. import _native as nat
+from .chunked_ce import count_valid, register_tc
+
+_status: dict[int, torch.Tensor] = {}
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _status.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=device)
+        _status[idx] = t
+    return t
+
+
+def check_status(device: torch.device | None = None) -> None:
+    for idx, t in _status.items():
+        v = int(t.item())
+        if v:
+            raise RuntimeError(f"tcgen05 pipeline on cuda:{idx} gave up waiting (status {v:#x})")
+
+
+def tc_gemm(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
+    """C = a @ b.T on the native tcgen05 core (a [M,K], b [N,K] bf16, K % 8 == 0)."""
+    M, K = a.shape
+    N = b.shape[0]
+    c = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    nat.call("nfb_tc_gemm_bf16", nat.ptr(a), nat.ptr(b), nat.ptr(c), M, N, K, a.stride(0), b.stride(0), c.stride(0),
+             int(out_dtype == torch.float32), nat.ptr(status_word(a.device)), nat.stream(a.device))
+    return c
+
+
+class _CrossEntropyTC(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, hidden, weight, targets, ignore_index, chunk_rows):
+        M, H = hidden.shape
+        V = weight.shape[0]
+        dev = hidden.device
+        h = hidden if hidden.dtype == torch.bfloat16 else hidden.to(torch.bfloat16)
+        w = weight if weight.dtype == torch.bfloat16 else weight.to(torch.bfloat16)
+        h = h.contiguous()
+        w = w.contiguous()
+        tg = targets.contiguous()
+        st = status_word(dev)
+        count = count_valid(tg, ignore_index)
+        n_tiles = int(nat.lib().nfb_ce_tc_tiles(V))
+        pmax = torch.empty((M, n_tiles), dtype=torch.float32, device=dev)
+        psum = torch.empty((M, n_tiles), dtype=torch.float32, device=dev)
+        tlogit = torch.zeros(M, dtype=torch.float32, device=dev)
+        lse = torch.empty(M, dtype=torch.float32, device=dev)
+        loss_rows = torch.empty(M, dtype=torch.float32, device=dev)
+        s = nat.stream(dev)
+        nat.call("nfb_ce_tc_stats", nat.ptr(h), h.stride(0), nat.ptr(w), w.stride(0), nat.ptr(tg), M, V, H,
+                 nat.ptr(pmax), nat.ptr(psum), nat.ptr(tlogit), nat.ptr(st), s)
+        nat.call("nfb_ce_tc_merge", nat.ptr(pmax), nat.ptr(psum), nat.ptr(tlogit), nat.ptr(tg), nat.ptr(count), M, V,
+                 ignore_index, nat.ptr(lse), nat.ptr(loss_rows), s)
+        d_hidden = torch.empty((M, H), dtype=hidden.dtype, device=dev)
+        d_weight = torch.zeros((V, H), dtype=torch.float32, device=dev)
+        for r0 in range(0, M, chunk_rows):
+            r1 = min(r0 + chunk_rows, M)
+            hc = h[r0:r1]
+            dl = torch.empty((r1 - r0, V), dtype=torch.bfloat16, device=dev)
+            nat.call("nfb_ce_tc_grad", nat.ptr(hc), hc.stride(0), nat.ptr(w), w.stride(0), nat.ptr(tg[r0:r1]),
+                     nat.ptr(lse[r0:r1]), nat.ptr(count), ignore_index, r1 - r0, V, H, nat.ptr(dl), dl.stride(0),
+                     nat.ptr(st), s)
+            d_hidden[r0:r1] = torch.mm(dl, w).to(hidden.dtype)
+            d_weight += torch.mm(dl.t(), hc, out_dtype=torch.float32)
+            del dl
+        ctx.save_for_backward(d_hidden, d_weight)
+        ctx.wdtype = weight.dtype
+        return loss_rows.sum()
+
+    @staticmethod
+    def backward(ctx, g):
+        d_hidden, d_weight = ctx.saved_tensors
+        return d_hidden * g.to(d_hidden.dtype), (d_weight * g).to(ctx.wdtype), None, None, None
+
+
+def cross_entropy_tc(hidden, weight, targets, ignore_index: int = -100, chunk_rows: int | None = None):
+    """Mean CE over hidden @ weight.T on the tcgen05 path, or None when the shape is unsupported."""
+    if not (hidden.is_cuda and nat.HAS_NATIVE) or hidden.dim() != 2:
+        return None
+    M, H = hidden.shape
+    V = weight.shape[0]
+    if H % 8 or M == 0 or M >= 2**31 or V >= 2**31:
+        return None
+    if chunk_rows is None:
+        # bound the bf16 dlogits buffer to ~256 MiB
+        chunk_rows = max(128, (256 * 2**20) // (2 * V) // 128 * 128)
+    return _CrossEntropyTC.apply(hidden, weight, targets, int(ignore_index), int(chunk_rows))
+
+
+def enable(flag: bool = True) -> None:
+    """Route ops.chunked_cross_entropy through the tcgen05 path (default: on unless NFB_CE_TC=0)."""
+    register_tc(cross_entropy_tc if flag else None)
+
+
+enable(os.environ.get("NFB_CE_TC", "1") != "0")
