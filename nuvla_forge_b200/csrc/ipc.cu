@@ -1,0 +1,42 @@
+// Peer-mapped device buffers for the fused collectives (CUDA IPC, no multicast).
+//
+// Each rank allocates one buffer, exports a CUDA IPC handle, and opens every
+// peer's handle; the resulting pointers are peer mappings over NVLink that the
+// kernels in comm.cu address with plain loads and stores. No NVLink multicast
+// object is ever created, so a rank that exits cannot leave peers bound to a
+// multicast group.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#define NFB_API extern "C" __attribute__((visibility("default")))
+
+NFB_API int nfb_ipc_handle_bytes() { return (int)sizeof(cudaIpcMemHandle_t); }
+
+// Allocate `bytes` of zeroed device memory on the current device and export its IPC handle.
+NFB_API int nfb_ipc_alloc(uint64_t bytes, void** ptr, void* handle_out) {
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return (int)e;
+  e = cudaMemset(p, 0, bytes);
+  if (e != cudaSuccess) { cudaFree(p); return (int)e; }
+  cudaIpcMemHandle_t h;
+  e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) { cudaFree(p); return (int)e; }
+  memcpy(handle_out, &h, sizeof(h));
+  *ptr = p;
+  return 0;
+}
+
+// Map a peer's exported buffer into this process (peer access enabled lazily).
+NFB_API int nfb_ipc_open(const void* handle, void** ptr) {
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return (int)cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+}
+
+NFB_API int nfb_ipc_close(void* ptr) { return (int)cudaIpcCloseMemHandle(ptr); }
+
+NFB_API int nfb_ipc_free(void* ptr) { return (int)cudaFree(ptr); }
+
+NFB_API int nfb_device_synchronize() { return (int)cudaDeviceSynchronize(); }

@@ -98,7 +98,8 @@ class DistributedDataParallel(nn.Module):
         self.ws = None
         if comm == "fused":
             maxb = max(b.end - b.start for b in self.buckets)
-            self.ws = SymmetricWorkspace(2 * maxb * 2, group=process_group, device=dev)
+            region = (maxb * 2 + 255) // 256 * 256
+            self.ws = SymmetricWorkspace(2 * region, group=process_group, device=dev)
             self.send_off = self.ws.alloc(maxb * 2)
             self.recv_off = self.ws.alloc(maxb * 2)
         # timing of the collective stream (exposed-communication accounting)

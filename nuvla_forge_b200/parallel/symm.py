@@ -1,19 +1,19 @@
-"""Symmetric device memory for the fused NVLink collectives.
+"""Symmetric device memory for the fused NVLink collectives (CUDA IPC peer mappings).
 
-One buffer of the same size on every rank, mapped into every peer's address
-space by PyTorch's symmetric-memory rendezvous (CUDA VMM + IPC handles
-exchanged through the process group's store). The native kernels (csrc/comm.cu)
-receive every rank's base pointer and address peers with plain loads and
-stores over NVLink.
+Every rank allocates one buffer of the same size (native ``nfb_ipc_alloc``),
+exports a CUDA IPC handle, gathers all ranks' handles through the process
+group, and maps every peer's buffer into its own address space. The native
+kernels (csrc/comm.cu) receive all ranks' base pointers and address peers with
+plain loads and stores over NVLink. No NVLink multicast object is created.
 
 Layout (byte offsets): [flags | scalar exchange | data ...]. ``alloc`` hands
-out 256-byte-aligned regions of the data area at construction time (callers
-reserve what they need up front; every rank must reserve the same sequence).
+out 256-byte-aligned regions of the data area (every rank must reserve the
+same sequence).
 
 Each collective kind uses its own flag *slot*; every launch takes the next
 epoch of its slot (a host counter that all ranks advance identically, because
-all ranks launch the same collectives in the same order). Bounded waits in
-the kernels report into ``status``; :meth:`check` raises ``CommTimeout``.
+all ranks launch the same collectives in the same order). Bounded waits in the
+kernels report into ``status``; :meth:`check` raises ``CommTimeout``.
 """
 
 from __future__ import annotations
@@ -43,30 +43,59 @@ def decode_status(v: int) -> str:
     return f"{kinds.get(code, f'code {code}')} at site {where & 0xFFFF} (peer {where >> 16})"
 
 
+def _ipc_fns():
+    lib = nat.lib()
+    for name, res, args in (("nfb_ipc_handle_bytes", ctypes.c_int, []),
+                            ("nfb_ipc_alloc", ctypes.c_int, [ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p),
+                                                             ctypes.c_void_p]),
+                            ("nfb_ipc_open", ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+                            ("nfb_ipc_close", ctypes.c_int, [ctypes.c_void_p]),
+                            ("nfb_ipc_free", ctypes.c_int, [ctypes.c_void_p]),
+                            ("nfb_device_synchronize", ctypes.c_int, [])):
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
 class SymmetricWorkspace:
     def __init__(self, data_bytes: int, group: dist.ProcessGroup | None = None,
                  device: torch.device | None = None, timeout_s: float | None = None):
-        import torch.distributed._symmetric_memory as symm_mem
-
         self.group = group or dist.group.WORLD
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.rank = dist.get_rank(self.group)
         self.world = dist.get_world_size(self.group)
+        lib = _ipc_fns()
+        self._lib = lib
         self.flag_off = 0
-        self.scalar_off = _align(int(nat.lib().nfb_comm_flag_bytes()))
+        self.scalar_off = _align(int(lib.nfb_comm_flag_bytes()))
         self.data_off = self.scalar_off + 256
         self.total = self.data_off + _align(max(int(data_bytes), 256))
-        self.buf = symm_mem.empty(self.total, dtype=torch.uint8, device=self.device)
-        self.buf.zero_()
-        torch.cuda.synchronize(self.device)
-        try:
-            self.handle = symm_mem.rendezvous(self.buf, self.group)
-        except Exception:  # older API wants the group enabled first
-            symm_mem.enable_symm_mem_for_group(self.group.group_name)
-            self.handle = symm_mem.rendezvous(self.buf, self.group.group_name)
-        ptrs = [int(p) for p in self.handle.buffer_ptrs]
+        hb = int(lib.nfb_ipc_handle_bytes())
+        handle = (ctypes.c_char * hb)()
+        local = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            rc = lib.nfb_ipc_alloc(self.total, ctypes.byref(local), ctypes.cast(handle, ctypes.c_void_p))
+            if rc != 0:
+                raise RuntimeError(f"nfb_ipc_alloc({self.total}) failed with CUDA error {rc}")
+            lib.nfb_device_synchronize()
+        self._local = local.value
+        handles: list = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=self.group)
+        ptrs, self._opened = [], []
+        with torch.cuda.device(self.device):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(self._local)
+                    continue
+                p = ctypes.c_void_p()
+                buf = (ctypes.c_char * hb).from_buffer_copy(h)
+                rc = lib.nfb_ipc_open(ctypes.cast(buf, ctypes.c_void_p), ctypes.byref(p))
+                if rc != 0:
+                    raise RuntimeError(f"rank {self.rank}: opening rank {r}'s IPC handle failed (CUDA error {rc})")
+                ptrs.append(p.value)
+                self._opened.append(p.value)
         self.bases = (ctypes.c_uint64 * self.world)(*ptrs)
-        self.multicast_ptr = int(getattr(self.handle, "multicast_ptr", 0) or 0)
         self._cursor = self.data_off
         self.epochs = [0] * 8
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
@@ -83,9 +112,8 @@ class SymmetricWorkspace:
         self._cursor = end
         return off
 
-    def local_view(self, off: int, numel: int, dtype: torch.dtype) -> torch.Tensor:
-        es = torch.empty((), dtype=dtype).element_size()
-        return self.buf[off: off + numel * es].view(dtype)
+    def local_ptr(self, off: int = 0) -> int:
+        return self._local + off
 
     def next_epoch(self, slot: int) -> int:
         self.epochs[slot] = (self.epochs[slot] + 1) & 0x7FFFFFFF
@@ -99,12 +127,22 @@ class SymmetricWorkspace:
         if v:
             raise CommTimeout(f"rank {self.rank}: fused collective failed: {decode_status(v)}")
 
+    def close(self) -> None:
+        """Unmap peers and free the local buffer (call on every rank, with no kernel in flight)."""
+        if getattr(self, "_local", None) is None:
+            return
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize(self.device)
+            for p in self._opened:
+                self._lib.nfb_ipc_close(ctypes.c_void_p(p))
+            self._lib.nfb_ipc_free(ctypes.c_void_p(self._local))
+        self._opened = []
+        self._local = None
+
 
 def symmetric_memory_available() -> bool:
     if not (torch.cuda.is_available() and nat.HAS_NATIVE and dist.is_initialized()):
         return False
-    try:
-        import torch.distributed._symmetric_memory  # noqa: F401
-    except Exception:  # noqa: BLE001
+    if os.environ.get("NFB_DISABLE_FUSED_COMM", "0") == "1":
         return False
     return dist.get_world_size() <= 8

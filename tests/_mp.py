@@ -14,14 +14,21 @@ def free_port() -> int:
         return s.getsockname()[1]
 
 
-def _entry(rank, world, port, fn, q, args, timeout_s):
+def _entry(rank, world, port, fn, q, args, timeout_s, backend="gloo", env=None):
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
+    os.environ.update(env or {})
     try:
-        dist.init_process_group("gloo", rank=rank, world_size=world,
-                                timeout=datetime.timedelta(seconds=timeout_s))
+        kw = {}
+        if backend == "nccl":
+            import torch
+
+            torch.cuda.set_device(rank)
+            kw["device_id"] = torch.device(f"cuda:{rank}")
+        dist.init_process_group(backend, rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=timeout_s), **kw)
         res = fn(rank, world, *args)
         q.put((rank, "ok", res))
     except BaseException as exc:  # noqa: BLE001 - report to the parent
@@ -34,12 +41,16 @@ def _entry(rank, world, port, fn, q, args, timeout_s):
             pass
 
 
-def run_ranks(fn, world: int = 2, args=(), timeout_s: float = 60.0, join_s: float = 120.0) -> dict:
-    """Run fn(rank, world, *args) on `world` gloo ranks; returns {rank: (status, result)}."""
+def run_ranks(fn, world: int = 2, args=(), timeout_s: float = 60.0, join_s: float = 120.0, backend: str = "gloo",
+              env: dict | None = None) -> dict:
+    """Run fn(rank, world, *args) on `world` ranks (gloo on CPU, or nccl with rank r on cuda:r).
+
+    Returns {rank: (status, result)}."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=_entry, args=(r, world, port, fn, q, args, timeout_s)) for r in range(world)]
+    procs = [ctx.Process(target=_entry, args=(r, world, port, fn, q, args, timeout_s, backend, env))
+             for r in range(world)]
     for p in procs:
         p.start()
     out = {}

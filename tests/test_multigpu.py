@@ -1,0 +1,128 @@
+"""Multi-GPU (NCCL + CUDA IPC peer memory) tests of the fused collectives and DDP.
+
+Each test spawns one process per GPU (2 to 4). NVLS is off in NCCL and the
+fused kernels use plain peer loads/stores (no multicast objects).
+"""
+
+import time
+
+import pytest
+import torch
+
+from _mp import run_ranks
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+ENV = {"NCCL_NVLS_ENABLE": "0"}
+
+
+def _world():
+    return min(torch.cuda.device_count(), 4)
+
+
+def _fused_ar(rank, world, sizes):
+    import torch.distributed as dist
+
+    from nuvla_forge_b200 import _native as nat
+    from nuvla_forge_b200.parallel.symm import SLOT_DDP, SymmetricWorkspace
+
+    dev = torch.device("cuda", rank)
+    maxn = max(sizes)
+    ws = SymmetricWorkspace(4 * maxn + 4096, device=dev, timeout_s=10)
+    send, recv = ws.alloc(2 * maxn), ws.alloc(2 * maxn)
+    worst = 0.0
+    for n in sizes:
+        g = torch.Generator(device=dev).manual_seed(1000 * rank + n)
+        x = torch.randn(n, generator=g, device=dev)
+        allx = [torch.empty_like(x) for _ in range(world)]
+        dist.all_gather(allx, x)
+        ref = sum(t.to(torch.bfloat16).double() for t in allx) / world
+        y = x.clone()
+        for _ in range(2):
+            y.copy_(x)
+            nat.call("nfb_ar_twoshot", ws.bases_ptr(), rank, world, nat.ptr(y), nat.ptr(y), n, send, recv,
+                     ws.flag_off, SLOT_DDP, 1.0 / world, ws.next_epoch(SLOT_DDP), ws.timeout_ns, nat.ptr(ws.status),
+                     32, nat.stream(dev))
+        torch.cuda.synchronize(dev)
+        ws.check()
+        err = float((y.double() - ref).norm() / ref.norm())
+        worst = max(worst, err)
+    dist.barrier()
+    ws.close()
+    return worst
+
+
+def test_fused_allreduce_matches_reference():
+    w = _world()
+    sizes = [8 * w, 8 * w * 1000, 8 * w * 131071, 8 * w * 1048576]
+    out = run_ranks(_fused_ar, w, args=(sizes,), backend="nccl", env=ENV, timeout_s=60)
+    assert len(out) == w and all(st == "ok" for st, _ in out.values()), out
+    assert max(r for _, r in out.values()) < 4e-3
+
+
+def _ddp_parity(rank, world, comm):
+    from nuvla_forge_b200.optim import FlatAdamW
+    from nuvla_forge_b200.parallel import DistributedDataParallel
+
+    dev = torch.device("cuda", rank)
+    torch.manual_seed(0)
+    model = torch.nn.Sequential(torch.nn.Linear(256, 512), torch.nn.GELU(), torch.nn.Linear(512, 256)).to(dev)
+    ddp = DistributedDataParallel(model, bucket_cap_mb=0.25, comm=comm, param_dtype=torch.float32)
+    opt = FlatAdamW(ddp.space, lr=1e-3, ddp=ddp)
+    for step in range(3):
+        for m in range(2):
+            g = torch.Generator(device=dev).manual_seed(100 * step + 10 * rank + m)
+            x = torch.randn(64, 256, generator=g, device=dev)
+            ctx = ddp.no_sync() if m == 0 else torch.enable_grad()
+            with ctx:
+                (ddp(x).square().mean() / 2).backward()
+        opt.step()
+        opt.zero_grad()
+    torch.cuda.synchronize(dev)
+    ddp.check_health()
+    return ddp.space.master.cpu()
+
+
+def test_ddp_fused_matches_nccl_fp32():
+    w = _world()
+    a = run_ranks(_ddp_parity, w, args=("fused",), backend="nccl", env=ENV)
+    b = run_ranks(_ddp_parity, w, args=("nccl_fp32",), backend="nccl", env=ENV)
+    assert all(st == "ok" for st, _ in a.values()) and all(st == "ok" for st, _ in b.values()), (a, b)
+    for r in range(w):
+        assert torch.equal(a[r][1], a[0][1])
+        rel = float((a[r][1] - b[r][1]).norm() / b[r][1].norm())
+        assert rel < 1e-3, rel
+
+
+def _peer_exit(rank, world):
+    import torch.distributed as dist
+
+    from nuvla_forge_b200.parallel import DistributedDataParallel
+    from nuvla_forge_b200.parallel.watchdog import Heartbeat, PeerLost
+
+    dev = torch.device("cuda", rank)
+    model = torch.nn.Linear(64, 64).to(dev)
+    ddp = DistributedDataParallel(model, comm="fused", param_dtype=torch.float32)
+    hb = Heartbeat(interval=0.1).start()
+    ddp(torch.randn(8, 64, device=dev)).sum().backward()      # one full step on every rank
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    if rank == world - 1:
+        hb.stop()            # leaves between steps: nothing of ours in flight
+        return "left"
+    time.sleep(1.5)
+    try:
+        hb.check_peers(max_age=0.8)   # host-side check before the next launch
+    except PeerLost as e:
+        hb.stop()
+        return f"detected: {e}"
+    hb.stop()
+    return "missed"
+
+
+def test_peer_exit_detected_on_host_before_next_launch():
+    w = _world()
+    out = run_ranks(_peer_exit, w, backend="nccl", env=ENV, timeout_s=30, join_s=120)
+    assert out[w - 1] == ("ok", "left"), out
+    for r in range(w - 1):
+        assert out[r][0] == "ok" and out[r][1].startswith("detected"), out
