@@ -46,6 +46,8 @@ def parse(argv=None):
     ap.add_argument("--grad-accum", type=int, default=4)
     ap.add_argument("--bucket-mb", type=float, default=100.0)
     ap.add_argument("--comm", default="auto")
+    ap.add_argument("--fsdp", action="store_true", help="fully sharded (BASELINE config 4 uses --model-config 3b "
+                                                         "--batch-size 4 --grad-accum 1)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--json-out", default=None)
     return ap.parse_args(argv)
@@ -155,7 +157,7 @@ def run_native(args) -> dict:
         raise RuntimeError("native library not loaded on a GPU box")
     cfg = NuVLAConfig.preset(args.model_config)
     trainer = Trainer(cfg, info, bucket_mb=args.bucket_mb, comm=args.comm, grad_accum=args.grad_accum,
-                      no_sync_accum=True, bf16=True)
+                      no_sync_accum=True, bf16=True, fsdp=args.fsdp)
     spec = SampleSpec.for_model(cfg)
     src = SyntheticBatchSource(spec, args.batch_size, seed=7, rank=info.rank, world=info.world)
     host_iter = iter(src)
@@ -219,7 +221,8 @@ def run_native(args) -> dict:
                    if args.model_config == "1b" else f"nuVLA-{args.model_config}",
                    "global_batch": gb, "micro_batch_per_gpu": args.batch_size, "grad_accum": A,
                    "seq_len": cfg.n_images * cfg.pooled_tokens + cfg.text_len,
-                   "parallelism": f"dp{info.world}", "comm": getattr(trainer.model, "comm", "?"),
+                   "parallelism": (f"fsdp{info.world}" if args.fsdp else f"dp{info.world}"),
+                   "comm": getattr(trainer.model, "comm", "?"),
                    "bucket_mb": args.bucket_mb,
                    "l2": "inputs larger than L2 (58 MB uint8 per micro-batch, tens of GB of activations)"},
         "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "peak_mem_mib": peak, "impl": "native",

@@ -1,7 +1,7 @@
 // Fused collectives over NVLink 5 / NVSwitch peer memory (one process per GPU).
 //
 // Every rank owns one symmetric buffer (same size on every rank, mapped into
-// every peer's address space by torch's symmetric-memory rendezvous); kernels
+// every peer's address space through CUDA IPC handles, parallel/symm.py); kernels
 // receive the base pointers of all ranks' buffers by value and address peer
 // memory with ordinary loads and stores. Layout of a rank's symmetric buffer
 // is decided by the host runtime (parallel/symm.py) and passed as byte offsets.
@@ -179,6 +179,7 @@ struct RsArgs {
   int64_t param_off;         // byte offset of this rank's bf16 parameter shard in its symmetric buffer (-1: none)
   float lr, beta1, beta2, eps, wd, bc1, bc2_sqrt, clip;
   int trailing_barrier;
+  int accumulate;            // nfb_rs_f32: out += reduced instead of out = reduced
 };
 
 template <bool ADAM>
@@ -204,8 +205,14 @@ __global__ void __launch_bounds__(512) rs_kernel(RsArgs a) {
     for (int j = 0; j < 8; ++j) { g[j] *= a.scale; ss += g[j] * g[j]; }
     if (!ADAM) {
       float4* d = reinterpret_cast<float4*>(a.out + v * 8);
-      d[0] = make_float4(g[0], g[1], g[2], g[3]);
-      d[1] = make_float4(g[4], g[5], g[6], g[7]);
+      if (a.accumulate) {
+        float4 o0 = d[0], o1 = d[1];
+        d[0] = make_float4(o0.x + g[0], o0.y + g[1], o0.z + g[2], o0.w + g[3]);
+        d[1] = make_float4(o1.x + g[4], o1.y + g[5], o1.z + g[6], o1.w + g[7]);
+      } else {
+        d[0] = make_float4(g[0], g[1], g[2], g[3]);
+        d[1] = make_float4(g[4], g[5], g[6], g[7]);
+      }
     } else {
       float p[8], m[8], w[8];
       float4* pp = reinterpret_cast<float4*>(a.param + v * 8);
@@ -360,15 +367,15 @@ NFB_API int nfb_ar_twoshot(const uint64_t* bases, int rank, int world, const flo
 
 NFB_API int nfb_rs_f32(const uint64_t* bases, int rank, int world, int64_t shard, int64_t send_off, int64_t flag_off,
                        int slot, float scale, uint32_t epoch, uint64_t timeout_ns, uint32_t* status, float* out,
-                       float* sumsq_partials, uint32_t* ticket, float* sumsq_out, int trailing_barrier, int ctas,
-                       void* stream) {
+                       float* sumsq_partials, uint32_t* ticket, float* sumsq_out, int trailing_barrier,
+                       int accumulate, int ctas, void* stream) {
   if (world < 1 || world > kMaxWorld || shard % 8 || ctas < 1 || ctas > kMaxCtas) return (int)cudaErrorInvalidValue;
   RsArgs a{};
   a.peers = make_peers(bases, world);
   a.shard = shard; a.send_off = send_off; a.flag_off = flag_off; a.rank = rank; a.world = world; a.slot = slot;
   a.scale = scale; a.epoch = epoch; a.timeout_ns = timeout_ns; a.status = status; a.out = out;
   a.sumsq_partials = sumsq_partials; a.ticket = ticket; a.sumsq_out = sumsq_out; a.param_off = -1;
-  a.trailing_barrier = trailing_barrier;
+  a.trailing_barrier = trailing_barrier; a.accumulate = accumulate;
   rs_kernel<false><<<ctas, 512, 0, (cudaStream_t)stream>>>(a);
   return (int)cudaGetLastError();
 }

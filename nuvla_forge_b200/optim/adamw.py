@@ -21,7 +21,7 @@ class FlatAdamW:
     def __init__(self, space, lr: float = 3e-4, betas: tuple[float, float] = (0.9, 0.999), eps: float = 1e-8,
                  weight_decay: float = 0.01, max_grad_norm: float = 1.0, ddp=None, grads: torch.Tensor | None = None,
                  master: torch.Tensor | None = None, params: torch.Tensor | None = None,
-                 norm_allreduce=None):
+                 norm_allreduce=None, params_ptr: int | None = None, after_step=None):
         self.space = space
         self.master = master if master is not None else space.master
         self.grads = grads if grads is not None else space.grads
@@ -33,6 +33,8 @@ class FlatAdamW:
         self.max_grad_norm = max_grad_norm
         self.ddp = ddp
         self.norm_allreduce = norm_allreduce   # FSDP: sums the norm^2 over ranks on the device
+        self.params_ptr = params_ptr           # raw bf16 destination (FSDP: the peer-mapped shard region)
+        self.after_step = after_step
         self.m = torch.zeros_like(self.master)
         self.v = torch.zeros_like(self.master)
         self.step_count = 0
@@ -65,13 +67,19 @@ class FlatAdamW:
             self.compute_norm2()
         b1, b2 = self.betas
         if self.native:
+            import ctypes
+
             lp = self.params if (self.params is not None and self.params.dtype == torch.bfloat16) else None
+            lp_ptr = ctypes.c_void_p(self.params_ptr) if self.params_ptr is not None else nat.ptr(lp)
             nat.call("nfb_adamw_flat", nat.ptr(self.master), nat.ptr(self.grads), nat.ptr(self.m), nat.ptr(self.v),
-                     nat.ptr(lp), self.master.numel(), self.lr, b1, b2, self.eps, self.weight_decay,
+                     lp_ptr, self.master.numel(), self.lr, b1, b2, self.eps, self.weight_decay,
                      self.step_count, 1.0, nat.ptr(self.norm2) if clip else nat.ptr(None),
                      float(self.max_grad_norm if clip else 0.0), nat.stream(self.master.device))
-            if lp is None and self.params is not None and self.params.data_ptr() != self.master.data_ptr():
+            if (self.params_ptr is None and lp is None and self.params is not None
+                    and self.params.data_ptr() != self.master.data_ptr()):
                 self.params.copy_(self.master)
+            if self.after_step is not None:
+                self.after_step()
             return
         with torch.no_grad():
             g = self.grads
@@ -88,6 +96,8 @@ class FlatAdamW:
             p.addcdiv_(self.m, denom, value=-self.lr / bc1)
             if self.params is not None and self.params.data_ptr() != p.data_ptr():
                 self.params.copy_(p.to(self.params.dtype))
+        if self.after_step is not None:
+            self.after_step()
 
     def zero_grad(self, set_to_none: bool = True) -> None:
         if self.ddp is not None:

@@ -1,0 +1,485 @@
+"""Fully sharded data parallelism (ZeRO-3) with fused NVLink collectives.
+
+Parity: the reference wraps the whole model in torch FSDP with no wrap policy
+(one flat parameter, fp32 parameters, per-rank gradient-norm clipping,
+nuvla_forge/train.py:158-160, 228). This runtime shards per block and fixes the
+clipping:
+
+* Units: every ``TransformerBlock`` and ``DiTBlock`` is a unit; all remaining
+  parameters form the root unit. A unit's parameters are flattened (padded to
+  a multiple of 8*world) and split into ``world`` contiguous shards.
+* Each rank keeps, for its shard of every unit, an fp32 master copy, AdamW
+  moments and an fp32 gradient in ONE flat shard space (so the optimizer is one
+  launch), and the bf16 parameter shard in peer-mapped memory, where the
+  optimizer writes it directly.
+* Forward: before a unit runs, its bf16 parameters are all-gathered into a
+  full buffer the module's parameters are views of (``nfb_allgather``: each
+  rank pulls its peers' shards over NVLink); after it runs, the buffer's
+  storage is released (``reshard_after_forward``). Backward: a hook on the
+  unit's outputs gathers it again before its backward runs.
+* Gradients: bf16 gradients are folded into a per-unit fp32 accumulator
+  (exact across micro-steps); when a unit's gradients are complete on a
+  syncing micro-step they are cast to bf16 into peer-mapped memory and
+  reduce-scattered by ``nfb_rs_f32`` (reduction in fp32, 1/world scale, fp32
+  shard output), in a fixed unit order on every rank. With clipping off, the
+  fused ``nfb_rs_adamw`` applies AdamW to the shard inside the reduce-scatter.
+* The gradient norm for clipping is global: shard norms^2 are summed over ranks
+  on the device (``nfb_allreduce_scalar``) before the update.
+
+``comm="nccl"`` runs the same schedule on NCCL all_gather_into_tensor /
+reduce_scatter_tensor (the baseline); ``comm="gloo"`` is the CPU test path.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import ctypes
+from dataclasses import dataclass, field
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+from .. import _native as nat
+from .symm import SLOT_AG, SLOT_RS, SLOT_SCALAR, SymmetricWorkspace, symmetric_memory_available
+
+
+def _round(n: int, a: int) -> int:
+    return (n + a - 1) // a * a
+
+
+@dataclass
+class _Seg:
+    name: str
+    param: nn.Parameter
+    start: int
+    numel: int
+    shape: torch.Size
+
+
+@dataclass
+class _Unit:
+    index: int
+    name: str
+    module: nn.Module | None
+    segs: list = field(default_factory=list)
+    numel: int = 0
+    shard: int = 0
+    shard_start: int = 0       # offset of this unit's shard in the flat shard space
+    full: torch.Tensor | None = None
+    gathered: bool = False
+    grad_off: int = -1         # peer-mapped bf16 full-gradient region (fused comm)
+    acc32: torch.Tensor | None = None
+    acc_fresh: bool = True
+    pending: int = 0
+    ready: bool = False
+    launched: bool = False
+    bwd_gathered: bool = False
+
+
+class FullyShardedDataParallel(nn.Module):
+    def __init__(self, module: nn.Module, param_dtype: torch.dtype | None = None, comm: str = "auto",
+                 unit_types: tuple | None = None, reshard_after_forward: bool = True, ctas: int = 32,
+                 process_group: dist.ProcessGroup | None = None):
+        super().__init__()
+        self.module = module
+        dev = next(module.parameters()).device
+        self.device = dev
+        self.group = process_group
+        self.world = dist.get_world_size(process_group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(process_group) if dist.is_initialized() else 0
+        self.param_dtype = param_dtype or (torch.bfloat16 if dev.type == "cuda" else torch.float32)
+        if comm == "auto":
+            if dev.type != "cuda":
+                comm = "gloo" if self.world > 1 else "none"
+            else:
+                comm = "fused" if (self.world > 1 and symmetric_memory_available()) else ("nccl" if self.world > 1
+                                                                                          else "none")
+        if comm == "fused" and self.param_dtype != torch.bfloat16:
+            comm = "nccl"
+        self.comm = comm
+        self.reshard_after_forward = reshard_after_forward
+        self.ctas = ctas
+        if unit_types is None:
+            from ..models.dit import DiTBlock
+            from ..models.layers import TransformerBlock
+            unit_types = (TransformerBlock, DiTBlock)
+        self.units = self._build_units(unit_types)
+        self.root = self.units[-1]
+        self.shard_numel = sum(u.shard for u in self.units)
+        self.master = torch.zeros(self.shard_numel, dtype=torch.float32, device=dev)
+        self.grads = torch.zeros(self.shard_numel, dtype=torch.float32, device=dev)
+        self.ws = None
+        self.param_shards = None
+        if comm == "fused":
+            grad_bytes = sum(_round(u.numel * 2, 256) for u in self.units)
+            self.ws = SymmetricWorkspace(_round(self.shard_numel * 2, 256) + grad_bytes + 4096, group=process_group,
+                                         device=dev)
+            self.param_off = self.ws.alloc(self.shard_numel * 2)
+            for u in self.units:
+                u.grad_off = self.ws.alloc(u.numel * 2)
+        else:
+            self.param_shards = torch.zeros(self.shard_numel, dtype=self.param_dtype, device=dev)
+        self.params = self.param_shards
+        self._init_shards()
+        self._order: list[_Unit] = []       # reverse-backward (= forward) order of the current iteration
+        self._rs_order: list[_Unit] = []
+        self._next_rs = 0
+        self.require_sync = True
+        self._shard_fresh = True
+        self._callback_queued = False
+        self.comm_timer = None
+        self._seg_of: dict[int, _Seg] = {}
+        for u in self.units:
+            for s in u.segs:
+                s.param.register_post_accumulate_grad_hook(self._grad_hook)
+                self._unit_of[id(s.param)] = u
+                self._seg_of[id(s.param)] = s
+        for u in self.units[:-1]:
+            self._wrap_unit(u)
+        self.module.register_forward_pre_hook(self._root_pre_forward)
+
+    # ------------------------------------------------------------------ setup
+    def _build_units(self, unit_types) -> list[_Unit]:
+        self._unit_of: dict[int, _Unit] = {}
+        units: list[_Unit] = []
+        claimed: set[int] = set()
+
+        def visit(mod: nn.Module, prefix: str):
+            for name, child in mod.named_children():
+                full = f"{prefix}{name}"
+                if isinstance(child, unit_types):
+                    units.append(self._make_unit(len(units), full, child, f"{full}."))
+                    for p in child.parameters():
+                        claimed.add(id(p))
+                else:
+                    visit(child, f"{full}.")
+
+        visit(self.module, "")
+        root = _Unit(len(units), "<root>", None)
+        named = [(n, p) for n, p in self.module.named_parameters() if p.requires_grad and id(p) not in claimed]
+        self._fill_unit(root, named)
+        units.append(root)
+        off = 0
+        for u in units:
+            u.shard_start = off
+            off += u.shard
+        return units
+
+    def _make_unit(self, idx, name, module, prefix) -> _Unit:
+        u = _Unit(idx, name, module)
+        self._fill_unit(u, [(prefix + n, p) for n, p in module.named_parameters() if p.requires_grad])
+        return u
+
+    def _fill_unit(self, u: _Unit, named) -> None:
+        off = 0
+        for n, p in named:
+            u.segs.append(_Seg(n, p, off, p.numel(), p.shape))
+            off += _round(p.numel(), 8)
+        u.numel = _round(max(off, 8), 8 * self.world)
+        u.shard = u.numel // self.world
+        u.pending = len(u.segs)
+
+    def _init_shards(self) -> None:
+        """Flatten each unit's initial fp32 parameters (rank 0's values), keep this rank's shard."""
+        with torch.no_grad():
+            for u in self.units:
+                flat = torch.zeros(u.numel, dtype=torch.float32, device=self.device)
+                for s in u.segs:
+                    flat[s.start: s.start + s.numel].copy_(s.param.detach().reshape(-1).float())
+                if self.world > 1:
+                    dist.broadcast(flat, src=0, group=self.group)
+                lo = self.rank * u.shard
+                self.master[u.shard_start: u.shard_start + u.shard].copy_(flat[lo: lo + u.shard])
+                u.full = torch.empty(u.numel, dtype=self.param_dtype, device=self.device)
+                for s in u.segs:
+                    s.param.data = u.full[s.start: s.start + s.numel].view(s.shape)
+                u.full.untyped_storage().resize_(0)
+            self._write_param_shards()
+
+    def _write_param_shards(self) -> None:
+        if self.comm == "fused":
+            nat.call("nfb_cast", 0, 1, ctypes.c_void_p(self.ws.local_ptr(self.param_off)), nat.ptr(self.master),
+                     self.shard_numel, 1.0, nat.stream(self.device))
+            torch.cuda.synchronize(self.device)
+        else:
+            self.param_shards.copy_(self.master.to(self.param_dtype))
+
+    # ------------------------------------------------------------ gather / reshard
+    def _gather(self, u: _Unit) -> None:
+        if u.gathered:
+            return
+        st = u.full.untyped_storage()
+        nbytes = u.numel * u.full.element_size()
+        if st.nbytes() != nbytes:
+            st.resize_(nbytes)
+        if self.comm == "fused":
+            ws = self.ws
+            nat.call("nfb_allgather", ws.bases_ptr(), ws.rank, ws.world, u.shard,
+                     self.param_off + u.shard_start * 2, nat.ptr(u.full), ws.flag_off, SLOT_AG,
+                     ws.next_epoch(SLOT_AG), ws.timeout_ns, nat.ptr(ws.status), self.ctas, nat.stream(self.device))
+        elif self.comm == "nccl":
+            dist.all_gather_into_tensor(u.full, self.param_shards[u.shard_start: u.shard_start + u.shard],
+                                        group=self.group)
+        elif self.comm == "gloo":
+            parts = [torch.empty(u.shard, dtype=u.full.dtype, device=u.full.device) for _ in range(self.world)]
+            dist.all_gather(parts, self.param_shards[u.shard_start: u.shard_start + u.shard].contiguous(),
+                            group=self.group)
+            u.full.copy_(torch.cat(parts))
+        else:  # single process
+            u.full.copy_(self.param_shards[u.shard_start: u.shard_start + u.shard])
+        u.gathered = True
+
+    def _reshard(self, u: _Unit) -> None:
+        if not u.gathered or u is self.root:
+            return
+        u.full.untyped_storage().resize_(0)
+        u.gathered = False
+
+    # ------------------------------------------------------------------ hooks
+    def _root_pre_forward(self, module, args):
+        self._order = []
+        self._gather(self.root)
+        return None
+
+    def _wrap_unit(self, u: _Unit) -> None:
+        mod = u.module
+        for meth in ("forward", "forward_chain"):
+            fn = getattr(mod, meth, None)
+            if fn is None:
+                continue
+
+            def wrapped(*a, _fn=fn, _u=u, **kw):
+                self._pre_forward(_u)
+                out = _fn(*a, **kw)
+                self._post_forward(_u, out)
+                return out
+
+            setattr(mod, meth, wrapped)
+
+    def _pre_forward(self, u: _Unit) -> None:
+        self._gather(u)
+        if u not in self._order:
+            self._order.append(u)
+        u.bwd_gathered = False
+
+    def _post_forward(self, u: _Unit, out) -> None:
+        if torch.is_grad_enabled():
+            for t in _tensors(out):
+                if t.requires_grad:
+                    t.register_hook(lambda g, _u=u: self._pre_backward(_u))
+        if self.reshard_after_forward:
+            self._reshard(u)
+
+    def _pre_backward(self, u: _Unit) -> None:
+        if not u.bwd_gathered:
+            u.bwd_gathered = True
+            self._gather(u)
+
+    def _grad_hook(self, p: nn.Parameter) -> None:
+        if not self._callback_queued:
+            self._callback_queued = True
+            self._rs_order = list(reversed(self._order)) + [self.root]
+            self._next_rs = 0
+            torch.autograd.Variable._execution_engine.queue_callback(self._finalize_backward)
+        u = self._unit_of[id(p)]
+        if u.acc32 is None:
+            u.acc32 = torch.zeros(u.numel, dtype=torch.float32, device=self.device)
+        elif u.acc_fresh:
+            u.acc32.zero_()      # new window: parameters without a gradient contribute zeros
+        u.acc_fresh = False
+        seg = self._seg_of[id(p)]
+        u.acc32[seg.start: seg.start + seg.numel].add_(p.grad.reshape(-1))
+        p.grad = None
+        u.pending -= 1
+        if u.pending == 0:
+            u.ready = True
+            if self.require_sync:
+                self._launch_ready()
+
+    def _launch_ready(self) -> None:
+        while self._next_rs < len(self._rs_order) and self._rs_order[self._next_rs].ready:
+            u = self._rs_order[self._next_rs]
+            self._reduce_scatter(u)
+            self._next_rs += 1
+
+    def _reduce_scatter(self, u: _Unit) -> None:
+        u.launched = True
+        if u.acc32 is None:
+            u.acc32 = torch.zeros(u.numel, dtype=torch.float32, device=self.device)
+        elif u.acc_fresh:
+            u.acc32.zero_()      # no gradient reached this unit in the window
+        out = self.grads[u.shard_start: u.shard_start + u.shard]
+        scale = 1.0 / self.world
+        if self.comm == "fused":
+            ws = self.ws
+            nat.call("nfb_cast", 0, 1, ctypes.c_void_p(ws.local_ptr(u.grad_off)), nat.ptr(u.acc32), u.numel, 1.0,
+                     nat.stream(self.device))
+            nat.call("nfb_rs_f32", ws.bases_ptr(), ws.rank, ws.world, u.shard, u.grad_off, ws.flag_off, SLOT_RS,
+                     scale, ws.next_epoch(SLOT_RS), ws.timeout_ns, nat.ptr(ws.status), nat.ptr(out), nat.ptr(None),
+                     nat.ptr(None), nat.ptr(None), 1, int(not self._shard_fresh), self.ctas, nat.stream(self.device))
+        elif self.comm == "nccl":
+            red = torch.empty(u.shard, dtype=torch.bfloat16, device=self.device)
+            dist.reduce_scatter_tensor(red, u.acc32.to(torch.bfloat16), group=self.group)
+            if self._shard_fresh:
+                out.copy_(red.float().mul_(scale))
+            else:
+                out.add_(red.float().mul_(scale))
+        elif self.comm == "gloo":
+            full = u.acc32.clone()
+            dist.all_reduce(full, group=self.group)
+            lo = self.rank * u.shard
+            red = full[lo: lo + u.shard] * scale
+            if self._shard_fresh:
+                out.copy_(red)
+            else:
+                out.add_(red)
+        else:
+            if self._shard_fresh:
+                out.copy_(u.acc32)
+            else:
+                out.add_(u.acc32)
+        u.acc_fresh = True
+        self._reshard(u)
+
+    def _finalize_backward(self) -> None:
+        self._callback_queued = False
+        if self.require_sync:
+            for u in self._rs_order:
+                u.ready = True
+            self._launch_ready()
+            self._shard_fresh = False
+        for u in self.units:
+            u.pending = len(u.segs)
+            u.ready = False
+            u.launched = False
+            self._reshard(u)
+
+    # ------------------------------------------------------------------ API
+    def forward(self, *args, **kwargs):
+        return self.module(*args, **kwargs)
+
+    @contextlib.contextmanager
+    def no_sync(self):
+        prev = self.require_sync
+        self.require_sync = False
+        try:
+            yield
+        finally:
+            self.require_sync = prev
+
+    def zero_grad(self) -> None:
+        self._shard_fresh = True
+        for u in self.units:
+            u.acc_fresh = True
+
+    def _norm_allreduce(self, norm2: torch.Tensor) -> None:
+        if self.world == 1:
+            return
+        if self.comm == "fused":
+            ws = self.ws
+            nat.call("nfb_allreduce_scalar", ws.bases_ptr(), ws.rank, ws.world, ws.scalar_off, nat.ptr(norm2),
+                     ws.flag_off, SLOT_SCALAR, ws.next_epoch(SLOT_SCALAR), ws.timeout_ns, nat.ptr(ws.status),
+                     nat.stream(self.device))
+        else:
+            dist.all_reduce(norm2, group=self.group)
+
+    def _after_step(self) -> None:
+        if self.comm != "fused":
+            self.param_shards.copy_(self.master.to(self.param_dtype))
+        self.root.gathered = False   # the root unit is re-gathered by the next forward
+
+    def make_optimizer(self, lr: float = 3e-4, weight_decay: float = 0.01, max_grad_norm: float = 1.0,
+                       betas=(0.9, 0.999), eps: float = 1e-8):
+        from ..optim.adamw import FlatAdamW
+
+        ptr = self.ws.local_ptr(self.param_off) if self.comm == "fused" else None
+        return FlatAdamW(self, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay, max_grad_norm=max_grad_norm,
+                         ddp=self, grads=self.grads, master=self.master,
+                         params=None if ptr is not None else self.param_shards, params_ptr=ptr,
+                         norm_allreduce=self._norm_allreduce, after_step=self._after_step)
+
+    def check_health(self) -> None:
+        if self.ws is not None:
+            self.ws.check()
+
+    # ------------------------------------------------------------- checkpoints
+    def _full_flat_master(self, u: _Unit) -> torch.Tensor:
+        shard = self.master[u.shard_start: u.shard_start + u.shard].contiguous()
+        if self.world == 1:
+            return shard.clone()
+        if self.comm == "gloo":
+            parts = [torch.empty_like(shard) for _ in range(self.world)]
+            dist.all_gather(parts, shard, group=self.group)
+            return torch.cat(parts)
+        full = torch.empty(u.numel, dtype=torch.float32, device=self.device)
+        dist.all_gather_into_tensor(full, shard, group=self.group)
+        return full
+
+    def full_master_views(self):
+        """{id(param): full fp32 tensor} on rank 0 (collective; other ranks get None)."""
+        views = {}
+        for u in self.units:
+            full = self._full_flat_master(u)
+            if self.rank == 0:
+                for s in u.segs:
+                    views[id(s.param)] = full[s.start: s.start + s.numel].view(s.shape)
+        return views if self.rank == 0 else None
+
+    def load_full_state_dict(self, sd: dict) -> None:
+        """Load a full reference-format state dict (every rank reads the same file)."""
+        from ..checkpoint import _fp32_state_dict  # noqa: F401  (same key mapping)
+
+        tmp = {id(s.param): torch.zeros(s.shape, dtype=torch.float32, device=self.device)
+               for u in self.units for s in u.segs}
+        saved = {}
+        for u in self.units:
+            for s in u.segs:
+                saved[id(s.param)] = s.param.data
+                s.param.data = tmp[id(s.param)]
+        try:
+            self.module.load_state_dict(sd, strict=True)
+        finally:
+            for u in self.units:
+                for s in u.segs:
+                    s.param.data = saved[id(s.param)]
+        with torch.no_grad():
+            for u in self.units:
+                flat = torch.zeros(u.numel, dtype=torch.float32, device=self.device)
+                for s in u.segs:
+                    flat[s.start: s.start + s.numel].copy_(tmp[id(s.param)].reshape(-1))
+                lo = self.rank * u.shard
+                self.master[u.shard_start: u.shard_start + u.shard].copy_(flat[lo: lo + u.shard])
+        self._write_param_shards()
+        self.root.gathered = False
+
+    def gather_optimizer_state(self, opt) -> dict:
+        """Optimizer moments of every rank's shard, collected on rank 0 (same world size to resume)."""
+        m, v = opt.m.contiguous(), opt.v.contiguous()
+        if self.world > 1:
+            ms = [torch.empty_like(m) for _ in range(self.world)]
+            vs = [torch.empty_like(v) for _ in range(self.world)]
+            dist.all_gather(ms, m, group=self.group)
+            dist.all_gather(vs, v, group=self.group)
+        else:
+            ms, vs = [m], [v]
+        return {"step": opt.step_count, "world": self.world, "exp_avg_shards": [t.cpu() for t in ms],
+                "exp_avg_sq_shards": [t.cpu() for t in vs]}
+
+    def load_optimizer_state(self, opt, sd: dict) -> None:
+        if sd.get("world") != self.world:
+            raise ValueError(f"optimizer state was saved with world={sd.get('world')}, running world={self.world}")
+        opt.step_count = int(sd["step"])
+        opt.m.copy_(sd["exp_avg_shards"][self.rank].to(opt.m.device))
+        opt.v.copy_(sd["exp_avg_sq_shards"][self.rank].to(opt.v.device))
+
+
+def _tensors(obj):
+    if isinstance(obj, torch.Tensor):
+        yield obj
+    elif isinstance(obj, (tuple, list)):
+        for o in obj:
+            yield from _tensors(o)
+    elif isinstance(obj, dict):
+        for o in obj.values():
+            yield from _tensors(o)

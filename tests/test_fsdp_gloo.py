@@ -1,0 +1,124 @@
+"""FSDP runtime on CPU gloo ranks (world=2): numerics vs single-process AdamW, no_sync, checkpoints."""
+
+import os
+import tempfile
+
+import torch
+from torch import nn
+
+from _mp import run_ranks
+
+
+class Block(nn.Module):
+    def __init__(self, d):
+        super().__init__()
+        self.a = nn.Linear(d, 2 * d)
+        self.b = nn.Linear(2 * d, d)
+
+    def forward(self, x):
+        return x + self.b(torch.tanh(self.a(x)))
+
+
+class Net(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.inp = nn.Linear(12, 16)
+        self.blocks = nn.ModuleList([Block(16) for _ in range(3)])
+        self.out = nn.Linear(16, 3)
+        self.unused = nn.Linear(3, 3)
+
+    def forward(self, x):
+        h = self.inp(x)
+        for b in self.blocks:
+            h = b(h)
+        return self.out(h)
+
+
+def _data(step, rank, m):
+    g = torch.Generator().manual_seed(97 * step + 13 * rank + m)
+    return torch.randn(6, 12, generator=g), torch.randn(6, 3, generator=g)
+
+
+def _fsdp_train(rank, world, steps, accum, no_sync, clip):
+    from nuvla_forge_b200.parallel.fsdp import FullyShardedDataParallel
+
+    torch.manual_seed(0)
+    net = Net()
+    fsdp = FullyShardedDataParallel(net, unit_types=(Block,))
+    opt = fsdp.make_optimizer(lr=1e-2, weight_decay=0.01, max_grad_norm=clip)
+    for step in range(steps):
+        for m in range(accum):
+            x, y = _data(step, rank, m)
+            ctx = fsdp.no_sync() if (no_sync and m < accum - 1) else torch.enable_grad()
+            with ctx:
+                (((fsdp(x) - y) ** 2).mean() / accum).backward()
+        opt.step()
+        opt.zero_grad()
+    views = fsdp.full_master_views()
+    if rank == 0:
+        return {n: views[id(p)].clone() for n, p in net.named_parameters()}
+    return None
+
+
+def _reference(world, steps, accum, clip):
+    torch.manual_seed(0)
+    net = Net()
+    opt = torch.optim.AdamW(net.parameters(), lr=1e-2, weight_decay=0.01)
+    for step in range(steps):
+        opt.zero_grad()
+        for r in range(world):
+            for m in range(accum):
+                x, y = _data(step, r, m)
+                (((net(x) - y) ** 2).mean() / (accum * world)).backward()
+        for p in net.parameters():
+            if p.grad is None:
+                p.grad = torch.zeros_like(p)
+        if clip > 0:
+            torch.nn.utils.clip_grad_norm_(net.parameters(), clip)
+        opt.step()
+    return {n: p.detach().clone() for n, p in net.named_parameters()}
+
+
+def _check(out, ref):
+    assert all(st == "ok" for st, _ in out.values()), out
+    got = out[0][1]
+    for n, t in ref.items():
+        assert torch.allclose(got[n], t, atol=3e-5), (n, float((got[n] - t).abs().max()))
+
+
+def test_fsdp_matches_single_process_no_sync_with_global_clip():
+    out = run_ranks(_fsdp_train, 2, args=(3, 2, True, 0.5))
+    _check(out, _reference(2, 3, 2, 0.5))
+
+
+def test_fsdp_sync_every_micro_step():
+    out = run_ranks(_fsdp_train, 2, args=(2, 2, False, 1.0))
+    _check(out, _reference(2, 2, 2, 1.0))
+
+
+def _fsdp_ckpt(rank, world, path):
+    from nuvla_forge_b200.checkpoint import load_checkpoint, save_checkpoint
+    from nuvla_forge_b200.parallel.fsdp import FullyShardedDataParallel
+
+    torch.manual_seed(0)
+    fsdp = FullyShardedDataParallel(Net(), unit_types=(Block,))
+    opt = fsdp.make_optimizer(lr=1e-2)
+    x, y = _data(0, rank, 0)
+    ((fsdp(x) - y) ** 2).mean().backward()
+    opt.step()
+    save_checkpoint(path, fsdp, opt, step=1)
+    torch.manual_seed(3)
+    fsdp2 = FullyShardedDataParallel(Net(), unit_types=(Block,))
+    opt2 = fsdp2.make_optimizer(lr=1e-2)
+    step = load_checkpoint(path, fsdp2, opt2)
+    return {"eq": torch.equal(fsdp.master, fsdp2.master) and torch.equal(opt.m, opt2.m), "step": step}
+
+
+def test_fsdp_checkpoint_roundtrip():
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "ck.pt")
+        out = run_ranks(_fsdp_ckpt, 2, args=(path,))
+        assert all(st == "ok" for st, _ in out.values()), out
+        assert out[0][1]["eq"] and out[1][1]["eq"] and out[0][1]["step"] == 1
+        sd = torch.load(path, weights_only=False)["model"]
+        assert set(sd) == set(Net().state_dict())

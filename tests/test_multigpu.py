@@ -126,3 +126,40 @@ def test_peer_exit_detected_on_host_before_next_launch():
     assert out[w - 1] == ("ok", "left"), out
     for r in range(w - 1):
         assert out[r][0] == "ok" and out[r][1].startswith("detected"), out
+
+
+def _fsdp_gpu(rank, world, comm):
+    import sys
+    import os
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from test_fsdp_gloo import Block, Net, _data
+
+    from nuvla_forge_b200.parallel.fsdp import FullyShardedDataParallel
+
+    dev = torch.device("cuda", rank)
+    torch.manual_seed(0)
+    net = Net().to(dev)
+    fsdp = FullyShardedDataParallel(net, param_dtype=torch.bfloat16, comm=comm, unit_types=(Block,))
+    opt = fsdp.make_optimizer(lr=1e-2, max_grad_norm=0.5)
+    for step in range(3):
+        for m in range(2):
+            x, y = _data(step, rank, m)
+            ctx = fsdp.no_sync() if m == 0 else torch.enable_grad()
+            with ctx:
+                (((fsdp(x.to(dev, torch.bfloat16)).float() - y.to(dev)) ** 2).mean() / 2).backward()
+        opt.step()
+        opt.zero_grad()
+    torch.cuda.synchronize(dev)
+    fsdp.check_health()
+    views = fsdp.full_master_views()
+    return {n: views[id(p)].cpu() for n, p in net.named_parameters()} if rank == 0 else None
+
+
+def test_fsdp_fused_matches_nccl():
+    w = _world()
+    a = run_ranks(_fsdp_gpu, w, args=("fused",), backend="nccl", env=ENV)
+    b = run_ranks(_fsdp_gpu, w, args=("nccl",), backend="nccl", env=ENV)
+    assert all(st == "ok" for st, _ in a.values()) and all(st == "ok" for st, _ in b.values()), (a, b)
+    for n, t in b[0][1].items():
+        rel = float((a[0][1][n] - t).norm() / (t.norm() + 1e-8))
+        assert rel < 2e-2, (n, rel)
