@@ -1,0 +1,141 @@
+"""Small, self-contained launches of each native kernel, for profiling one kernel at a time.
+
+    python -m nuvla_forge_b200.bench.profile_cases --case norm_bwd [--iters 3]
+    ncu --set full --clock-control none -k regex:norm_bwd -s 1 -c 1 -o prof \\
+        python -m nuvla_forge_b200.bench.profile_cases --case norm_bwd
+
+Every case keeps its working set above the 126 MB L2 (so DRAM counters mean
+something) and below ~2 GB on the device, and launches its kernel ``--iters``
+times (the first launch is a warm-up to skip with ``-s``).
+"""
+
+from __future__ import annotations
+
+import argparse
+
+import torch
+
+CASES = {}
+
+
+def case(fn):
+    CASES[fn.__name__] = fn
+    return fn
+
+
+def _bf(*s, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return torch.randn(*s, generator=g, device="cuda").to(torch.bfloat16)
+
+
+@case
+def norm_fwd(iters):
+    """adaLN seam forward at BASELINE config 2: x, y [8*2048, 1536] bf16."""
+    from ..ops import fused_adaln_residual_rmsnorm
+    b, t, n = 8, 2048, 1536
+    x, y, cond, w = _bf(b * t, n), _bf(b * t, n, seed=1), _bf(b, 3 * n, seed=2), _bf(n, seed=3)
+    with torch.no_grad():
+        for _ in range(iters):
+            fused_adaln_residual_rmsnorm(x, y, cond[:, :n], w, cond[:, n:2 * n], cond[:, 2 * n:], t)
+
+
+@case
+def norm_bwd(iters):
+    """adaLN seam backward at BASELINE config 2 (one launch incl. per-sample reductions)."""
+    from ..ops import fused_adaln_residual_rmsnorm
+    b, t, n = 8, 2048, 1536
+    leaves = [v.requires_grad_(True) for v in (_bf(b * t, n), _bf(b * t, n, seed=1), _bf(b, n, seed=2),
+                                                _bf(n, seed=3), _bf(b, n, seed=4), _bf(b, n, seed=5))]
+    dh, do = _bf(b * t, n, seed=6), _bf(b * t, n, seed=7)
+    h, o = fused_adaln_residual_rmsnorm(*leaves, tokens_per_sample=t)
+    for _ in range(iters):
+        torch.autograd.backward([h, o], [dh, do], retain_graph=True)
+
+
+@case
+def rmsnorm_bwd(iters):
+    """Plain RMSNorm backward at the ViT shape of the 1b config: [98304, 1024]."""
+    from ..ops import rmsnorm
+    x = _bf(98304, 1024).requires_grad_(True)
+    w = _bf(1024, seed=1).requires_grad_(True)
+    out = rmsnorm(x, w)
+    d = _bf(98304, 1024, seed=2)
+    for _ in range(iters):
+        out.backward(d, retain_graph=True)
+
+
+@case
+def swiglu_fwd(iters):
+    """SwiGLU forward at BASELINE config 2: a, b [16384, 4096]."""
+    from ..ops import fused_swiglu
+    a, b = _bf(16384, 4096), _bf(16384, 4096, seed=1)
+    with torch.no_grad():
+        for _ in range(iters):
+            fused_swiglu(a, b)
+
+
+@case
+def swiglu_bwd(iters):
+    """SwiGLU backward at BASELINE config 2."""
+    from ..ops import fused_swiglu
+    a, b = _bf(16384, 4096).requires_grad_(True), _bf(16384, 4096, seed=1).requires_grad_(True)
+    out = fused_swiglu(a, b)
+    d = _bf(16384, 4096, seed=2)
+    for _ in range(iters):
+        out.backward(d, retain_graph=True)
+
+
+@case
+def tc_gemm(iters):
+    """tcgen05 GEMM core, 8192 x 8192 x 8192 bf16 -> bf16."""
+    from ..ops.ce_tc import tc_gemm as g
+    a, b = _bf(8192, 8192), _bf(8192, 8192, seed=1)
+    for _ in range(iters):
+        g(a, b)
+
+
+@case
+def ce_tc(iters):
+    """Cross entropy on tcgen05 at BASELINE config 2: hidden [16384, 2048], W [32000, 2048]."""
+    from ..ops.ce_tc import cross_entropy_tc
+    h = _bf(16384, 2048).requires_grad_(True)
+    w = (_bf(32000, 2048, seed=1) * 0.02).requires_grad_(True)
+    t = torch.randint(0, 32000, (16384,), device="cuda")
+    for _ in range(iters):
+        cross_entropy_tc(h, w, t).backward()
+
+
+@case
+def adamw(iters):
+    """Flat AdamW over 256M parameters (fp32 master, grads, moments + bf16 copy)."""
+    from .. import _native as nat
+    n = 256 * 2**20
+    p, g, m, v = (torch.randn(n, device="cuda") for _ in range(4))
+    v.abs_()
+    lp = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    for i in range(iters):
+        nat.call("nfb_adamw_flat", nat.ptr(p), nat.ptr(g), nat.ptr(m), nat.ptr(v), nat.ptr(lp), n, 3e-4, 0.9, 0.999,
+                 1e-8, 0.01, i + 1, 1.0, nat.ptr(None), 0.0, nat.stream())
+
+
+@case
+def patchify(iters):
+    """uint8 -> normalised bf16 patch rows for 96 images of 448x448 (one micro-batch of the 1b config)."""
+    from ..ops import patchify_images
+    img = torch.randint(0, 256, (96, 448, 448, 3), dtype=torch.uint8, device="cuda")
+    for _ in range(iters):
+        patchify_images(img, 14)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", required=True, choices=sorted(CASES))
+    ap.add_argument("--iters", type=int, default=3)
+    args = ap.parse_args(argv)
+    CASES[args.case](args.iters)
+    torch.cuda.synchronize()
+    print(f"{args.case}: ok")
+
+
+if __name__ == "__main__":
+    main()

@@ -49,7 +49,11 @@ __global__ void image_normalize_kernel(const uint8_t* __restrict__ in, TO* __res
 template <typename TO>
 __global__ void __launch_bounds__(256) image_patchify_kernel(const uint8_t* __restrict__ in, TO* __restrict__ out,
                                                              int H, int W, int p, int kpad, NormConst k) {
-  extern __shared__ __align__(16) uint8_t strip[];
+  extern __shared__ __align__(16) uint8_t smem[];
+  // [kpad] offsets of each patch-row column inside the strip (or -1 for the zero
+  // padding), computed once per CTA so the hot loop has no divisions; then the strip.
+  int* koff = reinterpret_cast<int*>(smem);
+  uint8_t* strip = smem + ((kpad * 4 + 15) / 16) * 16;
   const int rows_of_patches = H / p;
   const int64_t img = blockIdx.x / rows_of_patches;
   const int py = blockIdx.x % rows_of_patches;
@@ -61,10 +65,21 @@ __global__ void __launch_bounds__(256) image_patchify_kernel(const uint8_t* __re
   } else {
     for (int64_t i = threadIdx.x; i < strip_bytes; i += blockDim.x) strip[i] = src[i];
   }
-  __syncthreads();
-  const int pw = W / p;
   const int K = 3 * p * p;
   const int pp = p * p;
+  for (int kk = threadIdx.x; kk < kpad; kk += blockDim.x) {
+    if (kk < K) {
+      const int c = kk / pp;
+      const int rem = kk - c * pp;
+      const int ky = rem / p;
+      const int kx = rem - ky * p;
+      koff[kk] = ((ky * W + kx) * 3 + c) | (c << 28);
+    } else {
+      koff[kk] = -1;
+    }
+  }
+  __syncthreads();
+  const int pw = W / p;
   TO* dst = out + (img * rows_of_patches + py) * (int64_t)pw * kpad;
   constexpr int PER = 16 / sizeof(TO);
   const int vec_per_patch = kpad / PER;
@@ -74,13 +89,10 @@ __global__ void __launch_bounds__(256) image_patchify_kernel(const uint8_t* __re
     float o[PER];
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
-      const int kk = k0 + j;
-      if (kk < K) {
-        const int c = kk / pp;
-        const int rem = kk - c * pp;
-        const int ky = rem / p;
-        const int kx = rem - ky * p;
-        const float val = (float)strip[(ky * W + px * p + kx) * 3 + c];
+      const int e = koff[k0 + j];
+      if (e >= 0) {
+        const int c = e >> 28;
+        const float val = (float)strip[(e & 0x0FFFFFFF) + px * p * 3];
         o[j] = val * k.scale[c] + k.bias[c];
       } else {
         o[j] = 0.f;
@@ -129,7 +141,7 @@ NFB_API int nfb_image_patchify(int out_dtype, const void* in, void* out, int64_t
   NormConst k = make_const(mean, std);
   cudaStream_t st = (cudaStream_t)stream;
   const int64_t grid = n_img * (H / p);
-  const size_t smem = ((size_t)p * W * 3 + 15) / 16 * 16;
+  const size_t smem = ((size_t)kpad * 4 + 15) / 16 * 16 + ((size_t)p * W * 3 + 15) / 16 * 16;
   if (smem > 200 * 1024) return (int)cudaErrorInvalidValue;
   if (out_dtype == kBF16) {
     if (smem > 48 * 1024) cudaFuncSetAttribute(image_patchify_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -167,11 +167,69 @@ __global__ void __launch_bounds__(512) norm_fwd_kernel(NormFwdArgs a, int K, int
   }
 }
 
+// Warp-per-row forward for N <= 4096: each lane owns NW chunks of 8 columns,
+// the row reduction is a warp shuffle (no shared memory, no named barriers),
+// and all chunk loads of a row are issued before any of them is used.
+template <typename T, int GATE, bool MOD, int NW>
+__global__ void __launch_bounds__(256) norm_fwd_warp_kernel(NormFwdArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t N = a.N;
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < a.M; row += warps) {
+    const int64_t b = row / a.T;
+    float hv[NW][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+      const int64_t col = ((int64_t)i * 32 + lane) * 8;
+      load_chunk<T>(reinterpret_cast<const T*>(a.x) + row * a.sx, col, N, hv[i]);
+      if (GATE != GATE_NONE) {
+        float yv[8];
+        load_chunk<T>(reinterpret_cast<const T*>(a.y) + row * a.sy, col, N, yv);
+        if (GATE == GATE_VEC) {
+          float gv[8];
+          load_chunk<T>(reinterpret_cast<const T*>(a.gate) + b * a.sg, col, N, gv);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) hv[i][j] += gv[j] * yv[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) hv[i][j] += yv[j];
+        }
+        round8<T>(hv[i]);
+        if (col < N) store8<T>(reinterpret_cast<T*>(a.h) + row * a.sh + col, hv[i]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += hv[i][j] * hv[i][j];
+    }
+    ss = warp_sum(ss);
+    const float rstd = rsqrtf(ss / (float)N + a.eps);
+    if (lane == 0) a.rstd[row] = rstd;
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+      const int64_t col = ((int64_t)i * 32 + lane) * 8;
+      if (col >= N) continue;
+      float wv[8], o[8];
+      load_weight_chunk<T>(a.weight, a.w_f32, col, N, wv);
+      if (MOD) {
+        float sc[8], sf[8];
+        load8<T>(reinterpret_cast<const T*>(a.scale) + b * a.ss + col, sc);
+        load8<T>(reinterpret_cast<const T*>(a.shift) + b * a.ssh + col, sf);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = hv[i][j] * rstd * wv[j] * (1.f + sc[j]) + sf[j];
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = hv[i][j] * rstd * wv[j];
+      }
+      store8<T>(reinterpret_cast<T*>(a.out) + row * a.so + col, o);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Backward
 // ---------------------------------------------------------------------------
 template <typename T, int GATE, bool MOD>
-__global__ void __launch_bounds__(512) norm_bwd_kernel(NormBwdArgs a, int K, int R) {
+__global__ void __launch_bounds__(512, (GATE == GATE_VEC || MOD) ? 1 : 2) norm_bwd_kernel(NormBwdArgs a, int K, int R) {
   extern __shared__ float smem[];
   const int tid = threadIdx.x;
   const int team = tid / (K * 32);
@@ -207,39 +265,45 @@ __global__ void __launch_bounds__(512) norm_bwd_kernel(NormBwdArgs a, int K, int
   for (int64_t t = p * R + team; t < a.T; t += a.P * R) {
     const int64_t row = b * a.T + t;
     const float rstd = a.rstd[row];
-    float xhat[CPT], dxh[CPT];
+    const T* dout_r = reinterpret_cast<const T*>(a.dout) + row * a.s_dout;
+    const T* h_r = reinterpret_cast<const T*>(a.h) + row * a.s_h;
+    // pass 1: row dot product and the per-column accumulators
     float dot = 0.f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int64_t col = ((int64_t)i * K * 32 + tt) * 8;
       float dv[8], hv[8];
-      load_chunk<T>(reinterpret_cast<const T*>(a.dout) + row * a.s_dout, col, N, dv);
-      load_chunk<T>(reinterpret_cast<const T*>(a.h) + row * a.s_h, col, N, hv);
+      load_chunk<T>(dout_r, col, N, dv);
+      load_chunk<T>(h_r, col, N, hv);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const float xh = hv[j] * rstd;
-        const float d = dv[j] * ws_s[col + j];
-        xhat[i * 8 + j] = xh;
-        dxh[i * 8 + j] = d;
-        dot += d * xh;
+        const float w = (col < N) ? ws_s[col + j] : 0.f;
+        dot += dv[j] * w * xh;
         accA[i * 8 + j] += dv[j] * xh;
         if (MOD) accD[i * 8 + j] += dv[j];
       }
     }
     dot = team_sum(dot, red, parity, wt, K, bar_id) * invN;
     parity ^= 1;
+    // pass 2: the row is re-read (L1-resident) rather than kept in registers
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int64_t col = ((int64_t)i * K * 32 + tt) * 8;
       if (col >= N) continue;
-      float dh[8];
+      float dv[8], hv[8], dh[8];
+      load8<T>(dout_r + col, dv);
+      load8<T>(h_r + col, hv);
       if (a.dh_up != nullptr) load8<T>(reinterpret_cast<const T*>(a.dh_up) + row * a.s_dhup + col, dh);
       else {
 #pragma unroll
         for (int j = 0; j < 8; ++j) dh[j] = 0.f;
       }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) dh[j] += rstd * (dxh[i * 8 + j] - xhat[i * 8 + j] * dot);
+      for (int j = 0; j < 8; ++j) {
+        const float xh = hv[j] * rstd;
+        dh[j] += rstd * (dv[j] * ws_s[col + j] - xh * dot);
+      }
       store8<T>(reinterpret_cast<T*>(a.dx) + row * a.s_dx + col, dh);
       if (GATE == GATE_VEC) {
         float yv[8], dyv[8];
@@ -251,7 +315,7 @@ __global__ void __launch_bounds__(512) norm_bwd_kernel(NormBwdArgs a, int K, int
         }
         store8<T>(reinterpret_cast<T*>(a.dy) + row * a.s_dy + col, dyv);
       } else if (GATE == GATE_ONE) {
-        store8<T>(reinterpret_cast<T*>(a.dy) + row * a.s_dy + col, dh);
+        if (a.dy != nullptr) store8<T>(reinterpret_cast<T*>(a.dy) + row * a.s_dy + col, dh);
       }
     }
   }
@@ -350,8 +414,25 @@ static int num_sms() {
 
 static inline int team_warps(int64_t N) { return (int)((N + 511) / 512); }
 
+template <typename T, int GATE, bool MOD, int NW>
+static int launch_fwd_warp(const NormFwdArgs& a, cudaStream_t st) {
+  const int64_t want = (a.M + 7) / 8;
+  const int64_t cap = (int64_t)num_sms() * 8;
+  const int grid = (int)(want < cap ? want : cap);
+  norm_fwd_warp_kernel<T, GATE, MOD, NW><<<grid < 1 ? 1 : grid, 256, 0, st>>>(a);
+  return (int)cudaGetLastError();
+}
+
 template <typename T, int GATE, bool MOD>
 static int launch_fwd(const NormFwdArgs& a, cudaStream_t st) {
+  const int64_t nw = (a.N + 255) / 256;
+  if (nw <= 1) return launch_fwd_warp<T, GATE, MOD, 1>(a, st);
+  if (nw <= 2) return launch_fwd_warp<T, GATE, MOD, 2>(a, st);
+  if (nw <= 4) return launch_fwd_warp<T, GATE, MOD, 4>(a, st);
+  if (nw <= 6) return launch_fwd_warp<T, GATE, MOD, 6>(a, st);
+  if (nw <= 8) return launch_fwd_warp<T, GATE, MOD, 8>(a, st);
+  if (nw <= 12) return launch_fwd_warp<T, GATE, MOD, 12>(a, st);
+  if (nw <= 16) return launch_fwd_warp<T, GATE, MOD, 16>(a, st);
   const int K = team_warps(a.N);
   int R = 1;
   while (R * 2 * K * 32 <= 256 && R * 2 <= 8) R *= 2;

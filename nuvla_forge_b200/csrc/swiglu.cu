@@ -19,31 +19,39 @@ struct SwigluArgs {
   int64_t sa, sb, sdo, so, sda, sdb; // row strides (elements)
 };
 
-template <typename T>
+// Element offset of 8-wide chunk i of a row-strided [M, N] view. DENSE views
+// (row stride == N) need no row/column split; strided ones split the chunk
+// index with 32-bit arithmetic (the launcher checks M * N / 8 < 2^31).
+template <bool DENSE>
+__device__ __forceinline__ int64_t chunk_off(uint32_t i, uint32_t cpr, int64_t stride) {
+  if (DENSE) return (int64_t)i * 8;
+  const uint32_t r = i / cpr;
+  return (int64_t)r * stride + (int64_t)(i - r * cpr) * 8;
+}
+
+template <typename T, bool DENSE>
 __global__ void __launch_bounds__(256) swiglu_fwd_kernel(SwigluArgs p) {
-  const int64_t cpr = p.N / 8;  // 8-wide chunks per row
-  const int64_t total = p.M * cpr;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / cpr, c = (i - r * cpr) * 8;
+  const uint32_t cpr = (uint32_t)(p.N / 8);  // 8-wide chunks per row
+  const uint32_t total = (uint32_t)(p.M * cpr);
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
     float av[8], bv[8], o[8];
-    load8_stream<T>(reinterpret_cast<const T*>(p.a) + r * p.sa + c, av);
-    load8_stream<T>(reinterpret_cast<const T*>(p.b) + r * p.sb + c, bv);
+    load8_stream<T>(reinterpret_cast<const T*>(p.a) + chunk_off<DENSE>(i, cpr, p.sa), av);
+    load8_stream<T>(reinterpret_cast<const T*>(p.b) + chunk_off<DENSE>(i, cpr, p.sb), bv);
 #pragma unroll
     for (int j = 0; j < 8; ++j) o[j] = av[j] * sigmoidf_fast(av[j]) * bv[j];
-    store8<T>(reinterpret_cast<T*>(p.out) + r * p.so + c, o);
+    store8<T>(reinterpret_cast<T*>(p.out) + chunk_off<DENSE>(i, cpr, p.so), o);
   }
 }
 
-template <typename T>
+template <typename T, bool DENSE>
 __global__ void __launch_bounds__(256) swiglu_bwd_kernel(SwigluArgs p) {
-  const int64_t cpr = p.N / 8;
-  const int64_t total = p.M * cpr;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / cpr, c = (i - r * cpr) * 8;
+  const uint32_t cpr = (uint32_t)(p.N / 8);
+  const uint32_t total = (uint32_t)(p.M * cpr);
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
     float av[8], bv[8], dv[8], da[8], db[8];
-    load8_stream<T>(reinterpret_cast<const T*>(p.a) + r * p.sa + c, av);
-    load8_stream<T>(reinterpret_cast<const T*>(p.b) + r * p.sb + c, bv);
-    load8_stream<T>(reinterpret_cast<const T*>(p.dout) + r * p.sdo + c, dv);
+    load8_stream<T>(reinterpret_cast<const T*>(p.a) + chunk_off<DENSE>(i, cpr, p.sa), av);
+    load8_stream<T>(reinterpret_cast<const T*>(p.b) + chunk_off<DENSE>(i, cpr, p.sb), bv);
+    load8_stream<T>(reinterpret_cast<const T*>(p.dout) + chunk_off<DENSE>(i, cpr, p.sdo), dv);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float s = sigmoidf_fast(av[j]);
@@ -51,8 +59,8 @@ __global__ void __launch_bounds__(256) swiglu_bwd_kernel(SwigluArgs p) {
       da[j] = dv[j] * bv[j] * s * (1.f + av[j] * (1.f - s));
       db[j] = dv[j] * silu;
     }
-    store8<T>(reinterpret_cast<T*>(p.da) + r * p.sda + c, da);
-    store8<T>(reinterpret_cast<T*>(p.db) + r * p.sdb + c, db);
+    store8<T>(reinterpret_cast<T*>(p.da) + chunk_off<DENSE>(i, cpr, p.sda), da);
+    store8<T>(reinterpret_cast<T*>(p.db) + chunk_off<DENSE>(i, cpr, p.sdb), db);
   }
 }
 
@@ -79,7 +87,7 @@ static int elementwise_grid(int64_t work, int threads) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   int64_t blocks = (work + threads - 1) / threads;
-  int64_t cap = (int64_t)sms * 8;  // grid-stride beyond 8 CTAs of 256 per SM
+  int64_t cap = (int64_t)sms * 16;  // grid-stride beyond 16 waves of 8 CTAs of 256 per SM
   if (blocks > cap) blocks = cap;
   return (int)(blocks < 1 ? 1 : blocks);
 }
@@ -94,11 +102,15 @@ NFB_API int nfb_swiglu_fwd(int dtype, const void* a, const void* b, void* out,
   if (M * N == 0) return 0;
   SwigluArgs p{a, b, nullptr, out, nullptr, nullptr, M, N, sa, sb, 0, so, 0, 0};
   if (N % 8 == 0) {
+    if (M * N / 8 >= (int64_t)1 << 31) return (int)cudaErrorInvalidValue;
     int grid = elementwise_grid(M * N / 8, 256);
-    if (dtype == kF32) swiglu_fwd_kernel<float><<<grid, 256, 0, st>>>(p);
-    else if (dtype == kBF16) swiglu_fwd_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
-    else if (dtype == kF16) swiglu_fwd_kernel<__half><<<grid, 256, 0, st>>>(p);
+    const bool dense = sa == N && sb == N && so == N;
+#define NFB_SWF(T) (dense ? (swiglu_fwd_kernel<T, true><<<grid, 256, 0, st>>>(p), 0) : (swiglu_fwd_kernel<T, false><<<grid, 256, 0, st>>>(p), 0))
+    if (dtype == kF32) NFB_SWF(float);
+    else if (dtype == kBF16) NFB_SWF(__nv_bfloat16);
+    else if (dtype == kF16) NFB_SWF(__half);
     else return (int)cudaErrorInvalidValue;
+#undef NFB_SWF
   } else {
     // scalar path requires dense rows
     if (sa != N || sb != N || so != N) return (int)cudaErrorInvalidValue;
@@ -118,11 +130,15 @@ NFB_API int nfb_swiglu_bwd(int dtype, const void* dout, const void* a, const voi
   if (M * N == 0) return 0;
   SwigluArgs p{a, b, dout, nullptr, da, db, M, N, sa, sb, sdo, 0, sda, sdb};
   if (N % 8 == 0) {
+    if (M * N / 8 >= (int64_t)1 << 31) return (int)cudaErrorInvalidValue;
     int grid = elementwise_grid(M * N / 8, 256);
-    if (dtype == kF32) swiglu_bwd_kernel<float><<<grid, 256, 0, st>>>(p);
-    else if (dtype == kBF16) swiglu_bwd_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
-    else if (dtype == kF16) swiglu_bwd_kernel<__half><<<grid, 256, 0, st>>>(p);
+    const bool dense = sa == N && sb == N && sdo == N && sda == N && sdb == N;
+#define NFB_SWB(T) (dense ? (swiglu_bwd_kernel<T, true><<<grid, 256, 0, st>>>(p), 0) : (swiglu_bwd_kernel<T, false><<<grid, 256, 0, st>>>(p), 0))
+    if (dtype == kF32) NFB_SWB(float);
+    else if (dtype == kBF16) NFB_SWB(__nv_bfloat16);
+    else if (dtype == kF16) NFB_SWB(__half);
     else return (int)cudaErrorInvalidValue;
+#undef NFB_SWB
   } else {
     if (sa != N || sb != N || sdo != N || sda != N || sdb != N) return (int)cudaErrorInvalidValue;
     int grid = elementwise_grid(M * N, 256);

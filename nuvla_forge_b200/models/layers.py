@@ -27,6 +27,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
+from ..ops import add_rmsnorm
 from ..ops import attention as attention_op
 from ..ops import rmsnorm as rmsnorm_op
 from ..ops import swiglu_packed
@@ -185,3 +186,33 @@ class TransformerBlock(nn.Module):
     def forward(self, x):
         x = self.attn(self.norm1(x), residual=x)
         return self.mlp(self.norm2(x), residual=x)
+
+    def forward_chain(self, x, pending=None):
+        """Same block with every residual add folded into the following RMSNorm kernel.
+
+        ``pending`` is the previous block's MLP output not yet added to ``x``.
+        Returns (x, this block's MLP output, not yet added).
+        """
+        ref = not self.norm1.fused
+        if pending is None:
+            h = self.norm1(x)
+        else:
+            x, h = add_rmsnorm(x, pending, self.norm1.weight, self.norm1.eps, force_reference=ref)
+        x, h = add_rmsnorm(x, self.attn(h), self.norm2.weight, self.norm2.eps, force_reference=ref)
+        return x, self.mlp(h)
+
+
+def run_blocks(blocks, x, final_norm: RMSNorm | None = None):
+    """Run a stack of TransformerBlocks with residual adds fused into the norms.
+
+    Returns final_norm(x_out) when ``final_norm`` is given, else x_out.
+    """
+    pending = None
+    for blk in blocks:
+        x, pending = blk.forward_chain(x, pending)
+    if pending is None:
+        return final_norm(x) if final_norm is not None else x
+    if final_norm is None:
+        return x + pending
+    _, out = add_rmsnorm(x, pending, final_norm.weight, final_norm.eps, force_reference=not final_norm.fused)
+    return out

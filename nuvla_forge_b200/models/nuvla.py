@@ -41,7 +41,7 @@ from ..ops import chunked_cross_entropy, patchify_images
 from ..ops import attention as attention_op
 from ..ops.image import patch_kpad
 from .dit import TrajectoryDiT
-from .layers import RMSNorm, TransformerBlock, _linear
+from .layers import RMSNorm, TransformerBlock, _linear, run_blocks
 
 
 @dataclass
@@ -186,9 +186,7 @@ class MultiViewEncoder(nn.Module):
         x, b, ni = self.embed_patches(images)
         x = x + self.pos
         x = x + self.image_embed().repeat(b, 1).unsqueeze(1)
-        for blk in self.blocks:
-            x = blk(x)
-        x = self.norm(x)
+        x = run_blocks(self.blocks, x, self.norm)
         return x.reshape(b, ni * x.shape[1], x.shape[2])
 
 
@@ -263,8 +261,7 @@ class NuVLA(nn.Module):
     def encode_scene(self, images):
         x = self.encoder(images)
         b = x.shape[0]
-        for blk in self.fusion:
-            x = blk(x)
+        x = run_blocks(self.fusion, x)
         if self.cfg.n_scene_queries > 0:
             return self.scene_attn(self.scene_queries.expand(b, -1, -1), x)
         return x
@@ -294,9 +291,7 @@ class NuVLA(nn.Module):
                 h = torch.cat([img, txt.to(img.dtype)], dim=1)
             else:
                 h = img
-            for blk in self.text_blocks:
-                h = blk(h)
-            h = self.text_norm(h)
+            h = run_blocks(self.text_blocks, h, self.text_norm)
             context = h
             text_h = h[:, n_img:]
         else:
@@ -306,8 +301,7 @@ class NuVLA(nn.Module):
             if text_tokens is not None:
                 t = self.text_embed(text_tokens)
                 h = torch.cat([scene, t.to(scene.dtype)], dim=1)
-                for blk in self.text_blocks:
-                    h = blk(h)
+                h = run_blocks(self.text_blocks, h)
                 text_h = h[:, scene.shape[1]:]
         if trajectory is not None:
             plan = self.dit.flow_loss(trajectory, context)

@@ -100,7 +100,8 @@ def _bwd(ctx, dh_up, dout):
     dwb = torch.empty(B * N, dtype=torch.float32, device=dev)
     tickets = ticket_buffer(dev, B + 1)
     dx = torch.empty((M, N), dtype=hs.dtype, device=dev)
-    dy = torch.empty((M, N), dtype=hs.dtype, device=dev) if gate_mode != GATE_NONE else None
+    # with a gate of one, dy == dx: the kernel writes it once and both inputs share the tensor
+    dy = torch.empty((M, N), dtype=hs.dtype, device=dev) if gate_mode == GATE_VEC else None
     dgate = torch.empty((B, N), dtype=hs.dtype, device=dev) if gate_mode == GATE_VEC else None
     dscale = torch.empty((B, N), dtype=hs.dtype, device=dev) if mod else None
     dshift = torch.empty((B, N), dtype=hs.dtype, device=dev) if mod else None
@@ -153,6 +154,8 @@ class _ResNormFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dh, dout):
         dx, dy, dgate, dweight, dscale, dshift = _bwd(ctx, dh, dout)
+        if ctx.gate_mode == GATE_ONE:
+            dy = dx
         return dx, dy, dgate, dweight.to(ctx.wdtype), dscale, dshift, None, None
 
 
