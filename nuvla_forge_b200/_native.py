@@ -47,6 +47,8 @@ _SIGS: dict[str, tuple] = {
     "nfb_cast": (I, [I, I, P, P, L, F, P]),
     "nfb_comm_flag_bytes": (I, []),
     "nfb_ar_twoshot": (I, [P, I, I, P, P, L, L, L, L, I, F, U32, U64, P, I, P]),
+    "nfb_ar_oneshot": (I, [P, I, I, P, P, L, L, L, L, I, F, U32, U64, P, I, P]),
+    "nfb_rs_push": (I, [P, I, I, P, L, L, L, I, F, U32, U64, P, P, I, I, P]),
     "nfb_rs_f32": (I, [P, I, I, L, L, L, I, F, U32, U64, P, P, P, P, P, I, I, I, P]),
     "nfb_rs_adamw": (I, [P, I, I, L, L, L, I, F, U32, U64, P, P, P, P, L, F, F, F, F, F, L, F, I, I, P]),
     "nfb_allgather": (I, [P, I, I, L, L, P, L, I, U32, U64, P, I, P]),

@@ -18,10 +18,12 @@
 //
 // What is fused, per reference collective site (nuvla_forge/train.py:157-167):
 // * nfb_ar_twoshot: DDP bucket all-reduce. fp32 local gradient -> bf16 cast
-//   (phase 1, local) -> each rank reduces its 1/world slice reading all peers
-//   (phase 2) and pushes the scaled bf16 result into every peer's receive
-//   buffer -> fp32 unpack into the gradient buffer (phase 3). 2(N-1)/N of the
-//   bf16 bucket crosses NVLink per rank, like a ring, but in 2 hops.
+//   pushed into each slice owner's inbox (phase 1) -> each owner reduces its
+//   1/world slice locally and pushes the scaled bf16 result into every rank's
+//   outbox (phase 2) -> fp32 unpack into the gradient buffer (phase 3).
+//   2(N-1)/N of the bf16 bucket crosses NVLink per rank, all as posted writes.
+// * nfb_ar_oneshot: small buckets, one barrier (double-buffered inboxes).
+// * nfb_rs_push: FSDP reduce-scatter straight from the fp32 gradient (cast fused).
 // * nfb_rs_f32: FSDP reduce-scatter of bf16 gradients into an fp32 shard,
 //   fused with the 1/world scale and the shard's sum of squares (for the
 //   global gradient-norm clip).
@@ -94,66 +96,172 @@ struct ArArgs {
   uint32_t* status;
 };
 
+constexpr int kU = 4;  // 16-byte vectors per thread per iteration (memory-level parallelism)
+
+__device__ __forceinline__ void load_f32x8(const float* p, float* f) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+  float4 x0 = __ldcs(q), x1 = __ldcs(q + 1);
+  f[0] = x0.x; f[1] = x0.y; f[2] = x0.z; f[3] = x0.w; f[4] = x1.x; f[5] = x1.y; f[6] = x1.z; f[7] = x1.w;
+}
+
+__device__ __forceinline__ void store_f32x8(float* p, const float* f, bool accumulate) {
+  float4* q = reinterpret_cast<float4*>(p);
+  if (accumulate) {
+    float4 o0 = q[0], o1 = q[1];
+    q[0] = make_float4(o0.x + f[0], o0.y + f[1], o0.z + f[2], o0.w + f[3]);
+    q[1] = make_float4(o1.x + f[4], o1.y + f[5], o1.z + f[6], o1.w + f[7]);
+  } else {
+    q[0] = make_float4(f[0], f[1], f[2], f[3]);
+    q[1] = make_float4(f[4], f[5], f[6], f[7]);
+  }
+}
+
+// Push phase shared by the two-shot all-reduce and the reduce-scatter: CTA b
+// casts its chunk of every destination slice to bf16 and writes it straight
+// into the owner's inbox [rank][v] with (posted) NVLink stores.
+__device__ __forceinline__ void push_slices(const ArArgs& a, int64_t slice_vecs, int64_t v0, int64_t v1) {
+  for (int s = 0; s < a.world; ++s) {
+    uint4* inbox = reinterpret_cast<uint4*>(a.peers.base[s] + a.send_off) + (int64_t)a.rank * slice_vecs;
+    const float* src = a.src + (int64_t)s * slice_vecs * 8;
+    for (int64_t v = v0 + threadIdx.x; v < v1; v += (int64_t)blockDim.x * kU) {
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t w = v + (int64_t)u * blockDim.x;
+        if (w < v1) {
+          float f[8];
+          load_f32x8(src + w * 8, f);
+          uint4 o;
+          f32x8_to_bf16(f, o);
+          inbox[w] = o;
+        }
+      }
+    }
+  }
+}
+
+// Reduce this rank's slice from its local inbox: out[j] = scale * sum_q inbox[q][v].
+__device__ __forceinline__ void reduce_inbox(const ArArgs& a, int64_t slice_vecs, int64_t w, float* acc) {
+  const uint4* inbox = reinterpret_cast<const uint4*>(a.peers.base[a.rank] + a.send_off);
+  uint4 in[kMaxWorld];
+#pragma unroll
+  for (int q = 0; q < kMaxWorld; ++q)
+    if (q < a.world) in[q] = __ldcg(inbox + (int64_t)q * slice_vecs + w);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll
+  for (int q = 0; q < kMaxWorld; ++q)
+    if (q < a.world) bf16x8_add(in[q], acc);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] *= a.scale;
+}
+
+// Two-shot all-reduce by pushes: (1) push bf16 slices to their owners' inboxes,
+// (2) each owner reduces its slice locally and pushes the bf16 result into
+// every rank's outbox, (3) every rank unpacks its outbox into fp32. All NVLink
+// traffic is writes: 2(N-1)/N of the bf16 buffer per rank.
 __global__ void __launch_bounds__(512) ar_twoshot_kernel(ArArgs a) {
   const int64_t slice_vecs = a.n / 8 / a.world;
   const int64_t per_cta = (slice_vecs + gridDim.x - 1) / gridDim.x;
   const int64_t v0 = (int64_t)blockIdx.x * per_cta;
   const int64_t v1 = v0 + per_cta < slice_vecs ? v0 + per_cta : slice_vecs;
-  uint4* my_send = reinterpret_cast<uint4*>(a.peers.base[a.rank] + a.send_off);
-  const uint4* my_recv = reinterpret_cast<const uint4*>(a.peers.base[a.rank] + a.recv_off);
 
-  // Phase 1: fp32 -> bf16 into my send buffer (my CTA's part of every slice).
-  for (int s = 0; s < a.world; ++s) {
-    for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
-      const int64_t idx = s * slice_vecs + v;
-      float f[8];
-      const float4* p = reinterpret_cast<const float4*>(a.src + idx * 8);
-      float4 x0 = __ldcs(p), x1 = __ldcs(p + 1);
-      f[0] = x0.x; f[1] = x0.y; f[2] = x0.z; f[3] = x0.w; f[4] = x1.x; f[5] = x1.y; f[6] = x1.z; f[7] = x1.w;
-      uint4 u;
-      f32x8_to_bf16(f, u);
-      my_send[idx] = u;
-    }
-  }
+  push_slices(a, slice_vecs, v0, v1);
   if (!cta_barrier(a.peers, a.rank, a.world, a.flag_off, a.slot, 2u * a.epoch + 1u, a.timeout_ns, a.status, 1)) return;
 
-  // Phase 2: reduce my slice across all ranks, push to every rank's recv.
-  const int64_t base = (int64_t)a.rank * slice_vecs;
+  for (int64_t v = v0 + threadIdx.x; v < v1; v += (int64_t)blockDim.x * kU) {
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t w = v + (int64_t)u * blockDim.x;
+      if (w < v1) {
+        float acc[8];
+        reduce_inbox(a, slice_vecs, w, acc);
+        uint4 o;
+        f32x8_to_bf16(acc, o);
+#pragma unroll
+        for (int q = 0; q < kMaxWorld; ++q)
+          if (q < a.world)
+            reinterpret_cast<uint4*>(a.peers.base[q] + a.recv_off)[(int64_t)a.rank * slice_vecs + w] = o;
+      }
+    }
+  }
+  if (!cta_barrier(a.peers, a.rank, a.world, a.flag_off, a.slot, 2u * a.epoch + 2u, a.timeout_ns, a.status, 2)) return;
+
+  const uint4* outbox = reinterpret_cast<const uint4*>(a.peers.base[a.rank] + a.recv_off);
+  for (int s = 0; s < a.world; ++s) {
+    for (int64_t v = v0 + threadIdx.x; v < v1; v += (int64_t)blockDim.x * kU) {
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t w = v + (int64_t)u * blockDim.x;
+        if (w < v1) {
+          const int64_t idx = (int64_t)s * slice_vecs + w;
+          float f[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) f[j] = 0.f;
+          bf16x8_add(__ldcg(outbox + idx), f);
+          store_f32x8(a.dst + idx * 8, f, false);
+        }
+      }
+    }
+  }
+}
+
+// One-shot all-reduce for small buffers (latency-bound): every rank pushes its
+// whole bf16 buffer into every peer's inbox [parity][rank], one barrier, then
+// each rank sums the inboxes locally. Inboxes alternate by epoch parity, so a
+// launch never overwrites an inbox a peer may still be reading.
+__global__ void __launch_bounds__(512) ar_oneshot_kernel(ArArgs a, int64_t cap_vecs) {
+  const int64_t nvec = a.n / 8;
+  const int64_t per_cta = (nvec + gridDim.x - 1) / gridDim.x;
+  const int64_t v0 = (int64_t)blockIdx.x * per_cta;
+  const int64_t v1 = v0 + per_cta < nvec ? v0 + per_cta : nvec;
+  const int64_t par = (int64_t)(a.epoch & 1u) * a.world * cap_vecs;
   for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
-    uint4 in[kMaxWorld];
+    float f[8];
+    load_f32x8(a.src + v * 8, f);
+    uint4 o;
+    f32x8_to_bf16(f, o);
 #pragma unroll
     for (int q = 0; q < kMaxWorld; ++q)
-      if (q < a.world) in[q] = __ldcg(reinterpret_cast<const uint4*>(a.peers.base[q] + a.send_off) + base + v);
+      if (q < a.world) reinterpret_cast<uint4*>(a.peers.base[q] + a.send_off)[par + (int64_t)a.rank * cap_vecs + v] = o;
+  }
+  if (!cta_barrier(a.peers, a.rank, a.world, a.flag_off, a.slot, a.epoch, a.timeout_ns, a.status, 10)) return;
+  const uint4* inbox = reinterpret_cast<const uint4*>(a.peers.base[a.rank] + a.send_off) + par;
+  for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
     float acc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.f;
 #pragma unroll
     for (int q = 0; q < kMaxWorld; ++q)
-      if (q < a.world) bf16x8_add(in[q], acc);
+      if (q < a.world) bf16x8_add(__ldcg(inbox + (int64_t)q * cap_vecs + v), acc);
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] *= a.scale;
-    uint4 out;
-    f32x8_to_bf16(acc, out);
-#pragma unroll
-    for (int q = 0; q < kMaxWorld; ++q)
-      if (q < a.world) reinterpret_cast<uint4*>(a.peers.base[q] + a.recv_off)[base + v] = out;
+    store_f32x8(a.dst + v * 8, acc, false);
   }
-  if (!cta_barrier(a.peers, a.rank, a.world, a.flag_off, a.slot, 2u * a.epoch + 2u, a.timeout_ns, a.status, 2)) return;
+}
 
-  // Phase 3: unpack every slice's reduced bf16 into fp32 gradients.
-  for (int s = 0; s < a.world; ++s) {
-    for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
-      const int64_t idx = s * slice_vecs + v;
-      uint4 u = __ldcg(my_recv + idx);
-      float f[8];
+// Reduce-scatter by pushes, taking the local fp32 gradient directly (the bf16
+// cast is fused): push slices, one barrier, reduce the local inbox into the
+// fp32 shard (overwrite or accumulate), a trailing barrier so the inbox may be
+// reused by the next launch.
+__global__ void __launch_bounds__(512) rs_push_kernel(ArArgs a, int accumulate) {
+  const int64_t slice_vecs = a.n / 8 / a.world;
+  const int64_t per_cta = (slice_vecs + gridDim.x - 1) / gridDim.x;
+  const int64_t v0 = (int64_t)blockIdx.x * per_cta;
+  const int64_t v1 = v0 + per_cta < slice_vecs ? v0 + per_cta : slice_vecs;
+  push_slices(a, slice_vecs, v0, v1);
+  if (!cta_barrier(a.peers, a.rank, a.world, a.flag_off, a.slot, 2u * a.epoch + 1u, a.timeout_ns, a.status, 11)) return;
+  for (int64_t v = v0 + threadIdx.x; v < v1; v += (int64_t)blockDim.x * kU) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) f[j] = 0.f;
-      bf16x8_add(u, f);
-      float4* d = reinterpret_cast<float4*>(a.dst + idx * 8);
-      d[0] = make_float4(f[0], f[1], f[2], f[3]);
-      d[1] = make_float4(f[4], f[5], f[6], f[7]);
+    for (int u = 0; u < kU; ++u) {
+      const int64_t w = v + (int64_t)u * blockDim.x;
+      if (w < v1) {
+        float acc[8];
+        reduce_inbox(a, slice_vecs, w, acc);
+        store_f32x8(a.dst + w * 8, acc, accumulate != 0);
+      }
     }
   }
+  cta_barrier(a.peers, a.rank, a.world, a.flag_off, a.slot, 2u * a.epoch + 2u, a.timeout_ns, a.status, 12);
 }
 
 // ---------------------------------------------------------------------------
@@ -362,6 +470,41 @@ NFB_API int nfb_ar_twoshot(const uint64_t* bases, int rank, int world, const flo
   a.rank = rank; a.world = world; a.slot = slot; a.scale = scale; a.epoch = epoch; a.timeout_ns = timeout_ns;
   a.status = status;
   ar_twoshot_kernel<<<ctas, 512, 0, (cudaStream_t)stream>>>(a);
+  return (int)cudaGetLastError();
+}
+
+// Small-buffer all-reduce; box_off: region of 2 * world * cap_elems bf16 on every rank.
+NFB_API int nfb_ar_oneshot(const uint64_t* bases, int rank, int world, const float* src, float* dst, int64_t n,
+                           int64_t box_off, int64_t cap_elems, int64_t flag_off, int slot, float scale,
+                           uint32_t epoch, uint64_t timeout_ns, uint32_t* status, int ctas, void* stream) {
+  if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || slot < 0 || slot >= kSlots) return (int)cudaErrorInvalidValue;
+  if (n % 8 || n > cap_elems || cap_elems % 8 || ctas < 1 || ctas > kMaxCtas) return (int)cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) return (int)cudaErrorInvalidValue;
+  if (n == 0) return 0;
+  ArArgs a;
+  a.peers = make_peers(bases, world);
+  a.src = src; a.dst = dst; a.n = n; a.send_off = box_off; a.recv_off = 0; a.flag_off = flag_off;
+  a.rank = rank; a.world = world; a.slot = slot; a.scale = scale; a.epoch = epoch; a.timeout_ns = timeout_ns;
+  a.status = status;
+  ar_oneshot_kernel<<<ctas, 512, 0, (cudaStream_t)stream>>>(a, cap_elems / 8);
+  return (int)cudaGetLastError();
+}
+
+// Reduce-scatter of a local fp32 [n] buffer (bf16 on the wire) into this rank's fp32 shard [n / world];
+// inbox_off: region of n bf16 on every rank.
+NFB_API int nfb_rs_push(const uint64_t* bases, int rank, int world, const float* src, int64_t n, int64_t inbox_off,
+                        int64_t flag_off, int slot, float scale, uint32_t epoch, uint64_t timeout_ns, uint32_t* status,
+                        float* out, int accumulate, int ctas, void* stream) {
+  if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || slot < 0 || slot >= kSlots) return (int)cudaErrorInvalidValue;
+  if (n % (8 * world) || ctas < 1 || ctas > kMaxCtas) return (int)cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(out)) & 15) return (int)cudaErrorInvalidValue;
+  if (n == 0) return 0;
+  ArArgs a;
+  a.peers = make_peers(bases, world);
+  a.src = src; a.dst = out; a.n = n; a.send_off = inbox_off; a.recv_off = 0; a.flag_off = flag_off;
+  a.rank = rank; a.world = world; a.slot = slot; a.scale = scale; a.epoch = epoch; a.timeout_ns = timeout_ns;
+  a.status = status;
+  rs_push_kernel<<<ctas, 512, 0, (cudaStream_t)stream>>>(a, accumulate);
   return (int)cudaGetLastError();
 }
 

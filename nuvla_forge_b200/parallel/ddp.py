@@ -33,7 +33,9 @@ from torch import nn
 
 from .. import _native as nat
 from .flat import FlatParamSpace
-from .symm import SLOT_DDP, SymmetricWorkspace, symmetric_memory_available
+from .symm import SLOT_DDP, SLOT_DDP_SMALL, SymmetricWorkspace, symmetric_memory_available
+
+ONESHOT_MAX_ELEMS = 256 * 1024   # buckets up to 512 KB of bf16 use the one-barrier all-reduce
 
 
 @dataclass
@@ -60,7 +62,7 @@ def _accumulate(dst: torch.Tensor, src: torch.Tensor, overwrite: bool) -> None:
 class DistributedDataParallel(nn.Module):
     def __init__(self, module: nn.Module, bucket_cap_mb: float = 25.0, comm: str = "auto",
                  process_group: dist.ProcessGroup | None = None, param_dtype: torch.dtype | None = None,
-                 ctas: int = 32, broadcast: bool = True):
+                 ctas: int = 48, broadcast: bool = True):
         super().__init__()
         self.module = module
         dev = next(module.parameters()).device
@@ -99,9 +101,12 @@ class DistributedDataParallel(nn.Module):
         if comm == "fused":
             maxb = max(b.end - b.start for b in self.buckets)
             region = (maxb * 2 + 255) // 256 * 256
-            self.ws = SymmetricWorkspace(2 * region, group=process_group, device=dev)
+            self.small_cap = ONESHOT_MAX_ELEMS
+            box = 2 * self.world * self.small_cap * 2
+            self.ws = SymmetricWorkspace(2 * region + box + 256, group=process_group, device=dev)
             self.send_off = self.ws.alloc(maxb * 2)
             self.recv_off = self.ws.alloc(maxb * 2)
+            self.box_off = self.ws.alloc(box)
         # timing of the collective stream (exposed-communication accounting)
         self.comm_events: list[tuple[torch.cuda.Event, torch.cuda.Event]] = []
         self.record_comm_events = False
@@ -183,9 +188,15 @@ class DistributedDataParallel(nn.Module):
         scale = 1.0 / self.world
         if self.comm == "fused":
             ws = self.ws
-            nat.call("nfb_ar_twoshot", ws.bases_ptr(), ws.rank, ws.world, nat.ptr(g), nat.ptr(g), g.numel(),
-                     self.send_off, self.recv_off, ws.flag_off, SLOT_DDP, scale, ws.next_epoch(SLOT_DDP),
-                     ws.timeout_ns, nat.ptr(ws.status), self.ctas, nat.stream(self.device))
+            if g.numel() <= self.small_cap:   # latency-bound: one barrier
+                nat.call("nfb_ar_oneshot", ws.bases_ptr(), ws.rank, ws.world, nat.ptr(g), nat.ptr(g), g.numel(),
+                         self.box_off, self.small_cap, ws.flag_off, SLOT_DDP_SMALL, scale,
+                         ws.next_epoch(SLOT_DDP_SMALL), ws.timeout_ns, nat.ptr(ws.status), 8,
+                         nat.stream(self.device))
+            else:
+                nat.call("nfb_ar_twoshot", ws.bases_ptr(), ws.rank, ws.world, nat.ptr(g), nat.ptr(g), g.numel(),
+                         self.send_off, self.recv_off, ws.flag_off, SLOT_DDP, scale, ws.next_epoch(SLOT_DDP),
+                         ws.timeout_ns, nat.ptr(ws.status), self.ctas, nat.stream(self.device))
         elif self.comm == "nccl":
             t = g.to(torch.bfloat16)
             dist.all_reduce(t, group=self.group)

@@ -20,8 +20,9 @@ clipping:
 * Gradients: bf16 gradients are folded into a per-unit fp32 accumulator
   (exact across micro-steps); when a unit's gradients are complete on a
   syncing micro-step they are cast to bf16 into peer-mapped memory and
-  reduce-scattered by ``nfb_rs_f32`` (reduction in fp32, 1/world scale, fp32
-  shard output), in a fixed unit order on every rank. With clipping off, the
+  reduce-scattered by ``nfb_rs_push`` (one kernel: bf16 cast of the fp32
+  accumulator pushed to each slice's owner over NVLink, reduction in fp32,
+  1/world scale, fp32 shard output), in a fixed unit order on every rank. With clipping off, the
   fused ``nfb_rs_adamw`` applies AdamW to the shard inside the reduce-scatter.
 * The gradient norm for clipping is global: shard norms^2 are summed over ranks
   on the device (``nfb_allreduce_scalar``) before the update.
@@ -313,11 +314,10 @@ class FullyShardedDataParallel(nn.Module):
         scale = 1.0 / self.world
         if self.comm == "fused":
             ws = self.ws
-            nat.call("nfb_cast", 0, 1, ctypes.c_void_p(ws.local_ptr(u.grad_off)), nat.ptr(u.acc32), u.numel, 1.0,
-                     nat.stream(self.device))
-            nat.call("nfb_rs_f32", ws.bases_ptr(), ws.rank, ws.world, u.shard, u.grad_off, ws.flag_off, SLOT_RS,
-                     scale, ws.next_epoch(SLOT_RS), ws.timeout_ns, nat.ptr(ws.status), nat.ptr(out), nat.ptr(None),
-                     nat.ptr(None), nat.ptr(None), 1, int(not self._shard_fresh), self.ctas, nat.stream(self.device))
+            # one kernel: bf16 cast of the fp32 accumulator, pushed to the slice owners, reduced into the shard
+            nat.call("nfb_rs_push", ws.bases_ptr(), ws.rank, ws.world, nat.ptr(u.acc32), u.numel, u.grad_off,
+                     ws.flag_off, SLOT_RS, scale, ws.next_epoch(SLOT_RS), ws.timeout_ns, nat.ptr(ws.status),
+                     nat.ptr(out), int(not self._shard_fresh), self.ctas, nat.stream(self.device))
         elif self.comm == "nccl":
             red = torch.empty(u.shard, dtype=torch.bfloat16, device=self.device)
             dist.reduce_scatter_tensor(red, u.acc32.to(torch.bfloat16), group=self.group)
