@@ -1,0 +1,47 @@
+"""BASELINE config 1 plumbing: the tiny nuVLA config trained through the public Trainer / CLI on CPU."""
+
+import json
+import os
+
+import torch
+
+from _mp import run_ranks
+
+
+def _config1(rank, world):
+    from nuvla_forge_b200.data import SampleSpec, SyntheticBatchSource
+    from nuvla_forge_b200.models import NuVLAConfig
+    from nuvla_forge_b200.parallel.dist import DistInfo
+    from nuvla_forge_b200.train import Trainer
+
+    cfg = NuVLAConfig.preset("tiny", fused=False)
+    info = DistInfo(rank, world, rank, torch.device("cpu"), "gloo")
+    tr = Trainer(cfg, info, grad_accum=2, no_sync_accum=True, bf16=False, seed=0)
+    src = SyntheticBatchSource(SampleSpec.for_model(cfg), 2, seed=0, rank=rank, world=world, pin=False)
+    losses = [float(tr.step([src.batch(2 * s), src.batch(2 * s + 1)])) for s in range(2)]
+    return {"losses": losses, "master": tr.model.space.master[:4096].clone(), "params": tr.num_parameters()}
+
+
+def test_config1_gloo_world2_replicas_agree():
+    out = run_ranks(_config1, 2, timeout_s=120, join_s=600)
+    assert all(st == "ok" for st, _ in out.values()), out
+    a, b = out[0][1], out[1][1]
+    assert torch.equal(a["master"], b["master"])
+    assert all(l == l and l > 0 for l in a["losses"] + b["losses"])
+    assert 20e6 < a["params"] < 40e6
+
+
+def test_train_cli_writes_report(tmp_path):
+    from nuvla_forge_b200.train import main
+
+    stats = main(["--model-config", "tiny", "--steps", "1", "--warmup-steps", "0", "--batch-size", "1",
+                  "--num-workers", "0", "--out", str(tmp_path), "--tag", "cpu", "--save-every", "1",
+                  "--ckpt-dir", str(tmp_path / "ck")])
+    rep = json.loads((tmp_path / "train-cpu.json").read_text())
+    for k in ("step_ms", "n_steps", "samples_per_sec", "world_size", "global_batch", "flags", "model",
+              "exposed_comm_ms"):
+        assert k in rep, k
+    assert stats["n_steps"] == 1 and rep["world_size"] == 1
+    ck = torch.load(tmp_path / "ck" / "step-0000001.pt", weights_only=False)
+    assert ck["step"] == 1 and "encoder.patch.weight" in ck["model"]
+    assert os.path.getsize(tmp_path / "ck" / "step-0000001.pt") > 1e6
