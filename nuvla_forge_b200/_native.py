@@ -34,6 +34,9 @@ _SIGS: dict[str, tuple] = {
     "nfb_num_sms": (I, []),
     "nfb_norm_fwd": (I, [I, I, I, P, P, P, P, P, P, P, P, P, L, L, L, L, L, L, L, L, L, L, F, I, P]),
     "nfb_norm_bwd_P": (L, [L, L, L]),
+    "nfb_norm_set_status": (None, [P]),
+    "nfb_norm_set_impl": (None, [I]),
+    "nfb_norm_get_impl": (I, []),
     "nfb_norm_bwd": (I, [I, I, I, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P,
                          L, L, L, L, L, L, L, L, L, L, L, L, I, P]),
     "nfb_swiglu_fwd": (I, [I, P, P, P, L, L, L, L, L, P]),

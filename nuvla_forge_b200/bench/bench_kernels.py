@@ -90,7 +90,13 @@ def bench_adaln(b, t, n, dtype, peaks, ref):
 
     res = {"shape": f"B{b}xT{t}xN{n}", "dtype": str(dtype).split(".")[-1]}
     res["eager_ms"] = timeit(run(adaln_residual_rmsnorm_ref))
-    res["native_ms"] = timeit(run(fused_adaln_residual_rmsnorm))
+    from ..ops import norm as _norm
+    default = _norm.get_impl()
+    for impl, key in ((1, "native_pipelined_ms"), (0, "native_warp_team_ms")):
+        _norm.set_impl(impl)
+        res[key] = timeit(run(fused_adaln_residual_rmsnorm))
+    _norm.set_impl(default)
+    res["native_ms"] = res["native_pipelined_ms"] if default == 1 else res["native_warp_team_ms"]
     if ref is not None:
         res["reference_triton_ms"] = timeit(run(ref.fused_adaln_residual_rmsnorm))
     moved = 10 * b * t * n * torch.finfo(dtype).bits // 8
@@ -182,7 +188,8 @@ def main(argv=None):
         r = bench_adaln(*s, dt, peaks, ref)
         report["adaln"].append(r)
         print(f"adaLN  {r['shape']:<20} eager {r['eager_ms']:7.3f} | ref-triton {r.get('reference_triton_ms', float('nan')):7.3f}"
-              f" | native {r['native_ms']:7.3f} ms | {r['roofline']}")
+              f" | native {r['native_ms']:7.3f} ms (pipelined {r['native_pipelined_ms']:.3f}, warp/team "
+              f"{r['native_warp_team_ms']:.3f}) | {r['roofline']}")
     for s in swiglu_shapes:
         r = bench_swiglu(*s, dt, peaks, ref)
         report["swiglu"].append(r)

@@ -399,6 +399,423 @@ __global__ void __launch_bounds__(512, (GATE == GATE_VEC || MOD) ? 1 : 2) norm_b
 }
 
 // ---------------------------------------------------------------------------
+// Bulk-copy pipelined kernels (N % 8 == 0, 16-byte aligned rows)
+//
+// One producer thread streams whole rows of every input tensor into a
+// shared-memory ring of up to kStagesMax stages with 1-D bulk async copies
+// (cp.async.bulk ... mbarrier::complete_tx; no multicast), so the bytes in
+// flight per SM do not depend on registers. A stage holds G rows; thread group
+// g (nt threads) owns row g of every stage and NV2 fixed 8-column chunks of
+// it for the whole kernel, so per-column accumulators stay in registers. The
+// forward walks a contiguous block range per CTA and caches the per-sample
+// coefficients in registers; the backward prefetches its rows' rstd into
+// shared memory. Selected with nfb_norm_set_impl(1); the warp/team kernels
+// stay the default (see g_norm_impl for the measured comparison).
+// ---------------------------------------------------------------------------
+constexpr int kStagesMax = 8;
+constexpr uint64_t kCopyWaitNs = 2000000000ull;
+
+__device__ __forceinline__ uint32_t s_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void bar_init(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(s_u32(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void bar_expect(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool bar_try(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+               : "=r"(ok) : "r"(s_u32(b)), "r"(parity) : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity) {
+  if (bar_try(b, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!bar_try(b, parity)) {
+    if (globaltimer_ns() - t0 > kCopyWaitNs) return false;
+  }
+  return true;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* b) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(s_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(s_u32(b)) : "memory");
+}
+
+struct TmaGeom { int G; int stages; int nt; int rcap; };  // rows (= thread groups) per stage, stages, threads per group, rstd slots
+
+// ---------------- forward ----------------
+// Group g (nt threads) owns row g of every stage; one CTA barrier per stage.
+template <typename T, int GATE, bool MOD, int NV2>
+__global__ void __launch_bounds__(512, 1) norm_fwd_tma_kernel(NormFwdArgs a, TmaGeom g, uint32_t* status) {
+  extern __shared__ __align__(128) uint8_t tsmem[];
+  const int64_t N = a.N;
+  const int ntens = GATE != GATE_NONE ? 2 : 1;
+  const size_t rowb = (size_t)N * sizeof(T);
+  const size_t stage_b = (size_t)g.G * ntens * rowb;
+  uint64_t* full = reinterpret_cast<uint64_t*>(tsmem + (size_t)g.stages * stage_b);
+  float* red = reinterpret_cast<float*>(full + kStagesMax);           // [G][warps per group]
+  __shared__ int s_abort;
+  const int tid = threadIdx.x;
+  const int grp = tid / g.nt, lt = tid % g.nt, wpg = g.nt >> 5, wl = lt >> 5;
+  const int64_t nblocks = (a.M + g.G - 1) / g.G;
+  if (tid == 0) {
+    for (int s = 0; s < g.stages; ++s) bar_init(&full[s], 1);
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  __syncthreads();
+  auto issue = [&](int64_t blk, int stage) {
+    const int64_t r0 = blk * g.G;
+    const int rows = (int)min((int64_t)g.G, a.M - r0);
+    bar_expect(&full[stage], (uint32_t)(rows * ntens * rowb));
+    uint8_t* st = tsmem + (size_t)stage * stage_b;
+    for (int r = 0; r < rows; ++r) {
+      bulk_g2s(st + (size_t)(r * ntens) * rowb, reinterpret_cast<const T*>(a.x) + (r0 + r) * a.sx, (uint32_t)rowb, &full[stage]);
+      if (GATE != GATE_NONE)
+        bulk_g2s(st + (size_t)(r * ntens + 1) * rowb, reinterpret_cast<const T*>(a.y) + (r0 + r) * a.sy, (uint32_t)rowb, &full[stage]);
+    }
+  };
+  // contiguous block range per CTA, so the per-sample coefficients change rarely
+  const int64_t blk0 = nblocks * blockIdx.x / gridDim.x, blk1 = nblocks * (blockIdx.x + 1) / gridDim.x;
+  if (tid == 0)
+    for (int s = 0; s < g.stages; ++s)
+      if (blk0 + s < blk1) issue(blk0 + s, s);
+  constexpr bool kCache = NV2 <= 2;   // per-thread copies of weight*(1+scale), shift, gate for the current sample
+  float cw[kCache ? NV2 * 8 : 1], csf[(kCache && MOD) ? NV2 * 8 : 1], cg[(kCache && GATE == GATE_VEC) ? NV2 * 8 : 1];
+  int64_t cb = -1;
+  int64_t i = 0;
+  for (int64_t blk = blk0; blk < blk1; ++blk, ++i) {
+    const int stage = (int)(i % g.stages);
+    if (!bar_wait(&full[stage], (uint32_t)((i / g.stages) & 1))) {
+      if (tid == 0) { set_status(status, kTimeoutFlag, 20); s_abort = 1; }
+    }
+    __syncthreads();
+    if (s_abort) break;
+    const int64_t row = blk * g.G + grp;
+    const bool active = row < a.M;
+    const T* st = reinterpret_cast<const T*>(tsmem + (size_t)stage * stage_b) + (size_t)(grp * ntens) * N;
+    const int64_t b = active ? row / a.T : 0;
+    if (kCache && active && b != cb) {
+      cb = b;
+#pragma unroll
+      for (int c = 0; c < NV2; ++c) {
+        const int64_t col = ((int64_t)c * g.nt + lt) * 8;
+        if (col >= N) continue;
+        float wv[8];
+        load_weight_chunk<T>(a.weight, a.w_f32, col, N, wv);
+        if (MOD) {
+          float sc[8], sf[8];
+          load8<T>(reinterpret_cast<const T*>(a.scale) + b * a.ss + col, sc);
+          load8<T>(reinterpret_cast<const T*>(a.shift) + b * a.ssh + col, sf);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) { wv[j] *= 1.f + sc[j]; csf[(c * 8 + j) % (MOD ? NV2 * 8 : 1)] = sf[j]; }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) cw[(c * 8 + j) % (kCache ? NV2 * 8 : 1)] = wv[j];
+        if (GATE == GATE_VEC) {
+          float gv[8];
+          load8<T>(reinterpret_cast<const T*>(a.gate) + b * a.sg + col, gv);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) cg[(c * 8 + j) % (GATE == GATE_VEC ? NV2 * 8 : 1)] = gv[j];
+        }
+      }
+    }
+    float h[NV2][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < NV2; ++c) {
+      const int64_t col = ((int64_t)c * g.nt + lt) * 8;
+      if (!active || col >= N) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) h[c][j] = 0.f;
+        continue;
+      }
+      load8<T>(st + col, h[c]);
+      if (GATE != GATE_NONE) {
+        float yv[8];
+        load8<T>(st + N + col, yv);
+        if (GATE == GATE_VEC) {
+          float gv[8];
+          if (kCache) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) gv[j] = cg[(c * 8 + j) % (kCache && GATE == GATE_VEC ? NV2 * 8 : 1)];
+          } else {
+            load8<T>(reinterpret_cast<const T*>(a.gate) + b * a.sg + col, gv);
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) h[c][j] += gv[j] * yv[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) h[c][j] += yv[j];
+        }
+        round8<T>(h[c]);
+        store8<T>(reinterpret_cast<T*>(a.h) + row * a.sh + col, h[c]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += h[c][j] * h[c][j];
+    }
+    ss = warp_sum(ss);
+    if ((lt & 31) == 0) red[grp * wpg + wl] = ss;
+    __syncthreads();   // row sums visible; every thread is done reading this stage
+    if (tid == 0 && blk + g.stages < blk1) issue(blk + g.stages, stage);
+    float tot = 0.f;
+    for (int w = 0; w < wpg; ++w) tot += red[grp * wpg + w];
+    if (active) {
+      const float rstd = rsqrtf(tot / (float)N + a.eps);
+      if (lt == 0) a.rstd[row] = rstd;
+#pragma unroll
+      for (int c = 0; c < NV2; ++c) {
+        const int64_t col = ((int64_t)c * g.nt + lt) * 8;
+        if (col >= N) continue;
+        float o[8];
+        if (kCache) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int q = (c * 8 + j) % (kCache ? NV2 * 8 : 1);
+            o[j] = h[c][j] * rstd * cw[q] + (MOD ? csf[q % (MOD ? NV2 * 8 : 1)] : 0.f);
+          }
+        } else {
+          float wv[8];
+          load_weight_chunk<T>(a.weight, a.w_f32, col, N, wv);
+          if (MOD) {
+            float sc[8], sf[8];
+            load8<T>(reinterpret_cast<const T*>(a.scale) + b * a.ss + col, sc);
+            load8<T>(reinterpret_cast<const T*>(a.shift) + b * a.ssh + col, sf);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = h[c][j] * rstd * (wv[j] * (1.f + sc[j])) + sf[j];
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = h[c][j] * rstd * wv[j];
+          }
+        }
+        store8<T>(reinterpret_cast<T*>(a.out) + row * a.so + col, o);
+      }
+    }
+    __syncthreads();   // red[] reuse
+  }
+  if (tid == 0) {
+    for (int s = 0; s < g.stages; ++s) {
+      const int64_t k = i + s;
+      if (blk0 + k >= blk1) break;
+      const uint64_t t0 = globaltimer_ns();
+      while (!bar_try(&full[k % g.stages], (uint32_t)((k / g.stages) & 1))) {
+        if (globaltimer_ns() - t0 > kCopyWaitNs) break;
+      }
+    }
+  }
+}
+
+// ---------------- backward ----------------
+template <typename T, int GATE, bool MOD, int NV2>
+__global__ void __launch_bounds__(512, 1) norm_bwd_tma_kernel(NormBwdArgs a, TmaGeom g, uint32_t* status) {
+  extern __shared__ __align__(128) uint8_t tsmem[];
+  const int64_t N = a.N;
+  const bool has_up = a.dh_up != nullptr;
+  const int ntens = 2 + (has_up ? 1 : 0) + (GATE == GATE_VEC ? 1 : 0);
+  const int i_up = 2, i_y = has_up ? 3 : 2;
+  const size_t rowb = (size_t)N * sizeof(T);
+  const size_t stage_b = (size_t)g.G * ntens * rowb;
+  uint64_t* full = reinterpret_cast<uint64_t*>(tsmem + (size_t)g.stages * stage_b);
+  float* red = reinterpret_cast<float*>(full + kStagesMax);       // [G][warps per group]
+  float* ws_s = red + 32;                                          // [N]
+  float* gv_s = ws_s + N;                                          // [N]
+  float* rs_s = gv_s + N;                                          // [g.rcap] rstd of this CTA's rows
+  __shared__ int s_abort;
+  __shared__ uint32_t s_ticket;
+  const int tid = threadIdx.x;
+  const int grp = tid / g.nt, lt = tid % g.nt, wpg = g.nt >> 5, wl = lt >> 5;
+  const int64_t b = blockIdx.x / a.P, p = blockIdx.x % a.P;
+  const int64_t nblk_s = (a.T + g.G - 1) / g.G;
+  for (int64_t c = tid; c < N; c += blockDim.x) {
+    const float w = a.w_f32 ? reinterpret_cast<const float*>(a.weight)[c] : to_f32(reinterpret_cast<const T*>(a.weight)[c]);
+    const float s1 = MOD ? 1.f + to_f32(reinterpret_cast<const T*>(a.scale)[b * a.ss + c]) : 1.f;
+    ws_s[c] = w * s1;
+    gv_s[c] = (GATE == GATE_VEC) ? to_f32(reinterpret_cast<const T*>(a.gate)[b * a.sg + c]) : 1.f;
+  }
+  const int64_t my_blocks = nblk_s > p ? (nblk_s - p + a.P - 1) / a.P : 0;
+  const bool rs_pre = my_blocks * g.G <= g.rcap;
+  if (rs_pre)
+    for (int64_t e = tid; e < my_blocks * g.G; e += blockDim.x) {
+      const int64_t t = (p + (e / g.G) * a.P) * g.G + e % g.G;
+      rs_s[e] = t < a.T ? a.rstd[b * a.T + t] : 0.f;
+    }
+  if (tid == 0) {
+    for (int s = 0; s < g.stages; ++s) bar_init(&full[s], 1);
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  __syncthreads();
+  auto issue = [&](int64_t kb, int stage) {
+    const int64_t t0 = kb * g.G;
+    const int rows = (int)min((int64_t)g.G, a.T - t0);
+    bar_expect(&full[stage], (uint32_t)(rows * ntens * rowb));
+    uint8_t* st = tsmem + (size_t)stage * stage_b;
+    for (int r = 0; r < rows; ++r) {
+      const int64_t row = b * a.T + t0 + r;
+      uint8_t* d = st + (size_t)(r * ntens) * rowb;
+      bulk_g2s(d, reinterpret_cast<const T*>(a.dout) + row * a.s_dout, (uint32_t)rowb, &full[stage]);
+      bulk_g2s(d + rowb, reinterpret_cast<const T*>(a.h) + row * a.s_h, (uint32_t)rowb, &full[stage]);
+      if (has_up) bulk_g2s(d + (size_t)i_up * rowb, reinterpret_cast<const T*>(a.dh_up) + row * a.s_dhup, (uint32_t)rowb, &full[stage]);
+      if (GATE == GATE_VEC) bulk_g2s(d + (size_t)i_y * rowb, reinterpret_cast<const T*>(a.y) + row * a.s_y, (uint32_t)rowb, &full[stage]);
+    }
+  };
+  float accA[NV2 * 8], accD[NV2 * 8], accG[NV2 * 8];
+#pragma unroll
+  for (int j = 0; j < NV2 * 8; ++j) { accA[j] = 0.f; accD[j] = 0.f; accG[j] = 0.f; }
+  const float invN = 1.f / (float)N;
+  if (tid == 0)
+    for (int s = 0; s < g.stages; ++s)
+      if (p + (int64_t)s * a.P < nblk_s) issue(p + (int64_t)s * a.P, s);
+  int64_t i = 0;
+  for (int64_t kb = p; kb < nblk_s; kb += a.P, ++i) {
+    const int stage = (int)(i % g.stages);
+    if (!bar_wait(&full[stage], (uint32_t)((i / g.stages) & 1))) {
+      if (tid == 0) { set_status(status, kTimeoutFlag, 21); s_abort = 1; }
+    }
+    __syncthreads();
+    if (s_abort) break;
+    const int64_t t = kb * g.G + grp;
+    const bool active = t < a.T;
+    const int64_t row = b * a.T + t;
+    const T* st = reinterpret_cast<const T*>(tsmem + (size_t)stage * stage_b) + (size_t)(grp * ntens) * N;
+    const float rstd = !active ? 0.f : rs_pre ? rs_s[i * g.G + grp] : a.rstd[row];
+    float dot = 0.f;
+    if (active) {
+#pragma unroll
+      for (int c = 0; c < NV2; ++c) {
+        const int64_t col = ((int64_t)c * g.nt + lt) * 8;
+        if (col >= N) continue;
+        float dv[8], hv[8];
+        load8<T>(st + col, dv);
+        load8<T>(st + N + col, hv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float xh = hv[j] * rstd;
+          dot += dv[j] * ws_s[col + j] * xh;
+          accA[c * 8 + j] += dv[j] * xh;
+          if (MOD) accD[c * 8 + j] += dv[j];
+        }
+      }
+    }
+    dot = warp_sum(dot);
+    if ((lt & 31) == 0) red[grp * wpg + wl] = dot;
+    __syncthreads();
+    float tot = 0.f;
+    for (int w = 0; w < wpg; ++w) tot += red[grp * wpg + w];
+    const float d_r = tot * invN;
+    if (active) {
+#pragma unroll
+      for (int c = 0; c < NV2; ++c) {
+        const int64_t col = ((int64_t)c * g.nt + lt) * 8;
+        if (col >= N) continue;
+        float dv[8], hv[8], dh[8];
+        load8<T>(st + col, dv);
+        load8<T>(st + N + col, hv);
+        if (has_up) load8<T>(st + (size_t)i_up * N + col, dh);
+        else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) dh[j] = 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dh[j] += rstd * (dv[j] * ws_s[col + j] - hv[j] * rstd * d_r);
+        store8<T>(reinterpret_cast<T*>(a.dx) + row * a.s_dx + col, dh);
+        if (GATE == GATE_VEC) {
+          float yv[8], dyv[8];
+          load8<T>(st + (size_t)i_y * N + col, yv);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            dyv[j] = dh[j] * gv_s[col + j];
+            accG[c * 8 + j] += dh[j] * yv[j];
+          }
+          store8<T>(reinterpret_cast<T*>(a.dy) + row * a.s_dy + col, dyv);
+        } else if (GATE == GATE_ONE && a.dy != nullptr) {
+          store8<T>(reinterpret_cast<T*>(a.dy) + row * a.s_dy + col, dh);
+        }
+      }
+    }
+    __syncthreads();    // stage and red[] free
+    if (tid == 0 && kb + (int64_t)g.stages * a.P < nblk_s) issue(kb + (int64_t)g.stages * a.P, stage);
+  }
+  if (tid == 0) {
+    for (int s = 0; s < g.stages; ++s) {
+      const int64_t k = i + s;
+      if (p + k * a.P >= nblk_s) break;
+      const uint64_t t0 = globaltimer_ns();
+      while (!bar_try(&full[k % g.stages], (uint32_t)((k / g.stages) & 1))) {
+        if (globaltimer_ns() - t0 > kCopyWaitNs) break;
+      }
+    }
+  }
+  __syncthreads();
+  if (s_abort) return;
+  // fold the groups' column accumulators in shared memory (group order fixed), then write the CTA partial
+  float* fold = reinterpret_cast<float*>(tsmem);    // stages are drained: reuse as [G][3][N]
+#pragma unroll
+  for (int c = 0; c < NV2; ++c) {
+    const int64_t col = ((int64_t)c * g.nt + lt) * 8;
+    if (col >= N) continue;
+    float* f = fold + (size_t)grp * 3 * N;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      f[col + j] = accA[c * 8 + j];
+      f[N + col + j] = accD[c * 8 + j];
+      f[2 * N + col + j] = accG[c * 8 + j];
+    }
+  }
+  __syncthreads();
+  float* part = a.partials + (size_t)blockIdx.x * 3 * N;
+  for (int64_t e = tid; e < 3 * N; e += blockDim.x) {
+    float v = 0.f;
+    for (int q = 0; q < g.G; ++q) v += fold[(size_t)q * 3 * N + e];
+    part[e] = v;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_ticket = atomicAdd(&a.tickets[b], 1u);
+  __syncthreads();
+  if (s_ticket != (uint32_t)(a.P - 1)) return;
+  __threadfence();
+  const float* sp = a.partials + (size_t)b * a.P * 3 * N;
+  for (int64_t c = tid; c < N; c += blockDim.x) {
+    float A = 0.f, D = 0.f, Gs = 0.f;
+    for (int64_t q = 0; q < a.P; ++q) {
+      const float* pq = sp + (size_t)q * 3 * N;
+      A += __ldcg(pq + c);
+      if (MOD) D += __ldcg(pq + N + c);
+      if (GATE == GATE_VEC) Gs += __ldcg(pq + 2 * N + c);
+    }
+    const float w = a.w_f32 ? reinterpret_cast<const float*>(a.weight)[c] : to_f32(reinterpret_cast<const T*>(a.weight)[c]);
+    float s1 = 1.f;
+    if (MOD) {
+      s1 = 1.f + to_f32(reinterpret_cast<const T*>(a.scale)[b * a.ss + c]);
+      reinterpret_cast<T*>(a.dscale)[b * N + c] = from_f32<T>(w * A);
+      reinterpret_cast<T*>(a.dshift)[b * N + c] = from_f32<T>(D);
+    }
+    if (GATE == GATE_VEC) reinterpret_cast<T*>(a.dgate)[b * N + c] = from_f32<T>(Gs);
+    a.dwb[b * N + c] = s1 * A;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    a.tickets[b] = 0u;
+    s_ticket = atomicAdd(&a.tickets[a.B], 1u);
+  }
+  __syncthreads();
+  if (s_ticket != (uint32_t)(a.B - 1)) return;
+  __threadfence();
+  for (int64_t c = tid; c < N; c += blockDim.x) {
+    float sacc = 0.f;
+    for (int64_t q = 0; q < a.B; ++q) sacc += __ldcg(a.dwb + q * N + c);
+    if (a.w_f32) reinterpret_cast<float*>(a.dweight)[c] = sacc;
+    else reinterpret_cast<T*>(a.dweight)[c] = from_f32<T>(sacc);
+  }
+  if (tid == 0) a.tickets[a.B] = 0u;
+}
+
+// ---------------------------------------------------------------------------
 // Launch helpers
 // ---------------------------------------------------------------------------
 static int g_num_sms = 0;
@@ -414,6 +831,102 @@ static int num_sms() {
 
 static inline int team_warps(int64_t N) { return (int)((N + 511) / 512); }
 
+static inline int nv2_for(int64_t N) { return (int)((N / 8 + 255) / 256); }
+
+constexpr size_t kSmemCap = 227 * 1024;   // opt-in dynamic shared memory per CTA
+
+static size_t tma_smem(const TmaGeom& g, int64_t N, size_t esize, int ntens, bool bwd) {
+  size_t stages = (size_t)g.stages * g.G * ntens * N * esize;
+  if (bwd && stages < (size_t)g.G * 3 * N * 4) stages = (size_t)g.G * 3 * N * 4;
+  return stages + kStagesMax * 8 + 32 * 4 + (bwd ? (2 * N + g.rcap) * 4 : 0) + 128;
+}
+
+// Rows per stage G (one thread group of nt threads each, G * nt <= 512) and
+// the stage count that fit about 150 KB of staging; stages == 0 when even two
+// single-row stages do not fit in shared memory.
+static TmaGeom tma_geom(int64_t N, size_t esize, int ntens, bool bwd) {
+  TmaGeom g;
+  const int nv2 = nv2_for(N);
+  const int64_t chunks = (N / 8 + nv2 - 1) / nv2;
+  g.nt = (int)((chunks + 31) / 32 * 32);
+  g.rcap = bwd ? 2048 : 0;
+  int G = 512 / g.nt;
+  G = G < 1 ? 1 : (G > 8 ? 8 : G);
+  const size_t row_set = (size_t)ntens * N * esize;
+  while (G > 1 && 2 * (size_t)G * row_set > 150 * 1024) G >>= 1;
+  for (;; G >>= 1) {
+    g.G = G;
+    int st = (int)(150 * 1024 / ((size_t)G * row_set));
+    if (bwd) {   // the stage area is reused to fold G x 3 x N fp32 accumulators at the end
+      const size_t need = (size_t)G * 3 * N * 4;
+      while ((size_t)st * G * row_set < need) ++st;
+    }
+    g.stages = st < 2 ? 2 : (st > kStagesMax ? kStagesMax : st);
+    if (tma_smem(g, N, esize, ntens, bwd) <= kSmemCap) return g;
+    if (G == 1) break;
+  }
+  g.stages = 0;
+  return g;
+}
+
+// Device status word (per device) for the pipelined kernels' bounded waits; nonzero after a copy timed out.
+static uint32_t* g_status_dev[64] = {};
+NFB_API void nfb_norm_set_status(uint32_t* status) {
+  int d = 0;
+  cudaGetDevice(&d);
+  if (d >= 0 && d < 64) g_status_dev[d] = status;
+}
+static uint32_t* cur_status() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return (d >= 0 && d < 64) ? g_status_dev[d] : nullptr;
+}
+// 0 (default): register-resident warp/team kernels. 1: bulk-copy pipelined kernels where the rows
+// allow them. Measured on B200 (adaLN fwd+bwd, B8 x T2048 x N1536 bf16): 0.297 ms for 0 against
+// 0.469 ms for 1 -- with one CTA of 12 warps per SM the pipelined kernels stall on issue latency and
+// per-stage barriers (ncu: "wait", "barrier" and "short scoreboard" stalls, DRAM 21%), while the
+// warp/team kernels keep 32+ warps per SM loading straight into registers.
+static int g_norm_impl = 0;
+NFB_API void nfb_norm_set_impl(int impl) { g_norm_impl = impl; }
+NFB_API int nfb_norm_get_impl() { return g_norm_impl; }
+
+static inline bool al16(const void* p, int64_t stride_elems, size_t es) {
+  return p == nullptr || (((reinterpret_cast<uintptr_t>(p) & 15) == 0) && ((stride_elems * (int64_t)es) % 16 == 0));
+}
+template <typename T>
+static bool tma_ok_fwd(const NormFwdArgs& a, int gate) {
+  return g_norm_impl == 1 && a.N % 8 == 0 && a.N <= 8192 && al16(a.x, a.sx, sizeof(T)) && al16(a.y, a.sy, sizeof(T)) &&
+         tma_geom(a.N, sizeof(T), gate != GATE_NONE ? 2 : 1, false).stages > 0;
+}
+template <typename T>
+static bool tma_ok_bwd(const NormBwdArgs& a, int gate) {
+  return g_norm_impl == 1 && a.N % 8 == 0 && a.N <= 8192 && al16(a.dout, a.s_dout, sizeof(T)) && al16(a.h, a.s_h, sizeof(T)) &&
+         al16(a.dh_up, a.s_dhup, sizeof(T)) && al16(a.y, a.s_y, sizeof(T)) &&
+         tma_geom(a.N, sizeof(T), 2 + (a.dh_up ? 1 : 0) + (gate == GATE_VEC ? 1 : 0), true).stages > 0;
+}
+
+template <typename T, int GATE, bool MOD, int NV2>
+static int launch_fwd_tma(const NormFwdArgs& a, cudaStream_t st) {
+  const int ntens = GATE != GATE_NONE ? 2 : 1;
+  TmaGeom g = tma_geom(a.N, sizeof(T), ntens, false);
+  const size_t sm = tma_smem(g, a.N, sizeof(T), ntens, false);
+  cudaFuncSetAttribute(norm_fwd_tma_kernel<T, GATE, MOD, NV2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  const int64_t nblocks = (a.M + g.G - 1) / g.G;
+  const int grid = (int)(nblocks < num_sms() ? nblocks : num_sms());
+  norm_fwd_tma_kernel<T, GATE, MOD, NV2><<<grid, g.G * g.nt, sm, st>>>(a, g, cur_status());
+  return (int)cudaGetLastError();
+}
+
+template <typename T, int GATE, bool MOD, int NV2>
+static int launch_bwd_tma(const NormBwdArgs& a, cudaStream_t st) {
+  const int ntens = 2 + (a.dh_up ? 1 : 0) + (GATE == GATE_VEC ? 1 : 0);
+  TmaGeom g = tma_geom(a.N, sizeof(T), ntens, true);
+  const size_t sm = tma_smem(g, a.N, sizeof(T), ntens, true);
+  cudaFuncSetAttribute(norm_bwd_tma_kernel<T, GATE, MOD, NV2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  norm_bwd_tma_kernel<T, GATE, MOD, NV2><<<(int)(a.B * a.P), g.G * g.nt, sm, st>>>(a, g, cur_status());
+  return (int)cudaGetLastError();
+}
+
 template <typename T, int GATE, bool MOD, int NW>
 static int launch_fwd_warp(const NormFwdArgs& a, cudaStream_t st) {
   const int64_t want = (a.M + 7) / 8;
@@ -425,6 +938,14 @@ static int launch_fwd_warp(const NormFwdArgs& a, cudaStream_t st) {
 
 template <typename T, int GATE, bool MOD>
 static int launch_fwd(const NormFwdArgs& a, cudaStream_t st) {
+  if (tma_ok_fwd<T>(a, GATE)) {
+    switch (nv2_for(a.N)) {
+      case 1: return launch_fwd_tma<T, GATE, MOD, 1>(a, st);
+      case 2: return launch_fwd_tma<T, GATE, MOD, 2>(a, st);
+      case 3: return launch_fwd_tma<T, GATE, MOD, 3>(a, st);
+      default: return launch_fwd_tma<T, GATE, MOD, 4>(a, st);
+    }
+  }
   const int64_t nw = (a.N + 255) / 256;
   if (nw <= 1) return launch_fwd_warp<T, GATE, MOD, 1>(a, st);
   if (nw <= 2) return launch_fwd_warp<T, GATE, MOD, 2>(a, st);
@@ -449,10 +970,18 @@ static int launch_fwd(const NormFwdArgs& a, cudaStream_t st) {
 // Scratch sizes the Python side must provide for a backward call.
 NFB_API int64_t nfb_norm_bwd_P(int64_t M, int64_t N, int64_t B) {
   const int64_t T = M / B;
+  if (g_norm_impl == 1 && N % 8 == 0 && N <= 8192) {
+    // pipelined kernel: one wave with one CTA per SM (each keeps several stages
+    // of rows in flight); never more CTAs than rows
+    int64_t P = ((int64_t)num_sms() + B - 1) / B;
+    if (P > T) P = T;
+    return P < 1 ? 1 : P;
+  }
+  // team kernel: about two CTAs per SM, each with R row-teams
   const int K = team_warps(N);
   int R = 1;
   while (R * 2 * K * 32 <= 512 && R * 2 <= 8 && (size_t)R * 2 * 3 * N * 4 <= 160 * 1024) R *= 2;
-  int64_t target = (2 * (int64_t)num_sms() + B - 1) / B;  // ~2 CTAs per SM overall
+  int64_t target = (2 * (int64_t)num_sms() + B - 1) / B;
   int64_t maxP = (T + R - 1) / R;
   int64_t P = target < maxP ? target : maxP;
   return P < 1 ? 1 : P;
@@ -460,6 +989,14 @@ NFB_API int64_t nfb_norm_bwd_P(int64_t M, int64_t N, int64_t B) {
 
 template <typename T, int GATE, bool MOD>
 static int launch_bwd(const NormBwdArgs& a, cudaStream_t st) {
+  if (tma_ok_bwd<T>(a, GATE)) {
+    switch (nv2_for(a.N)) {
+      case 1: return launch_bwd_tma<T, GATE, MOD, 1>(a, st);
+      case 2: return launch_bwd_tma<T, GATE, MOD, 2>(a, st);
+      case 3: return launch_bwd_tma<T, GATE, MOD, 3>(a, st);
+      default: return launch_bwd_tma<T, GATE, MOD, 4>(a, st);
+    }
+  }
   const int K = team_warps(a.N);
   int R = 1;
   while (R * 2 * K * 32 <= 512 && R * 2 <= 8 && (size_t)R * 2 * 3 * a.N * 4 <= 160 * 1024) R *= 2;

@@ -28,6 +28,53 @@ GATE_NONE, GATE_ONE, GATE_VEC = 0, 1, 2
 MAX_N = 8192
 
 _tickets: dict[int, torch.Tensor] = {}
+_status: dict[int, torch.Tensor] = {}
+_impl_set = [False]
+
+
+class NormTimeout(RuntimeError):
+    """A pipelined norm kernel gave up waiting for its row copies (bounded wait expired)."""
+
+
+def _dev_index(device: torch.device) -> int:
+    return device.index if device.index is not None else torch.cuda.current_device()
+
+
+def _ensure_native_state(device: torch.device) -> None:
+    """Register this device's status word with the kernels and apply ``NFB_NORM_IMPL`` once.
+
+    The default (``NFB_NORM_IMPL=0``) is the register-resident warp/team
+    kernels; ``1`` selects the bulk-copy pipelined kernels where rows allow
+    (slower on B200 at the model's shapes; kept for comparison).
+    """
+    idx = _dev_index(device)
+    if idx not in _status:
+        _status[idx] = torch.zeros(1, dtype=torch.int32, device=device)
+        with torch.cuda.device(idx):
+            nat.lib().nfb_norm_set_status(nat.ptr(_status[idx]))
+    if not _impl_set[0]:
+        import os
+        set_impl(int(os.environ.get("NFB_NORM_IMPL", "0")))
+
+
+def set_impl(impl: int) -> None:
+    """Select the norm kernel family: 0 = warp/team (default), 1 = bulk-copy pipelined."""
+    nat.lib().nfb_norm_set_impl(int(impl))
+    _impl_set[0] = True
+
+
+def get_impl() -> int:
+    return int(nat.lib().nfb_norm_get_impl())
+
+
+def check_status(device: torch.device | None = None) -> None:
+    """Raise :class:`NormTimeout` if a pipelined norm kernel on ``device`` timed out (synchronises)."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    st = _status.get(_dev_index(device))
+    if st is not None and int(st.item()) != 0:
+        v = int(st.item())
+        st.zero_()
+        raise NormTimeout(f"norm kernel copy wait timed out (status 0x{v:08x}, site {v & 0xFFFFFF})")
 
 
 def ticket_buffer(device: torch.device, n: int) -> torch.Tensor:
@@ -66,6 +113,7 @@ def _wflag(weight: torch.Tensor, x: torch.Tensor) -> tuple[torch.Tensor, int]:
 
 def _fwd(x, y, gate, weight, scale, shift, T, eps, gate_mode, mod):
     M, N = x.shape
+    _ensure_native_state(x.device)
     w, wf = _wflag(weight, x)
     h = torch.empty((M, N), dtype=x.dtype, device=x.device) if gate_mode != GATE_NONE else None
     out = torch.empty((M, N), dtype=x.dtype, device=x.device)
@@ -90,6 +138,7 @@ def _bwd(ctx, dh_up, dout):
     M, N = hs.shape
     B = M // T
     dev = hs.device
+    _ensure_native_state(dev)
     if dout is None:
         dout = torch.zeros_like(hs)
     dout = _rows(dout, N)

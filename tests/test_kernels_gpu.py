@@ -42,12 +42,25 @@ def _inputs(b, t, n, dtype, seed=0, strided=True):
     return x, y, gate, w, scale, shift
 
 
-SHAPES = [(2, 16, 256), (4, 32, 1024), (3, 7, 768), (1, 64, 1536), (2, 5, 1000), (8, 128, 2048)]
+SHAPES = [(2, 16, 256), (4, 32, 1024), (3, 7, 768), (1, 64, 1536), (2, 5, 1000), (8, 128, 2048),
+          (2, 300, 4096), (1, 37, 8192)]
+
+
+@pytest.fixture(params=[0, 1], ids=["warp_team", "pipelined"])
+def norm_impl(request):
+    """Run a norm test with the warp/team kernels (0, default) and the bulk-copy pipelined kernels (1)."""
+    _nat()
+    from nuvla_forge_b200.ops import norm
+
+    norm.set_impl(request.param)
+    yield request.param
+    norm.check_status()
+    norm.set_impl(0)
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("shape", SHAPES)
-def test_adaln_fwd_bwd(shape, dtype):
+def test_adaln_fwd_bwd(shape, dtype, norm_impl):
     _nat()
     from nuvla_forge_b200.ops import fused_adaln_residual_rmsnorm
     from nuvla_forge_b200.ops.reference import adaln_residual_rmsnorm_ref
@@ -85,7 +98,7 @@ def test_adaln_deterministic():
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_rmsnorm_variants(dtype):
+def test_rmsnorm_variants(dtype, norm_impl):
     _nat()
     from nuvla_forge_b200.ops import add_rmsnorm, rmsnorm
     from nuvla_forge_b200.ops.reference import add_rmsnorm_ref, rmsnorm_ref
@@ -115,6 +128,25 @@ def test_rmsnorm_variants(dtype):
     h, o = add_rmsnorm(x, y, w)
     hr, orf = add_rmsnorm_ref(x.float(), y.float(), w.float())
     assert rel_err(h, hr) < TOL[dtype] and rel_err(o, orf) < TOL[dtype]
+
+
+def test_norm_impls_agree():
+    """Pipelined and warp/team kernels give the same result up to fp32 summation order."""
+    _nat()
+    from nuvla_forge_b200.ops import fused_adaln_residual_rmsnorm, norm
+
+    base = _inputs(8, 256, 1536, torch.bfloat16)
+    res = []
+    for impl in (1, 0):
+        norm.set_impl(impl)
+        leaves = [v.detach().clone().requires_grad_(True) for v in base]
+        h, o = fused_adaln_residual_rmsnorm(*leaves, tokens_per_sample=256)
+        (h.float().sum() + (o.float() ** 2).sum()).backward()
+        res.append([h, o] + [l.grad for l in leaves])
+    norm.set_impl(0)
+    norm.check_status()
+    for a, b in zip(*res):
+        assert rel_err(a, b) < 1e-2
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
