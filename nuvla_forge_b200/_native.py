@@ -64,6 +64,9 @@ _SIGS: dict[str, tuple] = {
     "nfb_ce_tc_stats": (I, [P, L, P, L, P, I, I, I, P, P, P, P, P]),
     "nfb_ce_tc_merge": (I, [P, P, P, P, P, I, I, L, P, P, P]),
     "nfb_ce_tc_grad": (I, [P, L, P, L, P, P, P, L, I, I, I, P, L, P, P]),
+    "nfb_ag_gemm": (I, [P, I, L, L, P, L, L, L, I, I, P, L, I, P, L, P, P, P]),
+    "nfb_ag_gemm_max_nblocks": (I, []),
+    "nfb_copy_async": (I, [P, P, L, P]),
 }
 
 _lib = None

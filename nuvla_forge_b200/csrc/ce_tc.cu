@@ -19,63 +19,18 @@
 #include <cudaTypedefs.h>
 
 #include "tc_gemm.cuh"
+#include "tc_host.cuh"
 
 namespace nfb {
 namespace tc {
-
-// ---------------------------------------------------------------------------
-// Host: tensor maps through the driver entry point (no libcuda link needed).
-// ---------------------------------------------------------------------------
-static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
-
-static int get_encode() {
-  if (g_encode) return 0;
-  void* fn = nullptr;
-  cudaDriverEntryPointQueryResult q;
-  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr) return (int)cudaErrorNotSupported;
-  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-  return 0;
-}
-
-// 2-D bf16 row-major [rows, cols] with row stride `ld` elements; box = box_rows x 64 columns, 128B swizzle.
-static int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
-  int rc = get_encode();
-  if (rc) return rc;
-  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * 2) % 16) || cols % 8) return (int)cudaErrorInvalidValue;
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
-}
-
-static int sm_count() {
-  int dev = 0, n = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  return n;
-}
-
-static GemmShape make_shape(int M, int N, int K) {
-  GemmShape s;
-  s.M = M; s.N = N; s.K = K;
-  s.m_tiles = (M + BM - 1) / BM;
-  s.n_tiles = (N + BN - 1) / BN;
-  s.k_tiles = (K + BK - 1) / BK;
-  s.group = 8;
-  return s;
-}
 
 template <class Epi>
 __global__ void __launch_bounds__(kThreads, 1) tc_kernel(const __grid_constant__ CUtensorMap ta,
                                                         const __grid_constant__ CUtensorMap tb, GemmShape sh,
                                                         Epi epi, uint32_t* status) {
   Epi e = epi;
-  gemm_body(&ta, &tb, sh, e, status);
+  NoGate g;
+  gemm_body(&ta, &tb, sh, e, status, g);
 }
 
 template <class Epi>
@@ -99,42 +54,6 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, int M,
 // ---------------------------------------------------------------------------
 // Epilogues (one TMEM lane = one output row per thread)
 // ---------------------------------------------------------------------------
-struct StoreEpi {
-  void* C;
-  int64_t ldc;
-  int out_f32;
-  int vec_ok;  // rows 16-byte aligned
-
-  __device__ void row(int m0, int n0, int r, uint32_t taddr, const GemmShape& sh) {
-    const int m = m0 + r;
-#pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      float v[32];
-      tmem_ld32(taddr + c, v);
-      if (m >= sh.M) continue;
-      const int n = n0 + c;
-      if (out_f32) {
-        float* dst = reinterpret_cast<float*>(C) + (int64_t)m * ldc + n;
-        if (vec_ok && n + 32 <= sh.N) {
-#pragma unroll
-          for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) if (n + j < sh.N) dst[j] = v[j];
-        }
-      } else {
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(C) + (int64_t)m * ldc + n;
-        if (vec_ok && n + 32 <= sh.N) {
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) store16<__nv_bfloat16>(dst + j, v + j);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) if (n + j < sh.N) dst[j] = __float2bfloat16_rn(v[j]);
-        }
-      }
-    }
-  }
-};
 
 struct CeStatsEpi {
   const int64_t* targets;

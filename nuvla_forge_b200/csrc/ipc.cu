@@ -40,3 +40,10 @@ NFB_API int nfb_ipc_close(void* ptr) { return (int)cudaIpcCloseMemHandle(ptr); }
 NFB_API int nfb_ipc_free(void* ptr) { return (int)cudaFree(ptr); }
 
 NFB_API int nfb_device_synchronize() { return (int)cudaDeviceSynchronize(); }
+
+// Asynchronous copy between any two device addresses of this process (a peer's
+// IPC-mapped memory included; the copy engine moves it over NVLink).
+NFB_API int nfb_copy_async(void* dst, const void* src, int64_t bytes, void* stream) {
+  if (bytes <= 0) return 0;
+  return (int)cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDefault, (cudaStream_t)stream);
+}

@@ -13,6 +13,9 @@
 // Two accumulators let the epilogue of tile i overlap the main loop of tile i+1.
 // No TMA multicast and no clusters are used.
 //
+// A Gate policy can add worker warps (warp 6 onward) and make the producer wait
+// until the B rows of an N-block are ready before loading them (NoGate: none).
+//
 // Every mbarrier wait is bounded by %globaltimer. On timeout a role records an
 // error code in the caller's status word, raises the CTA-wide abort flag and
 // stops; the other roles see the flag and stop too; the producer waits (bounded)
@@ -48,8 +51,25 @@ struct alignas(8) Shared {
   int abort;
 };
 
-// smem layout: [1 KB-aligned stage buffers][Shared]
-constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + sizeof(Shared) + 1024;
+// smem layout: [1 KB-aligned stage buffers][Shared (1 KB slot)][gate area]
+constexpr size_t kSharedSlot = 1024;
+static_assert(sizeof(Shared) <= kSharedSlot, "Shared must fit its slot");
+constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + kSharedSlot + 1024;
+
+// Default gate: no worker warps, every N-block always ready.
+struct NoGate {
+  static constexpr int kWarps = 0;
+  static constexpr size_t kSmemBytes = 0;
+  __device__ __forceinline__ void bind(uint8_t*) {}   // every thread: locate the gate's shared memory
+  __device__ __forceinline__ void init() {}           // thread 0, before the CTA barrier
+  __device__ __forceinline__ bool wait_nblock(int, volatile int*) { return true; }
+  __device__ __forceinline__ void worker(int, uint8_t*, volatile int*) {}
+};
+
+template <class Gate>
+constexpr size_t smem_bytes() { return kSmemBytes + Gate::kSmemBytes; }
+template <class Gate>
+constexpr int threads_for() { return kThreads + 32 * Gate::kWarps; }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -181,16 +201,57 @@ struct GemmShape {
   int group;
 };
 
+// Plain store epilogue: C[m, n] (bf16 or fp32, row stride ldc), 16-byte
+// vector stores when the rows allow them.
+struct StoreEpi {
+  void* C;
+  int64_t ldc;
+  int out_f32;
+  int vec_ok;  // rows 16-byte aligned
+
+  __device__ void row(int m0, int n0, int r, uint32_t taddr, const GemmShape& sh) {
+    const int m = m0 + r;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      float v[32];
+      tmem_ld32(taddr + c, v);
+      if (m >= sh.M) continue;
+      const int n = n0 + c;
+      if (out_f32) {
+        float* dst = reinterpret_cast<float*>(C) + (int64_t)m * ldc + n;
+        if (vec_ok && n + 32 <= sh.N) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) if (n + j < sh.N) dst[j] = v[j];
+        }
+      } else {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(C) + (int64_t)m * ldc + n;
+        if (vec_ok && n + 32 <= sh.N) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) store16<__nv_bfloat16>(dst + j, v + j);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) if (n + j < sh.N) dst[j] = __float2bfloat16_rn(v[j]);
+        }
+      }
+    }
+  }
+};
+
 // The persistent kernel body. Epi must provide:
 //   __device__ void row(int tile_m0, int tile_n0, int row_in_tile, uint32_t tmem_row_addr, const GemmShape&)
 // which reads the 256 accumulator columns of its row (tmem_ld32 at tmem_row_addr + c)
 // and consumes them.
-template <class Epi>
+template <class Epi, class Gate = NoGate>
 __device__ void gemm_body(const CUtensorMap* tma_a, const CUtensorMap* tma_b, const GemmShape& sh, Epi& epi,
-                          uint32_t* status) {
+                          uint32_t* status, Gate& gate) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Shared* S = reinterpret_cast<Shared*>(smem + (size_t)kStages * kStageBytes);
+  uint8_t* gate_smem = smem + (size_t)kStages * kStageBytes + kSharedSlot;
+  gate.bind(gate_smem);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   volatile int* abort_flag = &S->abort;
@@ -206,6 +267,7 @@ __device__ void gemm_body(const CUtensorMap* tma_a, const CUtensorMap* tma_b, co
     }
     mbar_init(&S->mma_drain, 1);
     S->abort = 0;
+    gate.init();
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -231,6 +293,7 @@ __device__ void gemm_body(const CUtensorMap* tma_a, const CUtensorMap* tma_b, co
       bool ok = true;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
         const TileCoord tc = tile_coord(t, sh.m_tiles, sh.n_tiles, sh.group);
+        if (!gate.wait_nblock(tc.n_blk, abort_flag)) { ok = false; break; }
         for (int kb = 0; kb < sh.k_tiles; ++kb) {
           if (!mbar_wait(&S->empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
           uint8_t* sa = smem + (size_t)stage * kStageBytes;
@@ -297,6 +360,9 @@ __device__ void gemm_body(const CUtensorMap* tma_a, const CUtensorMap* tma_b, co
         if (globaltimer_ns() - t0 > kWaitNs) break;
       }
     }
+  } else if (warp >= kThreads / 32) {
+    // ---------------- gate worker warps (6 ..) ----------------
+    gate.worker(warp - kThreads / 32, gate_smem, abort_flag);
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int quarter = warp & 3;               // TMEM lanes 32*quarter .. +31

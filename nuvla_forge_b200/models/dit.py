@@ -25,7 +25,7 @@ import torch.nn.functional as F
 from torch import nn
 
 from ..ops import fused_adaln_residual_rmsnorm
-from .layers import Attention, RMSNorm, SwiGLUMLP, TimestepEmbedder, modulate
+from .layers import Attention, RMSNorm, SwiGLUMLP, TimestepEmbedder, linear, modulate
 
 
 class DiTBlock(nn.Module):
@@ -45,11 +45,15 @@ class DiTBlock(nn.Module):
         nn.init.zeros_(self.cond[1].weight)
         nn.init.zeros_(self.cond[1].bias)
 
+    def _cond(self, c):
+        lin = self.cond[1]
+        return linear(F.silu(c), lin.weight, lin.bias)
+
     def forward_chain(self, x, c, context, pending=None):
         """Fused path. ``pending`` = (y, gate): the previous block's gated branch
         output not yet added to x. Returns (x, (mlp_out, gate2))."""
         b, t, _ = x.shape
-        shift1, scale1, gate1, shift2, scale2, gate2 = self.cond(c).chunk(6, dim=-1)
+        shift1, scale1, gate1, shift2, scale2, gate2 = self._cond(c).chunk(6, dim=-1)
         if pending is None:
             h = self.norm1(x, scale=scale1, shift=shift1, tokens_per_sample=t)
         else:
@@ -66,7 +70,7 @@ class DiTBlock(nn.Module):
         if self.fused:
             x, (m, g) = self.forward_chain(x, c, context)
             return x + g.unsqueeze(1) * m
-        shift1, scale1, gate1, shift2, scale2, gate2 = self.cond(c).chunk(6, dim=-1)
+        shift1, scale1, gate1, shift2, scale2, gate2 = self._cond(c).chunk(6, dim=-1)
         x = x + gate1.unsqueeze(1) * self.attn(modulate(self.norm1(x), shift1, scale1))
         x = x + self.cross(self.norm_cross(x), context)
         return x + gate2.unsqueeze(1) * self.mlp(modulate(self.norm2(x), shift2, scale2))

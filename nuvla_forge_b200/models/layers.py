@@ -34,11 +34,33 @@ from ..ops import swiglu_packed
 from ..ops.reference import swiglu_ref
 
 
+# A parameter owner (the FSDP runtime) that deferred gathering a unit's
+# parameters to the unit's first linear layer; it returns that layer's output
+# (computed by the all-gather-fused GEMM) or None to let F.linear run.
+_pending_consumer = None
+
+
+def set_pending_consumer(fn) -> None:
+    """Register (or clear, with None) the callable that gets the next linear() call."""
+    global _pending_consumer
+    _pending_consumer = fn
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None) -> torch.Tensor:
+    """F.linear, except that a pending parameter consumer may compute it first."""
+    fn = _pending_consumer
+    if fn is not None:
+        y = fn(x, w, b)
+        if y is not None:
+            return y
+    return F.linear(x, w, b)
+
+
 def _linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None,
             residual: torch.Tensor | None = None) -> torch.Tensor:
     """y = x @ w.T (+ b) (+ residual), with the residual read by the GEMM itself."""
     if residual is None:
-        return F.linear(x, w, b)
+        return linear(x, w, b)
     shape = residual.shape
     x2 = x.reshape(-1, x.shape[-1])
     r2 = residual.reshape(-1, shape[-1])
@@ -114,16 +136,16 @@ class Attention(nn.Module):
         b, t, c = x.shape
         H, Hk, Dh = self.n_heads, self.kv_heads, self.head_dim
         if context is None:
-            qkv = F.linear(x, self.qkv.weight).view(b, t, H + 2 * Hk, Dh)
+            qkv = linear(x, self.qkv.weight).view(b, t, H + 2 * Hk, Dh)
             q, k, v = qkv.split([H, Hk, Hk], dim=2)
         else:
             s = context.shape[1]
             if self.split_ctx:
-                q = F.linear(x, self.q.weight).view(b, t, H, Dh)
-                kv = F.linear(context, self.kv.weight).view(b, s, 2 * Hk, Dh)
+                q = linear(x, self.q.weight).view(b, t, H, Dh)
+                kv = linear(context, self.kv.weight).view(b, s, 2 * Hk, Dh)
             else:
-                q = F.linear(x, self.qkv.weight[:c]).view(b, t, H, Dh)
-                kv = F.linear(context, self.qkv.weight[c:]).view(b, s, 2 * Hk, Dh)
+                q = linear(x, self.qkv.weight[:c]).view(b, t, H, Dh)
+                kv = linear(context, self.qkv.weight[c:]).view(b, s, 2 * Hk, Dh)
             k, v = kv.split([Hk, Hk], dim=2)
         o = attention_op(q, k, v, causal=self.causal and context is None, force_reference=not self.fused)
         o = o.reshape(b, t, c)
@@ -160,7 +182,7 @@ class SwiGLUMLP(nn.Module):
             state_dict[prefix + "w_gate_up"] = torch.cat([state_dict.pop(g), state_dict.pop(u)], dim=0)
 
     def forward(self, x, residual=None):
-        ab = F.linear(x, self.w_gate_up)
+        ab = linear(x, self.w_gate_up)
         if self.fused:
             act = swiglu_packed(ab)
         else:

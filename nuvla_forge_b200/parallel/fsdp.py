@@ -13,10 +13,16 @@ clipping:
   launch), and the bf16 parameter shard in peer-mapped memory, where the
   optimizer writes it directly.
 * Forward: before a unit runs, its bf16 parameters are all-gathered into a
-  full buffer the module's parameters are views of (``nfb_allgather``: each
-  rank pulls its peers' shards over NVLink); after it runs, the buffer's
-  storage is released (``reshard_after_forward``). Backward: a hook on the
-  unit's outputs gathers it again before its backward runs.
+  full buffer the module's parameters are views of; after it runs, the
+  buffer's storage is released (``reshard_after_forward``). For transformer
+  and DiT blocks (``fuse_ag_gemm``) the gather is fused into the block's first
+  linear layer: the 1-D parameters (norm weights, biases; laid out first in
+  the unit) are copied ahead by the copy engine, and the block's first GEMM is
+  ``nfb_ag_gemm`` -- one kernel that pulls the whole unit over NVLink while
+  its tensor-core tiles consume the weight's row blocks as they land. Other
+  units use ``nfb_allgather`` (each rank pulls its peers' shards). Backward: a
+  hook on the unit's outputs gathers it again (``nfb_allgather``) before its
+  backward runs.
 * Gradients: bf16 gradients are folded into a per-unit fp32 accumulator
   (exact across micro-steps); when a unit's gradients are complete on a
   syncing micro-step they are cast to bf16 into peer-mapped memory and
@@ -76,12 +82,15 @@ class _Unit:
     ready: bool = False
     launched: bool = False
     bwd_gathered: bool = False
+    prefix: int = 0            # elements of the leading 1-D parameters (copied ahead of a fused gather)
+    ag_ok: bool = False        # the unit's first parameter consumer is a linear layer (fused gather allowed)
+    ag_pending: bool = False   # storage allocated, prefix copied, the rest awaits the fused GEMM
 
 
 class FullyShardedDataParallel(nn.Module):
     def __init__(self, module: nn.Module, param_dtype: torch.dtype | None = None, comm: str = "auto",
                  unit_types: tuple | None = None, reshard_after_forward: bool = True, ctas: int = 32,
-                 process_group: dist.ProcessGroup | None = None):
+                 process_group: dist.ProcessGroup | None = None, fuse_ag_gemm: bool | None = None):
         super().__init__()
         self.module = module
         dev = next(module.parameters()).device
@@ -107,6 +116,18 @@ class FullyShardedDataParallel(nn.Module):
             unit_types = (TransformerBlock, DiTBlock)
         self.units = self._build_units(unit_types)
         self.root = self.units[-1]
+        from ..models.dit import DiTBlock
+        from ..models.layers import TransformerBlock
+        if fuse_ag_gemm is None:   # default on; NFB_FSDP_FUSE_AG=0 keeps the separate all-gather kernel
+            import os
+            fuse_ag_gemm = os.environ.get("NFB_FSDP_FUSE_AG", "1") != "0"
+        self.fuse_ag_gemm = bool(fuse_ag_gemm and comm == "fused")
+        for u in self.units[:-1]:
+            # blocks whose first parameter use is a linear layer (after 1-D norm weights / biases)
+            u.ag_ok = self.fuse_ag_gemm and isinstance(u.module, (TransformerBlock, DiTBlock))
+        self._ag_unit: _Unit | None = None
+        self._ag_ready = torch.zeros(1024, dtype=torch.int32, device=dev) if self.fuse_ag_gemm else None
+        self.ag_fused_launches = 0
         self.shard_numel = sum(u.shard for u in self.units)
         self.master = torch.zeros(self.shard_numel, dtype=torch.float32, device=dev)
         self.grads = torch.zeros(self.shard_numel, dtype=torch.float32, device=dev)
@@ -173,10 +194,14 @@ class FullyShardedDataParallel(nn.Module):
         return u
 
     def _fill_unit(self, u: _Unit, named) -> None:
+        # 1-D parameters first: they form the prefix a fused gather copies ahead
+        named = [(n, p) for n, p in named if p.dim() <= 1] + [(n, p) for n, p in named if p.dim() > 1]
         off = 0
         for n, p in named:
             u.segs.append(_Seg(n, p, off, p.numel(), p.shape))
             off += _round(p.numel(), 8)
+            if p.dim() <= 1:
+                u.prefix = off
         u.numel = _round(max(off, 8), 8 * self.world)
         u.shard = u.numel // self.world
         u.pending = len(u.segs)
@@ -207,13 +232,25 @@ class FullyShardedDataParallel(nn.Module):
             self.param_shards.copy_(self.master.to(self.param_dtype))
 
     # ------------------------------------------------------------ gather / reshard
-    def _gather(self, u: _Unit) -> None:
+    def _gather(self, u: _Unit, lazy: bool = False) -> None:
         if u.gathered:
             return
         st = u.full.untyped_storage()
         nbytes = u.numel * u.full.element_size()
         if st.nbytes() != nbytes:
             st.resize_(nbytes)
+        if lazy and u.ag_ok:
+            self._copy_prefix(u)
+            u.ag_pending = True
+            u.gathered = True
+            self._ag_unit = u
+            from ..models import layers
+            layers.set_pending_consumer(self._consume_linear)
+            return
+        self._launch_allgather(u)
+        u.gathered = True
+
+    def _launch_allgather(self, u: _Unit) -> None:
         if self.comm == "fused":
             ws = self.ws
             nat.call("nfb_allgather", ws.bases_ptr(), ws.rank, ws.world, u.shard,
@@ -229,7 +266,55 @@ class FullyShardedDataParallel(nn.Module):
             u.full.copy_(torch.cat(parts))
         else:  # single process
             u.full.copy_(self.param_shards[u.shard_start: u.shard_start + u.shard])
-        u.gathered = True
+
+    # ------------------------------------------------ all-gather fused into the first GEMM
+    def _copy_prefix(self, u: _Unit) -> None:
+        """Copy the unit's leading 1-D parameters from their owners (copy engine, over NVLink)."""
+        end = u.prefix * 2
+        if end == 0:
+            return
+        S = u.shard * 2
+        src0 = self.param_off + u.shard_start * 2
+        stream = nat.stream(self.device)
+        for q in range(self.world):
+            f0, f1 = q * S, min((q + 1) * S, end)
+            if f1 <= f0:
+                break
+            nat.call("nfb_copy_async", ctypes.c_void_p(u.full.data_ptr() + f0),
+                     ctypes.c_void_p(self.ws.bases[q] + src0), f1 - f0, stream)
+
+    def _consume_linear(self, x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None):
+        """The pending unit's first linear layer: run it as the all-gather-fused GEMM."""
+        u = self._ag_unit
+        if u is None or not u.ag_pending:
+            return None
+        full = u.full
+        if w.untyped_storage().data_ptr() != full.untyped_storage().data_ptr():
+            return None
+        from ..models import layers
+        u.ag_pending = False
+        self._ag_unit = None
+        layers.set_pending_consumer(None)
+        K = x.shape[-1]
+        off = w.data_ptr() - full.data_ptr()
+        fits = (x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and w.dim() == 2 and w.is_contiguous()
+                and K % 8 == 0 and x.numel() > 0 and off % 16 == 0
+                and (w.shape[0] + 255) // 256 <= self._ag_ready.numel())
+        if not fits:
+            self._launch_allgather(u)
+            return None
+        y = _AgLinear.apply(x, w, self, u)
+        return y if b is None else y + b
+
+    def _launch_ag_gemm(self, u: _Unit, x2: torch.Tensor, w: torch.Tensor, y: torch.Tensor) -> None:
+        ws = self.ws
+        M, K = x2.shape
+        N = w.shape[0]
+        nat.call("nfb_ag_gemm", ws.bases_ptr(), ws.world, self.param_off + u.shard_start * 2, u.shard * 2,
+                 nat.ptr(u.full), u.prefix * 2, u.numel * 2, w.data_ptr() - u.full.data_ptr(), N, K, nat.ptr(x2),
+                 x2.stride(0), M, nat.ptr(y), y.stride(0), nat.ptr(self._ag_ready), nat.ptr(ws.status),
+                 nat.stream(self.device))
+        self.ag_fused_launches += 1
 
     def _reshard(self, u: _Unit) -> None:
         if not u.gathered or u is self.root:
@@ -259,12 +344,14 @@ class FullyShardedDataParallel(nn.Module):
             setattr(mod, meth, wrapped)
 
     def _pre_forward(self, u: _Unit) -> None:
-        self._gather(u)
+        self._gather(u, lazy=self.fuse_ag_gemm)
         if u not in self._order:
             self._order.append(u)
         u.bwd_gathered = False
 
     def _post_forward(self, u: _Unit, out) -> None:
+        if u.ag_pending:
+            raise RuntimeError(f"FSDP unit {u.name}: its deferred all-gather was never consumed by a linear layer")
         if torch.is_grad_enabled():
             for t in _tensors(out):
                 if t.requires_grad:
@@ -472,6 +559,35 @@ class FullyShardedDataParallel(nn.Module):
         opt.step_count = int(sd["step"])
         opt.m.copy_(sd["exp_avg_shards"][self.rank].to(opt.m.device))
         opt.v.copy_(sd["exp_avg_sq_shards"][self.rank].to(opt.v.device))
+
+
+class _AgLinear(torch.autograd.Function):
+    """y = x @ w.T where the forward GEMM also gathers w's FSDP unit (``nfb_ag_gemm``).
+
+    Backward runs after the unit was gathered again, with plain GEMMs.
+    """
+
+    @staticmethod
+    def forward(ctx, x, w, fsdp, u):
+        K = x.shape[-1]
+        x2 = x.reshape(-1, K)
+        if not x2.is_contiguous() or x2.data_ptr() % 16:
+            x2 = x2.contiguous()
+        y = torch.empty((x2.shape[0], w.shape[0]), dtype=x.dtype, device=x.device)
+        fsdp._launch_ag_gemm(u, x2, w, y)
+        ctx.save_for_backward(x, w)
+        return y.view(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, w = ctx.saved_tensors
+        gy2 = gy.reshape(-1, gy.shape[-1])
+        gx = gw = None
+        if ctx.needs_input_grad[0]:
+            gx = (gy2 @ w).view(x.shape)
+        if ctx.needs_input_grad[1]:
+            gw = gy2.t() @ x.reshape(-1, x.shape[-1])
+        return gx, gw, None, None
 
 
 def _tensors(obj):

@@ -1,9 +1,11 @@
 """Multi-GPU (NCCL + CUDA IPC peer memory) tests of the fused collectives and DDP.
 
-Each test spawns one process per GPU (2 to 4). NVLS is off in NCCL and the
-fused kernels use plain peer loads/stores (no multicast objects).
+Each test spawns one process per GPU (2 to 4 by default; ``NFB_TEST_MAX_WORLD``
+raises the cap, e.g. to 8). NVLS is off in NCCL and the fused kernels use plain
+peer loads/stores (no multicast objects).
 """
 
+import os
 import time
 
 import pytest
@@ -17,7 +19,7 @@ ENV = {"NCCL_NVLS_ENABLE": "0"}
 
 
 def _world():
-    return min(torch.cuda.device_count(), 4)
+    return min(torch.cuda.device_count(), int(os.environ.get("NFB_TEST_MAX_WORLD", "4")))
 
 
 def _fused_ar(rank, world, sizes):
@@ -162,4 +164,101 @@ def test_fsdp_fused_matches_nccl():
     assert all(st == "ok" for st, _ in a.values()) and all(st == "ok" for st, _ in b.values()), (a, b)
     for n, t in b[0][1].items():
         rel = float((a[0][1][n] - t).norm() / (t.norm() + 1e-8))
+        assert rel < 2e-2, (n, rel)
+
+
+def _ag_gemm_kernel(rank, world, cases):
+    """nfb_ag_gemm on every rank: the gathered flat buffer and Y = X @ W^T against torch."""
+    import ctypes
+
+    import torch.distributed as dist
+
+    from nuvla_forge_b200 import _native as nat
+    from nuvla_forge_b200.parallel.symm import SymmetricWorkspace
+
+    dev = torch.device("cuda", rank)
+    worst = []
+    for (prefix, M, N, K, tail) in cases:
+        numel = prefix + N * K + tail
+        numel += (-numel) % (8 * world)
+        shard = numel // world
+        g = torch.Generator(device=dev).manual_seed(7)         # same flat unit on every rank
+        flat = torch.randn(numel, generator=g, device=dev).to(torch.bfloat16)
+        x = torch.randn(M, K, generator=torch.Generator(device=dev).manual_seed(100 + rank), device=dev)
+        x = x.to(torch.bfloat16)
+        ws = SymmetricWorkspace(shard * 2 + 4096, device=dev, timeout_s=10)
+        off = ws.alloc(shard * 2)
+        nat.call("nfb_copy_async", ctypes.c_void_p(ws.local_ptr(off)),
+                 ctypes.c_void_p(flat[rank * shard:].data_ptr()), shard * 2, nat.stream(dev))
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        full = torch.zeros(numel, dtype=torch.bfloat16, device=dev)
+        full[:prefix].copy_(flat[:prefix])
+        y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        ready = torch.zeros(1024, dtype=torch.int32, device=dev)
+        for _ in range(2):   # twice in a row: the ready counters are re-zeroed per launch
+            nat.call("nfb_ag_gemm", ws.bases_ptr(), world, off, shard * 2, nat.ptr(full), prefix * 2, numel * 2,
+                     prefix * 2, N, K, nat.ptr(x), K, M, nat.ptr(y), N, nat.ptr(ready), nat.ptr(ws.status),
+                     nat.stream(dev))
+        torch.cuda.synchronize(dev)
+        ws.check()
+        assert torch.equal(full, flat), "gathered buffer differs"
+        w = flat[prefix: prefix + N * K].view(N, K).float()
+        ref = x.float() @ w.t()
+        worst.append(float((y.float() - ref).norm() / ref.norm()))
+        dist.barrier()
+        ws.close()
+    return worst
+
+
+def test_ag_gemm_kernel():
+    w = _world()
+    cases = [(64, 300, 600, 192, 5000), (1536, 1000, 2048, 1024, 70000), (8, 130, 4096, 256, 0)]
+    out = run_ranks(_ag_gemm_kernel, w, args=(cases,), backend="nccl", env=ENV, timeout_s=120, join_s=240)
+    for r, (st, val) in out.items():
+        assert st == "ok", (r, val)
+        assert max(val) < 1e-2, (r, val)
+
+
+def _fsdp_model(rank, world, fuse):
+    from nuvla_forge_b200.data import SampleSpec, SyntheticBatchSource
+    from nuvla_forge_b200.models import NuVLA, NuVLAConfig
+    from nuvla_forge_b200.parallel.fsdp import FullyShardedDataParallel
+
+    dev = torch.device("cuda", rank)
+    cfg = NuVLAConfig.preset("tiny")
+    torch.manual_seed(0)
+    model = NuVLA(cfg).to(dev)
+    fsdp = FullyShardedDataParallel(model, comm="fused", fuse_ag_gemm=fuse)
+    opt = fsdp.make_optimizer(lr=1e-3)
+    src = SyntheticBatchSource(SampleSpec.for_model(cfg), 2, seed=rank, pin=False)
+    losses = []
+    for step in range(3):
+        for m in range(2):
+            b = {k: v.to(dev) for k, v in src.batch(2 * step + m).items()}
+            ctx = fsdp.no_sync() if m == 0 else torch.enable_grad()
+            torch.manual_seed(10 * step + m)
+            with ctx:
+                out = fsdp(b["images"], b["trajectory"], b["text_tokens"], b["text_targets"])
+                (out["loss"] / 2).backward()
+            losses.append(float(out["loss"]))
+        opt.step()
+        opt.zero_grad()
+    torch.cuda.synchronize(dev)
+    fsdp.check_health()
+    views = fsdp.full_master_views()
+    params = {n: views[id(p)].cpu() for n, p in model.named_parameters()} if rank == 0 else None
+    return {"losses": losses, "fused_launches": fsdp.ag_fused_launches, "params": params}
+
+
+def test_fsdp_ag_gemm_matches_plain_gather():
+    w = _world()
+    a = run_ranks(_fsdp_model, w, args=(True,), backend="nccl", env=ENV, timeout_s=240, join_s=400)
+    b = run_ranks(_fsdp_model, w, args=(False,), backend="nccl", env=ENV, timeout_s=240, join_s=400)
+    assert all(st == "ok" for st, _ in a.values()) and all(st == "ok" for st, _ in b.values()), (a, b)
+    assert a[0][1]["fused_launches"] > 0 and b[0][1]["fused_launches"] == 0
+    for la, lb in zip(a[0][1]["losses"], b[0][1]["losses"]):
+        assert abs(la - lb) < 2e-2 * max(1.0, abs(lb)), (la, lb)
+    for n, t in b[0][1]["params"].items():
+        rel = float((a[0][1]["params"][n] - t).norm() / (t.norm() + 1e-8))
         assert rel < 2e-2, (n, rel)
