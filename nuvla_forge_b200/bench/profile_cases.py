@@ -127,6 +127,30 @@ def patchify(iters):
         patchify_images(img, 14)
 
 
+@case
+def ag_gemm(iters):
+    """All-gather-fused GEMM on one GPU (world 1: the gather copies the local shard):
+    a 64 MB parameter unit, first GEMM M=4096, N=5120, K=3072 (the 3b qkv shape)."""
+    import ctypes
+
+    from .. import _native as nat
+    numel = 32 * 2**20
+    prefix, M, N, K = 8192, 4096, 5120, 3072
+    shard = _bf(numel)
+    full = torch.empty(numel, dtype=torch.bfloat16, device="cuda")
+    x = _bf(M, K, seed=1)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    ready = torch.zeros(1024, dtype=torch.int32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    bases = (ctypes.c_uint64 * 1)(shard.data_ptr())
+    for _ in range(iters):
+        nat.call("nfb_ag_gemm", ctypes.cast(bases, ctypes.c_void_p), 1, 0, numel * 2, nat.ptr(full), prefix * 2,
+                 numel * 2, prefix * 2, N, K, nat.ptr(x), K, M, nat.ptr(y), N, nat.ptr(ready), nat.ptr(status),
+                 nat.stream())
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0, hex(int(status.item()))
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", required=True, choices=sorted(CASES))

@@ -62,6 +62,12 @@ class FlatAdamW:
 
     def step(self) -> None:
         self.step_count += 1
+        owner = getattr(self, "fused_owner", None)
+        if owner is not None and owner.take_fused_step():
+            # FSDP already applied this step inside each unit's reduce-scatter
+            if self.after_step is not None:
+                self.after_step()
+            return
         clip = self.max_grad_norm is not None and self.max_grad_norm > 0
         if clip:
             self.compute_norm2()

@@ -23,13 +23,21 @@ clipping:
   units use ``nfb_allgather`` (each rank pulls its peers' shards). Backward: a
   hook on the unit's outputs gathers it again (``nfb_allgather``) before its
   backward runs.
+* Overlap (fused comm): reduce-scatters run on a communication stream as
+  soon as a unit's gradients are complete, and while a unit's backward runs
+  the next unit's parameters are gathered on a prefetch stream (its own flag
+  slot, so the two streams' collectives never share an epoch sequence); the
+  compute stream waits for the prefetch only when it needs the unit, and for
+  the reduce-scatters only at the end of backward.
 * Gradients: bf16 gradients are folded into a per-unit fp32 accumulator
   (exact across micro-steps); when a unit's gradients are complete on a
   syncing micro-step they are cast to bf16 into peer-mapped memory and
   reduce-scattered by ``nfb_rs_push`` (one kernel: bf16 cast of the fp32
   accumulator pushed to each slice's owner over NVLink, reduction in fp32,
-  1/world scale, fp32 shard output), in a fixed unit order on every rank. With clipping off, the
-  fused ``nfb_rs_adamw`` applies AdamW to the shard inside the reduce-scatter.
+  1/world scale, fp32 shard output), in a fixed unit order on every rank. With clipping off
+  (``max_grad_norm`` <= 0), ``nfb_rs_adamw`` instead applies AdamW to the
+  shard inside the reduce-scatter (fp32 master, moments and the bf16 shard the
+  next all-gather reads), and the optimizer step has nothing left to do.
 * The gradient norm for clipping is global: shard norms^2 are summed over ranks
   on the device (``nfb_allreduce_scalar``) before the update.
 
@@ -48,7 +56,7 @@ import torch.distributed as dist
 from torch import nn
 
 from .. import _native as nat
-from .symm import SLOT_AG, SLOT_RS, SLOT_SCALAR, SymmetricWorkspace, symmetric_memory_available
+from .symm import SLOT_AG, SLOT_AG_PREFETCH, SLOT_RS, SLOT_SCALAR, SymmetricWorkspace, symmetric_memory_available
 
 
 def _round(n: int, a: int) -> int:
@@ -85,12 +93,14 @@ class _Unit:
     prefix: int = 0            # elements of the leading 1-D parameters (copied ahead of a fused gather)
     ag_ok: bool = False        # the unit's first parameter consumer is a linear layer (fused gather allowed)
     ag_pending: bool = False   # storage allocated, prefix copied, the rest awaits the fused GEMM
+    ready_event: object = None # prefetch all-gather in flight on the prefetch stream
 
 
 class FullyShardedDataParallel(nn.Module):
     def __init__(self, module: nn.Module, param_dtype: torch.dtype | None = None, comm: str = "auto",
                  unit_types: tuple | None = None, reshard_after_forward: bool = True, ctas: int = 32,
-                 process_group: dist.ProcessGroup | None = None, fuse_ag_gemm: bool | None = None):
+                 process_group: dist.ProcessGroup | None = None, fuse_ag_gemm: bool | None = None,
+                 fuse_rs_adamw: bool = True):
         super().__init__()
         self.module = module
         dev = next(module.parameters()).device
@@ -126,8 +136,15 @@ class FullyShardedDataParallel(nn.Module):
             # blocks whose first parameter use is a linear layer (after 1-D norm weights / biases)
             u.ag_ok = self.fuse_ag_gemm and isinstance(u.module, (TransformerBlock, DiTBlock))
         self._ag_unit: _Unit | None = None
+        self.comm_stream = self.ag_stream = None
+        if comm == "fused":
+            self.comm_stream = torch.cuda.Stream(device=dev)
+            self.ag_stream = torch.cuda.Stream(device=dev)
         self._ag_ready = torch.zeros(1024, dtype=torch.int32, device=dev) if self.fuse_ag_gemm else None
         self.ag_fused_launches = 0
+        self.fuse_rs_adamw = bool(fuse_rs_adamw and comm == "fused")
+        self._opt = None
+        self._fused_updates = 0
         self.shard_numel = sum(u.shard for u in self.units)
         self.master = torch.zeros(self.shard_numel, dtype=torch.float32, device=dev)
         self.grads = torch.zeros(self.shard_numel, dtype=torch.float32, device=dev)
@@ -232,8 +249,39 @@ class FullyShardedDataParallel(nn.Module):
             self.param_shards.copy_(self.master.to(self.param_dtype))
 
     # ------------------------------------------------------------ gather / reshard
+    def _ensure_ready(self, u: _Unit) -> None:
+        """Make the compute stream wait for a prefetch all-gather of ``u`` still in flight."""
+        if u.ready_event is not None:
+            main = torch.cuda.current_stream(self.device)
+            if self.comm_timer is not None:   # time the compute stream stalls on the prefetch
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(main)
+                main.wait_event(u.ready_event)
+                e1.record(main)
+                self.comm_timer.bracket(e0, e1)
+            else:
+                main.wait_event(u.ready_event)
+            u.ready_event = None
+
+    def _prefetch(self, u: _Unit) -> None:
+        """Gather ``u`` on the prefetch stream (fused comm only)."""
+        if u.gathered or self.comm != "fused" or u is self.root:
+            return
+        st = u.full.untyped_storage()
+        nbytes = u.numel * u.full.element_size()
+        if st.nbytes() != nbytes:
+            st.resize_(nbytes)
+        # the new storage may reuse memory the compute stream used until now
+        self.ag_stream.wait_stream(torch.cuda.current_stream(self.device))
+        self._launch_allgather(u, stream=self.ag_stream, slot=SLOT_AG_PREFETCH, barrier=False)
+        ev = torch.cuda.Event()
+        ev.record(self.ag_stream)
+        u.ready_event = ev
+        u.gathered = True
+
     def _gather(self, u: _Unit, lazy: bool = False) -> None:
         if u.gathered:
+            self._ensure_ready(u)
             return
         st = u.full.untyped_storage()
         nbytes = u.numel * u.full.element_size()
@@ -247,15 +295,36 @@ class FullyShardedDataParallel(nn.Module):
             from ..models import layers
             layers.set_pending_consumer(self._consume_linear)
             return
-        self._launch_allgather(u)
+        # the root unit's gather opens each step's forward and carries the rank barrier
+        self._launch_allgather(u, barrier=u is self.root)
         u.gathered = True
 
-    def _launch_allgather(self, u: _Unit) -> None:
+    def _launch_allgather(self, u: _Unit, stream: torch.cuda.Stream | None = None, slot: int = SLOT_AG,
+                          barrier: bool = True) -> None:
+        """Gather ``u`` into ``u.full``.
+
+        Fused comm: with ``barrier`` the ``nfb_allgather`` kernel (rank barriers before and after the
+        copy). Without it, one copy-engine transfer per shard and no SM use: valid for every gather
+        after the first one of an optimizer step (the root unit's, which has the barrier), because
+        a rank changes its shards only in its optimizer step or, with AdamW fused into the
+        reduce-scatter, in the unit's reduce-scatter, whose own barrier every peer reaches only
+        after its last gather of that unit.
+        """
+        if self.comm == "fused" and not barrier:
+            sh = ctypes.c_void_p(stream.cuda_stream) if stream is not None else nat.stream(self.device)
+            S = u.shard * 2
+            src = self.param_off + u.shard_start * 2
+            for i in range(self.world):
+                q = (self.rank + i) % self.world
+                nat.call("nfb_copy_async", ctypes.c_void_p(u.full.data_ptr() + q * S),
+                         ctypes.c_void_p(self.ws.bases[q] + src), S, sh)
+            return
         if self.comm == "fused":
             ws = self.ws
+            sh = ctypes.c_void_p(stream.cuda_stream) if stream is not None else nat.stream(self.device)
             nat.call("nfb_allgather", ws.bases_ptr(), ws.rank, ws.world, u.shard,
-                     self.param_off + u.shard_start * 2, nat.ptr(u.full), ws.flag_off, SLOT_AG,
-                     ws.next_epoch(SLOT_AG), ws.timeout_ns, nat.ptr(ws.status), self.ctas, nat.stream(self.device))
+                     self.param_off + u.shard_start * 2, nat.ptr(u.full), ws.flag_off, slot,
+                     ws.next_epoch(slot), ws.timeout_ns, nat.ptr(ws.status), self.ctas, sh)
         elif self.comm == "nccl":
             dist.all_gather_into_tensor(u.full, self.param_shards[u.shard_start: u.shard_start + u.shard],
                                         group=self.group)
@@ -301,7 +370,7 @@ class FullyShardedDataParallel(nn.Module):
                 and K % 8 == 0 and x.numel() > 0 and off % 16 == 0
                 and (w.shape[0] + 255) // 256 <= self._ag_ready.numel())
         if not fits:
-            self._launch_allgather(u)
+            self._launch_allgather(u, barrier=False)
             return None
         y = _AgLinear.apply(x, w, self, u)
         return y if b is None else y + b
@@ -319,6 +388,7 @@ class FullyShardedDataParallel(nn.Module):
     def _reshard(self, u: _Unit) -> None:
         if not u.gathered or u is self.root:
             return
+        self._ensure_ready(u)   # no prefetch may still be writing the storage being released
         u.full.untyped_storage().resize_(0)
         u.gathered = False
 
@@ -363,6 +433,10 @@ class FullyShardedDataParallel(nn.Module):
         if not u.bwd_gathered:
             u.bwd_gathered = True
             self._gather(u)
+            # the unit whose backward runs next (the previous one in forward order)
+            i = self._order.index(u) if u in self._order else -1
+            if i > 0 and not self._order[i - 1].bwd_gathered:
+                self._prefetch(self._order[i - 1])
 
     def _grad_hook(self, p: nn.Parameter) -> None:
         if not self._callback_queued:
@@ -399,12 +473,30 @@ class FullyShardedDataParallel(nn.Module):
             u.acc32.zero_()      # no gradient reached this unit in the window
         out = self.grads[u.shard_start: u.shard_start + u.shard]
         scale = 1.0 / self.world
-        if self.comm == "fused":
+        if self.comm == "fused" and self._rs_adamw_active():
+            ws, opt = self.ws, self._opt
+            cs = self.comm_stream
+            cs.wait_stream(torch.cuda.current_stream(self.device))
+            hs = ctypes.c_void_p(cs.cuda_stream)
+            # bf16 gradient into this rank's send region, then one kernel per unit: every rank pulls its slice
+            # from all peers, reduces, scales and applies AdamW to its fp32 master / moments / bf16 shard
+            nat.call("nfb_cast", 0, 1, ctypes.c_void_p(ws.local_ptr(u.grad_off)), nat.ptr(u.acc32), u.numel, 1.0, hs)
+            lo, hi = u.shard_start, u.shard_start + u.shard
+            b1, b2 = opt.betas
+            nat.call("nfb_rs_adamw", ws.bases_ptr(), ws.rank, ws.world, u.shard, u.grad_off, ws.flag_off, SLOT_RS,
+                     scale, ws.next_epoch(SLOT_RS), ws.timeout_ns, nat.ptr(ws.status), nat.ptr(self.master[lo:hi]),
+                     nat.ptr(opt.m[lo:hi]), nat.ptr(opt.v[lo:hi]), self.param_off + u.shard_start * 2, opt.lr, b1, b2,
+                     opt.eps, opt.weight_decay, opt.step_count + 1, 1.0, 1, self.ctas, hs)
+            self._fused_updates += 1
+        elif self.comm == "fused":
             ws = self.ws
+            # on the communication stream, after the unit's gradients are complete on the compute stream
+            cs = self.comm_stream
+            cs.wait_stream(torch.cuda.current_stream(self.device))
             # one kernel: bf16 cast of the fp32 accumulator, pushed to the slice owners, reduced into the shard
             nat.call("nfb_rs_push", ws.bases_ptr(), ws.rank, ws.world, nat.ptr(u.acc32), u.numel, u.grad_off,
                      ws.flag_off, SLOT_RS, scale, ws.next_epoch(SLOT_RS), ws.timeout_ns, nat.ptr(ws.status),
-                     nat.ptr(out), int(not self._shard_fresh), self.ctas, nat.stream(self.device))
+                     nat.ptr(out), int(not self._shard_fresh), self.ctas, ctypes.c_void_p(cs.cuda_stream))
         elif self.comm == "nccl":
             red = torch.empty(u.shard, dtype=torch.bfloat16, device=self.device)
             dist.reduce_scatter_tensor(red, u.acc32.to(torch.bfloat16), group=self.group)
@@ -436,6 +528,17 @@ class FullyShardedDataParallel(nn.Module):
                 u.ready = True
             self._launch_ready()
             self._shard_fresh = False
+        if self.comm_stream is not None:
+            # the optimizer and the next window's accumulation wait for every reduce-scatter
+            main = torch.cuda.current_stream(self.device)
+            if self.comm_timer is not None and self.require_sync:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(main)
+                main.wait_stream(self.comm_stream)
+                e1.record(main)
+                self.comm_timer.bracket(e0, e1)
+            else:
+                main.wait_stream(self.comm_stream)
         for u in self.units:
             u.pending = len(u.segs)
             u.ready = False
@@ -481,10 +584,27 @@ class FullyShardedDataParallel(nn.Module):
         from ..optim.adamw import FlatAdamW
 
         ptr = self.ws.local_ptr(self.param_off) if self.comm == "fused" else None
-        return FlatAdamW(self, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay, max_grad_norm=max_grad_norm,
-                         ddp=self, grads=self.grads, master=self.master,
-                         params=None if ptr is not None else self.param_shards, params_ptr=ptr,
-                         norm_allreduce=self._norm_allreduce, after_step=self._after_step)
+        opt = FlatAdamW(self, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay, max_grad_norm=max_grad_norm,
+                        ddp=self, grads=self.grads, master=self.master,
+                        params=None if ptr is not None else self.param_shards, params_ptr=ptr,
+                        norm_allreduce=self._norm_allreduce, after_step=self._after_step)
+        self._opt = opt
+        opt.fused_owner = self
+        return opt
+
+    def _rs_adamw_active(self) -> bool:
+        opt = self._opt
+        return (self.fuse_rs_adamw and opt is not None and self.require_sync
+                and not (opt.max_grad_norm is not None and opt.max_grad_norm > 0))
+
+    def take_fused_step(self) -> bool:
+        """True when every unit's AdamW update already ran inside its reduce-scatter this window."""
+        n, self._fused_updates = self._fused_updates, 0
+        if n == 0:
+            return False
+        if n != len(self.units):
+            raise RuntimeError(f"fused reduce-scatter + AdamW updated {n} of {len(self.units)} units")
+        return True
 
     def check_health(self) -> None:
         if self.ws is not None:

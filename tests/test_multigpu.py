@@ -220,7 +220,7 @@ def test_ag_gemm_kernel():
         assert max(val) < 1e-2, (r, val)
 
 
-def _fsdp_model(rank, world, fuse):
+def _fsdp_model(rank, world, fuse, fuse_rs=True, clip=1.0):
     from nuvla_forge_b200.data import SampleSpec, SyntheticBatchSource
     from nuvla_forge_b200.models import NuVLA, NuVLAConfig
     from nuvla_forge_b200.parallel.fsdp import FullyShardedDataParallel
@@ -229,8 +229,8 @@ def _fsdp_model(rank, world, fuse):
     cfg = NuVLAConfig.preset("tiny")
     torch.manual_seed(0)
     model = NuVLA(cfg).to(dev)
-    fsdp = FullyShardedDataParallel(model, comm="fused", fuse_ag_gemm=fuse)
-    opt = fsdp.make_optimizer(lr=1e-3)
+    fsdp = FullyShardedDataParallel(model, comm="fused", fuse_ag_gemm=fuse, fuse_rs_adamw=fuse_rs)
+    opt = fsdp.make_optimizer(lr=1e-3, max_grad_norm=clip)
     src = SyntheticBatchSource(SampleSpec.for_model(cfg), 2, seed=rank, pin=False)
     losses = []
     for step in range(3):
@@ -241,14 +241,15 @@ def _fsdp_model(rank, world, fuse):
             with ctx:
                 out = fsdp(b["images"], b["trajectory"], b["text_tokens"], b["text_targets"])
                 (out["loss"] / 2).backward()
-            losses.append(float(out["loss"]))
+            losses.append(float(out["loss"].detach()))
         opt.step()
         opt.zero_grad()
     torch.cuda.synchronize(dev)
     fsdp.check_health()
     views = fsdp.full_master_views()
     params = {n: views[id(p)].cpu() for n, p in model.named_parameters()} if rank == 0 else None
-    return {"losses": losses, "fused_launches": fsdp.ag_fused_launches, "params": params}
+    return {"losses": losses, "fused_launches": fsdp.ag_fused_launches, "params": params,
+            "streams": fsdp.comm_stream is not None}
 
 
 def test_fsdp_ag_gemm_matches_plain_gather():
@@ -260,5 +261,20 @@ def test_fsdp_ag_gemm_matches_plain_gather():
     for la, lb in zip(a[0][1]["losses"], b[0][1]["losses"]):
         assert abs(la - lb) < 2e-2 * max(1.0, abs(lb)), (la, lb)
     for n, t in b[0][1]["params"].items():
+        rel = float((a[0][1]["params"][n] - t).norm() / (t.norm() + 1e-8))
+        assert rel < 2e-2, (n, rel)
+
+
+def test_fsdp_rs_adamw_matches_unfused():
+    """Clipping off: AdamW inside each unit's reduce-scatter == reduce-scatter then one flat AdamW."""
+    w = _world()
+    a = run_ranks(_fsdp_model, w, args=(True, True, 0.0), backend="nccl", env=ENV, timeout_s=240, join_s=400)
+    b = run_ranks(_fsdp_model, w, args=(True, False, 0.0), backend="nccl", env=ENV, timeout_s=240, join_s=400)
+    assert all(st == "ok" for st, _ in a.values()) and all(st == "ok" for st, _ in b.values()), (a, b)
+    for la, lb in zip(a[0][1]["losses"], b[0][1]["losses"]):
+        assert abs(la - lb) < 1e-2 * max(1.0, abs(lb)), (la, lb)
+    for n, t in b[0][1]["params"].items():
+        # tiny run-to-run differences (attention backward) are amplified by Adam's normalised update in
+        # near-zero tensors such as the zero-initialised adaLN projections; most tensors agree to 1e-3
         rel = float((a[0][1]["params"][n] - t).norm() / (t.norm() + 1e-8))
         assert rel < 2e-2, (n, rel)
