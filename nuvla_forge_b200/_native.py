@@ -60,11 +60,12 @@ _SIGS: dict[str, tuple] = {
     "nfb_ce_rows": (I, [I, P, L, P, L, L, L, P, P, P]),
     "nfb_count_valid": (I, [P, L, L, P, P]),
     "nfb_tc_gemm_bf16": (I, [P, P, P, I, I, I, L, L, L, I, P, P]),
+    "nfb_tc_gemm_ex": (I, [P, P, P, I, I, I, L, L, L, I, I, I, I, P, P]),
     "nfb_ce_tc_tiles": (I, [I]),
     "nfb_ce_tc_stats": (I, [P, L, P, L, P, I, I, I, P, P, P, P, P]),
     "nfb_ce_tc_merge": (I, [P, P, P, P, P, I, I, L, P, P, P]),
     "nfb_ce_tc_grad": (I, [P, L, P, L, P, P, P, L, I, I, I, P, L, P, P]),
-    "nfb_ag_gemm": (I, [P, I, L, L, P, L, L, L, I, I, P, L, I, P, L, P, P, P]),
+    "nfb_ag_gemm": (I, [P, I, I, L, L, P, L, L, L, I, I, P, L, I, P, L, P, P, P]),
     "nfb_ag_gemm_max_nblocks": (I, []),
     "nfb_copy_async": (I, [P, P, L, P]),
 }

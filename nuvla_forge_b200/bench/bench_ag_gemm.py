@@ -12,6 +12,7 @@ ranks, L2 flushed between iterations):
 
 * fused:    ``nfb_ag_gemm`` (gather of the whole unit + the GEMM, one kernel)
 * separate: ``nfb_allgather`` of the unit, then the same GEMM by cuBLAS
+* separate_ce: the unit gathered by the copy engines (one peer copy per shard), then cuBLAS
 * gemm:     the GEMM alone (cuBLAS, weights already local)
 
 Roofline of the fused kernel = max(GEMM FLOPs / measured bf16 peak, bytes
@@ -79,6 +80,8 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default=None)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--orders", default="", help="comma-separated NFB_AG_ORDER values to time the fused kernel "
+                                                 "with (gather chunk orders, csrc/ag_gemm.cu); default: the built-in")
     args = ap.parse_args(argv)
     info = setup_distributed()
     rank, world, dev = info.rank, info.world, info.device
@@ -106,7 +109,7 @@ def main(argv=None):
         s = nat.stream(dev)
 
         def fused():
-            nat.call("nfb_ag_gemm", ws.bases_ptr(), world, off, shard * 2, nat.ptr(full), pre * 2, numel * 2,
+            nat.call("nfb_ag_gemm", ws.bases_ptr(), rank, world, off, shard * 2, nat.ptr(full), pre * 2, numel * 2,
                      pre * 2, N, K, nat.ptr(x), K, M, nat.ptr(y), N, nat.ptr(ready), nat.ptr(ws.status), s)
 
         w = full[pre: pre + N * K].view(N, K)
@@ -122,10 +125,25 @@ def main(argv=None):
         def gemm():
             torch.matmul(x, w.t(), out=y)
 
+        def separate_ce():
+            for i in range(world):
+                q = (rank + i) % world
+                nat.call("nfb_copy_async", ctypes.c_void_p(full.data_ptr() + q * shard * 2),
+                         ctypes.c_void_p(ws.bases[q] + off), shard * 2, s)
+            torch.matmul(x, w.t(), out=y)
+
         r = dict(c, world=world)
+        import os
+        for o in [x for x in args.orders.split(",") if x]:
+            os.environ["NFB_AG_ORDER"] = o
+            r[f"fused_order{o}_ms"] = _timed(fused, args.iters, dev, flush)
+            if rank == 0:
+                print(f"  {c['case']:<26} order {o}: fused {r[f'fused_order{o}_ms']:.3f} ms")
+        os.environ.pop("NFB_AG_ORDER", None)
         r["fused_ms"] = _timed(fused, args.iters, dev, flush)
         ws.check()
         r["separate_ms"] = _timed(separate, args.iters, dev, flush)
+        r["separate_ce_ms"] = _timed(separate_ce, args.iters, dev, flush)
         r["gemm_ms"] = _timed(gemm, args.iters, dev, flush)
         r["allgather_ms"] = _timed(allgather, args.iters, dev, flush)
         ws.check()
@@ -141,6 +159,7 @@ def main(argv=None):
         if rank == 0:
             print(f"{c['case']:<26} M{M} N{N} K{K} unit {numel * 2 / 2**20:7.1f} MiB | fused {r['fused_ms']:.3f} ms"
                   f" | separate {r['separate_ms']:.3f} (AG {r['allgather_ms']:.3f} + GEMM {r['gemm_ms']:.3f})"
+                  f" | copy-engine AG + GEMM {r['separate_ce_ms']:.3f}"
                   f" | roofline {r['roofline_ms']:.3f} ({r['roofline_bound']}) = {100 * r['frac_of_roofline']:.0f}%")
         dist.barrier()
         ws.close()

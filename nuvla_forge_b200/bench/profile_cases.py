@@ -144,7 +144,7 @@ def ag_gemm(iters):
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     bases = (ctypes.c_uint64 * 1)(shard.data_ptr())
     for _ in range(iters):
-        nat.call("nfb_ag_gemm", ctypes.cast(bases, ctypes.c_void_p), 1, 0, numel * 2, nat.ptr(full), prefix * 2,
+        nat.call("nfb_ag_gemm", ctypes.cast(bases, ctypes.c_void_p), 0, 1, 0, numel * 2, nat.ptr(full), prefix * 2,
                  numel * 2, prefix * 2, N, K, nat.ptr(x), K, M, nat.ptr(y), N, nat.ptr(ready), nat.ptr(status),
                  nat.stream())
     torch.cuda.synchronize()

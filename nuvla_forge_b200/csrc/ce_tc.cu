@@ -24,31 +24,40 @@
 namespace nfb {
 namespace tc {
 
-template <class Epi>
+template <class Epi, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1) tc_kernel(const __grid_constant__ CUtensorMap ta,
                                                         const __grid_constant__ CUtensorMap tb, GemmShape sh,
                                                         Epi epi, uint32_t* status) {
   Epi e = epi;
   NoGate g;
-  gemm_body(&ta, &tb, sh, e, status, g);
+  gemm_body<A_MN, B_MN>(&ta, &tb, sh, e, status, g);
+}
+
+// A K-major operand [rows, K] is read in boxes of 64 K x box_rows rows; an MN-major one, stored
+// [K, rows] with rows contiguous, in boxes of 64 rows x BK K (the core loads box_rows / 64 of them).
+template <class Epi, bool A_MN, bool B_MN>
+static int launch_t(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const Epi& epi,
+                    uint32_t* status, cudaStream_t st) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  CUtensorMap ta, tb;
+  int rc = A_MN ? make_tmap(&ta, A, K, M, lda, BK) : make_tmap(&ta, A, M, K, lda, BM);
+  if (rc) return rc;
+  rc = B_MN ? make_tmap(&tb, B, K, N, ldb, BK) : make_tmap(&tb, B, N, K, ldb, BN);
+  if (rc) return rc;
+  GemmShape sh = make_shape(M, N, K);
+  cudaError_t e = cudaFuncSetAttribute(tc_kernel<Epi, A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kSmemBytes);
+  if (e != cudaSuccess) return (int)e;
+  const int tiles = sh.m_tiles * sh.n_tiles;
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  tc_kernel<Epi, A_MN, B_MN><<<grid, kThreads, kSmemBytes, st>>>(ta, tb, sh, epi, status);
+  return (int)cudaGetLastError();
 }
 
 template <class Epi>
 static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K, const Epi& epi,
                   uint32_t* status, cudaStream_t st) {
-  if (M <= 0 || N <= 0 || K <= 0) return 0;
-  CUtensorMap ta, tb;
-  int rc = make_tmap(&ta, A, M, K, lda, BM);
-  if (rc) return rc;
-  rc = make_tmap(&tb, B, N, K, ldb, BN);
-  if (rc) return rc;
-  GemmShape sh = make_shape(M, N, K);
-  cudaError_t e = cudaFuncSetAttribute(tc_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
-  if (e != cudaSuccess) return (int)e;
-  const int tiles = sh.m_tiles * sh.n_tiles;
-  const int grid = tiles < sm_count() ? tiles : sm_count();
-  tc_kernel<Epi><<<grid, kThreads, kSmemBytes, st>>>(ta, tb, sh, epi, status);
-  return (int)cudaGetLastError();
+  return launch_t<Epi, false, false>(A, lda, B, ldb, M, N, K, epi, status, st);
 }
 
 // ---------------------------------------------------------------------------
@@ -163,13 +172,26 @@ using namespace nfb;
 using namespace nfb::tc;
 
 // C[M, N] = A[M, K] @ B[N, K]^T, A/B bf16 with row strides lda/ldb; C bf16 (out_f32=0) or fp32.
-NFB_API int nfb_tc_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, int64_t lda, int64_t ldb,
-                             int64_t ldc, int out_f32, uint32_t* status, void* stream) {
-  StoreEpi epi;
-  epi.C = C; epi.ldc = ldc; epi.out_f32 = out_f32;
+// C[M, N] (=|+=) A B^T with A K-major [M, K] (a_mn = 0) or MN-major [K, M] (a_mn = 1), B K-major [N, K]
+// or MN-major [K, N]; C bf16 or fp32 (out_f32), accumulate (fp32 only) adds into C.
+NFB_API int nfb_tc_gemm_ex(const void* A, const void* B, void* C, int M, int N, int K, int64_t lda, int64_t ldb,
+                           int64_t ldc, int out_f32, int a_mn, int b_mn, int accumulate, uint32_t* status,
+                           void* stream) {
+  if (accumulate && !out_f32) return (int)cudaErrorInvalidValue;
+  StoreEpi epi{};
+  epi.C = C; epi.ldc = ldc; epi.out_f32 = out_f32; epi.accumulate = accumulate;
   const int es = out_f32 ? 4 : 2;
   epi.vec_ok = ((reinterpret_cast<uintptr_t>(C) & 15) == 0) && ((ldc * es) % 16 == 0);
-  return launch(A, lda, B, ldb, M, N, K, epi, status, (cudaStream_t)stream);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (a_mn && b_mn) return launch_t<StoreEpi, true, true>(A, lda, B, ldb, M, N, K, epi, status, st);
+  if (a_mn) return launch_t<StoreEpi, true, false>(A, lda, B, ldb, M, N, K, epi, status, st);
+  if (b_mn) return launch_t<StoreEpi, false, true>(A, lda, B, ldb, M, N, K, epi, status, st);
+  return launch_t<StoreEpi, false, false>(A, lda, B, ldb, M, N, K, epi, status, st);
+}
+
+NFB_API int nfb_tc_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, int64_t lda, int64_t ldb,
+                             int64_t ldc, int out_f32, uint32_t* status, void* stream) {
+  return nfb_tc_gemm_ex(A, B, C, M, N, K, lda, ldb, ldc, out_f32, 0, 0, 0, status, stream);
 }
 
 NFB_API int nfb_ce_tc_tiles(int V) { return (V + BN - 1) / BN; }

@@ -1,6 +1,10 @@
 // Blackwell (sm_100a) tensor-core GEMM core: TMA + mbarrier pipeline + tcgen05.mma + TMEM.
 //
-//   C[m, n] = sum_k A[m, k] * B[n, k]          A: [M, K] bf16, B: [N, K] bf16, both K-contiguous
+//   C[m, n] = sum_k A[m, k] * B[n, k]          A: [M, K] bf16, B: [N, K] bf16
+//
+// Each operand is either K-major (rows of K contiguous: A stored [M, K], B [N, K]) or MN-major
+// (A stored as [K, M] with M contiguous, B as [K, N]), chosen at compile time; an MN-major tile
+// is loaded as 64-column TMA boxes and described to tcgen05.mma with its transpose bit.
 //
 // One persistent CTA per SM, 6 warps with fixed roles:
 //   warp 0      TMA producer: one elected lane streams 128x64 A tiles and 256x64 B tiles
@@ -137,9 +141,25 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor: kind::f16, A/B bf16, D fp32, both K-major, M x N.
-__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+// Shared-memory matrix descriptor for an MN-major tile written by TMA as boxes of
+// [BK rows of K] x [64 MN columns] (128-byte rows, 128-byte swizzle): 8-row K
+// groups 1024 bytes apart (stride byte offset), 64-column MN blocks one box
+// (BK * 128 bytes) apart (leading byte offset).
+__device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFF) >> 4);          // start address
+  d |= (uint64_t)((BK * 128) >> 4) << 16;           // leading byte offset: next 64-column MN block
+  d |= (uint64_t)(1024 >> 4) << 32;                 // stride byte offset: next 8 K rows
+  d |= (uint64_t)1 << 46;                           // descriptor version (sm100)
+  d |= (uint64_t)2 << 61;                           // layout: 128-byte swizzle
+  return d;
+}
+
+// Instruction descriptor: kind::f16, A/B bf16, D fp32, M x N; bit 15 / 16 mark an
+// MN-major ("transposed") A / B.
+__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n, bool a_mn = false, bool b_mn = false) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -207,7 +227,8 @@ struct StoreEpi {
   void* C;
   int64_t ldc;
   int out_f32;
-  int vec_ok;  // rows 16-byte aligned
+  int vec_ok;      // rows 16-byte aligned
+  int accumulate;  // fp32 output only: C += A B^T
 
   __device__ void row(int m0, int n0, int r, uint32_t taddr, const GemmShape& sh) {
     const int m = m0 + r;
@@ -219,7 +240,18 @@ struct StoreEpi {
       const int n = n0 + c;
       if (out_f32) {
         float* dst = reinterpret_cast<float*>(C) + (int64_t)m * ldc + n;
-        if (vec_ok && n + 32 <= sh.N) {
+        if (accumulate) {
+          if (vec_ok && n + 32 <= sh.N) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              const float4 o = *reinterpret_cast<const float4*>(dst + j);
+              *reinterpret_cast<float4*>(dst + j) = make_float4(o.x + v[j], o.y + v[j + 1], o.z + v[j + 2], o.w + v[j + 3]);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) if (n + j < sh.N) dst[j] += v[j];
+          }
+        } else if (vec_ok && n + 32 <= sh.N) {
 #pragma unroll
           for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
         } else {
@@ -244,7 +276,7 @@ struct StoreEpi {
 //   __device__ void row(int tile_m0, int tile_n0, int row_in_tile, uint32_t tmem_row_addr, const GemmShape&)
 // which reads the 256 accumulator columns of its row (tmem_ld32 at tmem_row_addr + c)
 // and consumes them.
-template <class Epi, class Gate = NoGate>
+template <bool A_MN, bool B_MN, class Epi, class Gate>
 __device__ void gemm_body(const CUtensorMap* tma_a, const CUtensorMap* tma_b, const GemmShape& sh, Epi& epi,
                           uint32_t* status, Gate& gate) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -299,8 +331,20 @@ __device__ void gemm_body(const CUtensorMap* tma_a, const CUtensorMap* tma_b, co
           uint8_t* sa = smem + (size_t)stage * kStageBytes;
           uint8_t* sb = sa + kATileBytes;
           mbar_arrive_expect_tx(&S->full[stage], kStageBytes);
-          tma_load_2d(sa, tma_a, &S->full[stage], kb * BK, tc.m_blk * BM);
-          tma_load_2d(sb, tma_b, &S->full[stage], kb * BK, tc.n_blk * BN);
+          if (A_MN) {
+#pragma unroll
+            for (int h = 0; h < BM / 64; ++h)
+              tma_load_2d(sa + h * (BK * 128), tma_a, &S->full[stage], tc.m_blk * BM + 64 * h, kb * BK);
+          } else {
+            tma_load_2d(sa, tma_a, &S->full[stage], kb * BK, tc.m_blk * BM);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int h = 0; h < BN / 64; ++h)
+              tma_load_2d(sb + h * (BK * 128), tma_b, &S->full[stage], tc.n_blk * BN + 64 * h, kb * BK);
+          } else {
+            tma_load_2d(sb, tma_b, &S->full[stage], kb * BK, tc.n_blk * BN);
+          }
           ++issued;
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
@@ -322,7 +366,7 @@ __device__ void gemm_body(const CUtensorMap* tma_a, const CUtensorMap* tma_b, co
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc = idesc_bf16(BM, BN);
+      const uint32_t idesc = idesc_bf16(BM, BN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -339,8 +383,11 @@ __device__ void gemm_body(const CUtensorMap* tma_a, const CUtensorMap* tma_b, co
           const uint32_t sb = sa + kATileBytes;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            umma_bf16(tmem_d, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc,
-                      (kb > 0 || kk > 0) ? 1u : 0u);
+            // K-major: the next 16 K columns are 32 bytes further along each row;
+            // MN-major: they are the next 16 rows of 128 bytes
+            const uint64_t ad = A_MN ? sw128_mn_desc(sa + kk * 16 * 128) : sw128_desc(sa + kk * 32);
+            const uint64_t bd = B_MN ? sw128_mn_desc(sb + kk * 16 * 128) : sw128_desc(sb + kk * 32);
+            umma_bf16(tmem_d, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&S->empty[stage]);   // frees this stage once the MMAs above are done
           if (++stage == kStages) { stage = 0; phase ^= 1u; }

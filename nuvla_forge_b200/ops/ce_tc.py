@@ -4,7 +4,9 @@ The [M, V] logits live only in tensor memory: pass 1 turns each 128x256 logit
 tile into per-row online-softmax partials, a merge kernel produces the
 log-sum-exp and the per-row losses, and pass 2 recomputes the tile and writes
 ``(softmax - onehot) / count`` in bf16 for one row chunk at a time, which the
-two gradient GEMMs (cuBLAS) consume. Like the reference
+two gradient GEMMs consume on the same tcgen05 core (d_hidden = dl @ W with W
+read MN-major; d_W += dl^T @ h with both operands MN-major, accumulated in
+fp32; ``NFB_CE_TC_GRAD_GEMM=0`` hands them to cuBLAS instead). Like the reference
 (nuvla_forge/kernels/chunked_ce.py:120-182) the gradients are produced during
 forward and backward only scales them; unlike it, no fp32 logit tile exists and
 nothing synchronises the host.
@@ -38,14 +40,28 @@ def check_status(device: torch.device | None = None) -> None:
             raise RuntimeError(f"tcgen05 pipeline on cuda:{idx} gave up waiting (status {v:#x})")
 
 
-def tc_gemm(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
-    """C = a @ b.T on the native tcgen05 core (a [M,K], b [N,K] bf16, K % 8 == 0)."""
-    M, K = a.shape
-    N = b.shape[0]
-    c = torch.empty((M, N), dtype=out_dtype, device=a.device)
-    nat.call("nfb_tc_gemm_bf16", nat.ptr(a), nat.ptr(b), nat.ptr(c), M, N, K, a.stride(0), b.stride(0), c.stride(0),
-             int(out_dtype == torch.float32), nat.ptr(status_word(a.device)), nat.stream(a.device))
-    return c
+def tc_gemm(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.bfloat16, a_mn: bool = False, b_mn: bool = False,
+            out: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
+    """C = A @ B.T on the native tcgen05 core (bf16 operands, fp32 accumulation).
+
+    ``a`` is A [M, K] (K contiguous), or with ``a_mn`` A stored transposed as [K, M];
+    ``b`` is B [N, K], or with ``b_mn`` B stored as [K, N]. Rows must be 16-byte aligned
+    (contiguous dimension a multiple of 8). ``out`` (optional, row-major, may be a row slice)
+    receives C; ``accumulate`` adds into an fp32 ``out``.
+    """
+    M, K = (a.shape[1], a.shape[0]) if a_mn else a.shape
+    N = b.shape[1] if b_mn else b.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    nat.call("nfb_tc_gemm_ex", nat.ptr(a), nat.ptr(b), nat.ptr(out), M, N, K, a.stride(0), b.stride(0),
+             out.stride(0), int(out.dtype == torch.float32), int(a_mn), int(b_mn), int(accumulate),
+             nat.ptr(status_word(a.device)), nat.stream(a.device))
+    return out
+
+
+def _native_grad_gemms(V: int, H: int, dtype: torch.dtype) -> bool:
+    return (os.environ.get("NFB_CE_TC_GRAD_GEMM", "1") != "0" and dtype == torch.bfloat16
+            and V % 8 == 0 and H % 8 == 0)
 
 
 class _CrossEntropyTC(torch.autograd.Function):
@@ -74,6 +90,7 @@ class _CrossEntropyTC(torch.autograd.Function):
                  ignore_index, nat.ptr(lse), nat.ptr(loss_rows), s)
         d_hidden = torch.empty((M, H), dtype=hidden.dtype, device=dev)
         d_weight = torch.zeros((V, H), dtype=torch.float32, device=dev)
+        native_grad = _native_grad_gemms(V, H, hidden.dtype) and h.stride(1) == 1
         for r0 in range(0, M, chunk_rows):
             r1 = min(r0 + chunk_rows, M)
             hc = h[r0:r1]
@@ -81,8 +98,13 @@ class _CrossEntropyTC(torch.autograd.Function):
             nat.call("nfb_ce_tc_grad", nat.ptr(hc), hc.stride(0), nat.ptr(w), w.stride(0), nat.ptr(tg[r0:r1]),
                      nat.ptr(lse[r0:r1]), nat.ptr(count), ignore_index, r1 - r0, V, H, nat.ptr(dl), dl.stride(0),
                      nat.ptr(st), s)
-            d_hidden[r0:r1] = torch.mm(dl, w).to(hidden.dtype)
-            d_weight += torch.mm(dl.t(), hc, out_dtype=torch.float32)
+            if native_grad:
+                # d_hidden[chunk] = dl @ W (W read as an MN-major B); d_W += dl^T @ h (both MN-major)
+                tc_gemm(dl, w, b_mn=True, out=d_hidden[r0:r1])
+                tc_gemm(dl, hc, a_mn=True, b_mn=True, out=d_weight, accumulate=True)
+            else:
+                d_hidden[r0:r1] = torch.mm(dl, w).to(hidden.dtype)
+                d_weight += torch.mm(dl.t(), hc, out_dtype=torch.float32)
             del dl
         ctx.save_for_backward(d_hidden, d_weight)
         ctx.wdtype = weight.dtype

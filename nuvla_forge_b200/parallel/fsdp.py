@@ -379,7 +379,7 @@ class FullyShardedDataParallel(nn.Module):
         ws = self.ws
         M, K = x2.shape
         N = w.shape[0]
-        nat.call("nfb_ag_gemm", ws.bases_ptr(), ws.world, self.param_off + u.shard_start * 2, u.shard * 2,
+        nat.call("nfb_ag_gemm", ws.bases_ptr(), ws.rank, ws.world, self.param_off + u.shard_start * 2, u.shard * 2,
                  nat.ptr(u.full), u.prefix * 2, u.numel * 2, w.data_ptr() - u.full.data_ptr(), N, K, nat.ptr(x2),
                  x2.stride(0), M, nat.ptr(y), y.stride(0), nat.ptr(self._ag_ready), nat.ptr(ws.status),
                  nat.stream(self.device))

@@ -197,7 +197,7 @@ def _ag_gemm_kernel(rank, world, cases):
         y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
         ready = torch.zeros(1024, dtype=torch.int32, device=dev)
         for _ in range(2):   # twice in a row: the ready counters are re-zeroed per launch
-            nat.call("nfb_ag_gemm", ws.bases_ptr(), world, off, shard * 2, nat.ptr(full), prefix * 2, numel * 2,
+            nat.call("nfb_ag_gemm", ws.bases_ptr(), rank, world, off, shard * 2, nat.ptr(full), prefix * 2, numel * 2,
                      prefix * 2, N, K, nat.ptr(x), K, M, nat.ptr(y), N, nat.ptr(ready), nat.ptr(ws.status),
                      nat.stream(dev))
         torch.cuda.synchronize(dev)

@@ -40,6 +40,30 @@ def test_tc_gemm_strided_operands():
     assert rel_err(c, a.float() @ b.float().t()) < 1e-5
 
 
+@pytest.mark.parametrize("a_mn,b_mn", [(True, False), (False, True), (True, True)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (304, 1000, 200), (136, 264, 72), (2048, 2048, 1024)])
+def test_tc_gemm_mn_major_operands(M, N, K, a_mn, b_mn):
+    """Operands stored transposed ([K, M] / [K, N], MN contiguous) against fp32, plus fp32 accumulate."""
+    from nuvla_forge_b200.ops import ce_tc
+
+    g = torch.Generator(device=DEV).manual_seed(3 * M + N + K)
+    a = torch.randn(M, K, generator=g, device=DEV).to(torch.bfloat16)
+    b = torch.randn(N, K, generator=g, device=DEV).to(torch.bfloat16)
+    a_in = a.t().contiguous() if a_mn else a
+    b_in = b.t().contiguous() if b_mn else b
+    ref = a.float() @ b.float().t()
+    c = ce_tc.tc_gemm(a_in, b_in, torch.float32, a_mn=a_mn, b_mn=b_mn)
+    torch.cuda.synchronize()
+    ce_tc.check_status()
+    assert rel_err(c, ref) < 1e-5, rel_err(c, ref)
+    base = torch.randn(M, N, generator=g, device=DEV)
+    acc = base.clone()
+    ce_tc.tc_gemm(a_in, b_in, a_mn=a_mn, b_mn=b_mn, out=acc, accumulate=True)
+    assert rel_err(acc, base + ref) < 1e-5
+    c16 = ce_tc.tc_gemm(a_in, b_in, torch.bfloat16, a_mn=a_mn, b_mn=b_mn)
+    assert rel_err(c16, ref) < 5e-3
+
+
 @pytest.mark.parametrize("M,H,V,chunk", [(256, 128, 1000, 128), (1000, 384, 32000, 512), (2048, 2048, 32000, 1024)])
 def test_ce_tc_matches_reference(M, H, V, chunk):
     from nuvla_forge_b200.ops import ce_tc
