@@ -61,6 +61,7 @@ _SIGS: dict[str, tuple] = {
     "nfb_count_valid": (I, [P, L, L, P, P]),
     "nfb_tc_gemm_bf16": (I, [P, P, P, I, I, I, L, L, L, I, P, P]),
     "nfb_tc_gemm_ex": (I, [P, P, P, I, I, I, L, L, L, I, I, I, I, P, P]),
+    "nfb_attn_fwd": (I, [P, P, P, P, P, I, I, I, I, I, I, L, L, L, L, L, L, L, L, L, L, L, L, I, F, P, P]),
     "nfb_ce_tc_tiles": (I, [I]),
     "nfb_ce_tc_stats": (I, [P, L, P, L, P, I, I, I, P, P, P, P, P]),
     "nfb_ce_tc_merge": (I, [P, P, P, P, P, I, I, L, P, P, P]),

@@ -151,6 +151,19 @@ def ag_gemm(iters):
     assert int(status.item()) == 0, hex(int(status.item()))
 
 
+@case
+def attn_fwd(iters):
+    """tcgen05 attention forward, ViT shape (24 images x 1024 patches, 16 heads, D 64; ~600 MB of q/k/v/o)."""
+    from ..ops import flash_attn
+    q = _bf(24, 1024, 16, 64)
+    kv = _bf(24, 1024, 32, 64, seed=1)
+    k, v = kv.split([16, 16], dim=2)
+    for _ in range(iters):
+        flash_attn.attention_fwd(q, k, v, False)
+    torch.cuda.synchronize()
+    flash_attn.check_status()
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", required=True, choices=sorted(CASES))

@@ -6,6 +6,7 @@ plus the ops the reference left to PyTorch.
 
 from .._native import HAS_NATIVE
 from . import ce_tc  # noqa: F401  (registers the tcgen05 cross-entropy path)
+from . import flash_attn  # noqa: F401  (tcgen05 attention forward; opt-in via NFB_ATTN_NATIVE=1)
 from .attention import attention
 from .chunked_ce import chunked_cross_entropy
 from .image import normalise_images, patchify_images
