@@ -15,12 +15,16 @@
 //               D-column TMEM accumulator (P from shared memory, K-major; V
 //               read MN-major straight from its TMA tile), so the tensor core
 //               computes S_j while the softmax warps work on S_{j-1}.
-//   warps 2-5   softmax: thread r owns query row r (TMEM lane r): it reads its
-//               128 scores with tcgen05.ld, keeps the running max / sum in
-//               registers (online softmax in base 2), rescales its O row in
-//               TMEM (tcgen05.ld/st) when the max grows, and writes its bf16
-//               probabilities into the 128-byte-swizzled P tile. At the end it
-//               normalises its O row and stores it with the log-sum-exp.
+//   warps 2-9   softmax: query row r (TMEM lane r) belongs to two threads, one
+//               in warps 2-5 (key columns 0-63 of each tile, O columns
+//               [0, D/2)) and one in warps 6-9 (the other halves). They read
+//               their scores with tcgen05.ld, exchange the tile maximum through
+//               shared memory, keep the running max / sums in registers (online
+//               softmax in base 2, SFU exp2), rescale their part of the O row in
+//               TMEM (tcgen05.ld/st) only when the max grows by more than 2^8,
+//               and write their bf16 probabilities -- one 64-key block each --
+//               into the 128-byte-swizzled P tile. At the end they normalise
+//               their O columns and store them with the log-sum-exp.
 // Every mbarrier wait is bounded by %globaltimer and reports a status; no
 // cluster, no multicast. Parity: the reference calls
 // F.scaled_dot_product_attention (nuvla_forge/model/dit.py:92).
@@ -34,7 +38,7 @@ using namespace nfb::tc;
 
 constexpr int BQ = 128;          // queries per CTA (TMEM lanes)
 constexpr int BKV = 128;         // keys per tile
-constexpr int kThreadsA = 192;
+constexpr int kThreadsA = 320;        // producer, MMA, 8 softmax warps
 constexpr uint32_t kTmemColsA = 512;   // S0 | S1 | O
 
 struct AttnArgs {
@@ -89,6 +93,28 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
       : "memory");
 }
 
+// Named barrier over the 64 threads of one row pair that also ANDs a flag across them, so both
+// warps of a pair always take the same branch (a warp that left alone would strand its partner).
+__device__ __forceinline__ bool pair_all(int id, bool v) {
+  int r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, 64, p;\n\t"
+      "selp.b32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((int)v), "r"(id)
+      : "memory");
+  return r != 0;
+}
+
+// 2^x with the SFU's approximate base-2 exponential (flushes denormal results to zero).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
@@ -108,7 +134,7 @@ struct Layout {
   static constexpr int kP = kV + 2 * kVBytes;
   static constexpr int kS = kP + kPBytes;
   // + AttnShared slot + alignment; at least 116 KB so that one CTA (and its 512 TMEM columns) owns an SM
-  static constexpr size_t kRaw = (size_t)kS + 1024 + 1024;
+  static constexpr size_t kRaw = (size_t)kS + 128 + 2048 + 1024;   // AttnShared, [2][2][128] fp32 exchange, alignment
   static constexpr size_t kBytes = kRaw > 116 * 1024 ? kRaw : 116 * 1024;
 };
 
@@ -139,7 +165,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       mbar_init(&S->kv_empty[s], 1);
       mbar_init(&S->s_full[s], 1);
     }
-    mbar_init(&S->p_full, 128);
+    mbar_init(&S->p_full, 256);
     mbar_init(&S->pv_done, 1);
     mbar_init(&S->o_full, 1);
     mbar_init(&S->drain, 1);
@@ -249,50 +275,67 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       while (!mbar_try_wait(&S->drain, 0u) && globaltimer_ns() - t0 < kWaitNs) {}
     }
   } else {
-    // ---------------- softmax + epilogue (warps 2..5) ----------------
+    // ---------------- softmax + epilogue (warps 2..9) ----------------
+    // Two warps share each TMEM lane quarter: warps 2-5 take key columns 0-63 of
+    // every tile (and O columns [0, D/2)), warps 6-9 key columns 64-127 (and O
+    // columns [D/2, D)). The two threads of a row exchange their tile maxima
+    // through shared memory behind a 64-thread named barrier.
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;           // query row in the tile = TMEM lane
     const int q = q0 + r;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    uint8_t* prow = smem + L::kP + (r >> 3) * 1024 + (r & 7) * 128;
-    float m = -INFINITY, l = 0.f;
+    const int bar_id = 1 + quarter;
+    float* xmax = reinterpret_cast<float*>(smem + L::kS + 128);   // [2][128] partial maxima, then [2][128] sums
+    uint8_t* prow = smem + L::kP + half * 16384 + (r >> 3) * 1024 + (r & 7) * 128;
+    const int lim = a.causal ? q + (a.Sk - a.Sq) : a.Sk - 1;
+    const int last = lim < a.Sk - 1 ? lim : a.Sk - 1;      // last key this row may see
+    constexpr int HC = BKV / 2;                            // key columns per thread
+    float m = -INFINITY, l = 0.f;                          // running max (log2 units), this half's sum
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       const int st = j & 1;
-      bool w = mbar_wait(&S->s_full[st], (j >> 1) & 1, abort_flag);
-      if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+      // (this barrier also orders the previous tile's reads of the exchange buffer before its reuse)
+      if (!pair_all(bar_id, mbar_wait(&S->s_full[st], (j >> 1) & 1, abort_flag))) { ok = false; break; }
       tmem_fence_after();
-      float s[BKV];
+      float s[HC];
 #pragma unroll
-      for (int c = 0; c < BKV; c += 32) tmem_ld32(tmem_base + lane_off + (uint32_t)(st * BKV + c), s + c);
-      const int kv0 = j * BKV;
-      const int lim = a.causal ? q + (a.Sk - a.Sq) : a.Sk - 1;     // last key this row may see
-      const int last = lim < a.Sk - 1 ? lim : a.Sk - 1;
-      float mt = -INFINITY;
+      for (int c = 0; c < HC; c += 32)
+        tmem_ld32(tmem_base + lane_off + (uint32_t)(st * BKV + half * HC + c), s + c);
+      const int kv0 = j * BKV + half * HC;
+      if (kv0 + HC - 1 > last) {
 #pragma unroll
-      for (int c = 0; c < BKV; ++c) {
-        s[c] = (kv0 + c <= last) ? s[c] * a.scale_log2 : -INFINITY;
-        mt = fmaxf(mt, s[c]);
+        for (int c = 0; c < HC; ++c) s[c] = (kv0 + c <= last) ? s[c] : -INFINITY;
       }
-      const float m_new = fmaxf(m, mt);
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = m == -INFINITY ? 0.f : exp2f(m - m_use);
+      float mt = s[0];
+#pragma unroll
+      for (int c = 1; c < HC; ++c) mt = fmaxf(mt, s[c]);
+      xmax[half * 128 + r] = mt;
+      asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
+      mt = fmaxf(mt, xmax[(half ^ 1) * 128 + r]) * a.scale_log2;
+      // lazy rescaling: keep the old reference max unless the new one exceeds it by more than 8 (2^8
+      // headroom in fp32), so O is rescaled only on large jumps
+      float m_ref = m, alpha = 1.f;
+      if (mt > m + 8.f) {
+        m_ref = mt;
+        alpha = m == -INFINITY ? 0.f : ex2_approx(m - mt);
+      }
+      const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
       float sum = 0.f;
 #pragma unroll
-      for (int c = 0; c < BKV; ++c) {
-        s[c] = exp2f(s[c] - m_use);
+      for (int c = 0; c < HC; ++c) {
+        s[c] = ex2_approx(fmaf(s[c], a.scale_log2, -m_use));
         sum += s[c];
       }
       l = l * alpha + sum;
-      m = m_new;
+      m = m_ref;
       if (j >= 1) {
         // O may be rescaled (and P overwritten) only after the previous P V finished
-        w = mbar_wait(&S->pv_done, (j - 1) & 1, abort_flag);
-        if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+        if (!pair_all(bar_id, mbar_wait(&S->pv_done, (j - 1) & 1, abort_flag))) { ok = false; break; }
         tmem_fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-          for (int c = 0; c < D; c += 32) {
+          for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 32) {
             float o[32];
             tmem_ld32(tmem_base + lane_off + 256u + (uint32_t)c, o);
 #pragma unroll
@@ -301,24 +344,26 @@ __global__ void __launch_bounds__(kThreadsA, 1)
           }
         }
       }
-      // bf16 probabilities into the 128-byte-swizzled K-major P tile (two 64-key blocks)
+      // this half's 64 bf16 probabilities = one 64-key block of the 128-byte-swizzled K-major P tile
 #pragma unroll
-      for (int kb = 0; kb < 2; ++kb) {
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const float* p = s + kb * 64 + c * 8;
-          uint4 v;
-          v.x = pack_bf16(p[0], p[1]);
-          v.y = pack_bf16(p[2], p[3]);
-          v.z = pack_bf16(p[4], p[5]);
-          v.w = pack_bf16(p[6], p[7]);
-          *reinterpret_cast<uint4*>(prow + kb * 16384 + ((c ^ (r & 7)) << 4)) = v;
-        }
+      for (int c = 0; c < 8; ++c) {
+        const float* p = s + c * 8;
+        uint4 v;
+        v.x = pack_bf16(p[0], p[1]);
+        v.y = pack_bf16(p[2], p[3]);
+        v.z = pack_bf16(p[4], p[5]);
+        v.w = pack_bf16(p[6], p[7]);
+        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = v;
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tmem_fence_before();
       mbar_arrive(&S->p_full);
     }
+    // the row's total sum: this half's plus the partner's
+    float* xsum = xmax + 256;
+    xsum[half * 128 + r] = l;
+    asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
+    const float l_row = l + xsum[(half ^ 1) * 128 + r];
     if (!ok) {
       if (lane == 0) {
         set_status(a.status, kTimeoutFlag, 122);
@@ -328,17 +373,18 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       // no key is visible to any row of this tile (causal with Sq > Sk): zero rows
       if (q < a.Sq) {
         __nv_bfloat16* orow = a.o + (int64_t)b * a.so_b + (int64_t)q * a.so_s + (int64_t)h * a.so_h;
-        for (int c = 0; c < D; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0u, 0u, 0u, 0u);
-        if (a.lse) a.lse[((int64_t)b * a.Hq + h) * a.Sq + q] = -INFINITY;
+        for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 8)
+          *reinterpret_cast<uint4*>(orow + c) = make_uint4(0u, 0u, 0u, 0u);
+        if (a.lse && half == 0) a.lse[((int64_t)b * a.Hq + h) * a.Sq + q] = -INFINITY;
       }
     } else {
       const bool w = mbar_wait(&S->o_full, 0u, abort_flag);
       if (__all_sync(0xffffffffu, w)) {
         tmem_fence_after();
-        const float inv = l > 0.f ? 1.f / l : 0.f;
+        const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
         __nv_bfloat16* orow = a.o + (int64_t)b * a.so_b + (int64_t)q * a.so_s + (int64_t)h * a.so_h;
 #pragma unroll 1
-        for (int c = 0; c < D; c += 32) {
+        for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 32) {
           float o[32];
           tmem_ld32(tmem_base + lane_off + 256u + (uint32_t)c, o);
           if (q < a.Sq) {
@@ -353,8 +399,9 @@ __global__ void __launch_bounds__(kThreadsA, 1)
             }
           }
         }
-        if (q < a.Sq && a.lse)
-          a.lse[((int64_t)b * a.Hq + h) * a.Sq + q] = l > 0.f ? m * 0.69314718055994531f + logf(l) : -INFINITY;
+        if (q < a.Sq && a.lse && half == 0)
+          a.lse[((int64_t)b * a.Hq + h) * a.Sq + q] =
+              l_row > 0.f ? m * 0.69314718055994531f + logf(l_row) : -INFINITY;
       } else if (lane == 0) {
         set_status(a.status, kTimeoutFlag, 123);
         S->abort = 1;
