@@ -81,6 +81,27 @@ __device__ __forceinline__ void load_chunk(const T* base, int64_t col, int64_t N
   }
 }
 
+// 8 elements held as raw loaded vectors (16 bytes for 16-bit types, 32 for fp32); zeros past N or
+// for a null row.
+template <typename T>
+struct RawChunk {
+  uint4 u[sizeof(T) == 2 ? 1 : 2];
+  __device__ __forceinline__ void load(const T* base, int64_t col, int64_t N) {
+    if (base != nullptr && col < N) {
+      u[0] = *reinterpret_cast<const uint4*>(base + col);
+      if (sizeof(T) == 4) u[sizeof(T) == 2 ? 0 : 1] = *reinterpret_cast<const uint4*>(base + col + 4);
+    } else {
+#pragma unroll
+      for (int k = 0; k < (sizeof(T) == 2 ? 1 : 2); ++k) u[k] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  __device__ __forceinline__ void get(float* out) const {
+    const T* v = reinterpret_cast<const T*>(u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) out[j] = to_f32(v[j]);
+  }
+};
+
 template <typename T>
 __device__ __forceinline__ void load_weight_chunk(const void* w, int w_f32, int64_t col, int64_t N, float* out) {
   if (col >= N) {
@@ -178,22 +199,29 @@ __global__ void __launch_bounds__(256) norm_fwd_warp_kernel(NormFwdArgs a) {
   for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < a.M; row += warps) {
     const int64_t b = row / a.T;
     float hv[NW][8];
+    float yv[GATE != GATE_NONE ? NW : 1][8];
     float ss = 0.f;
+    // every load of the row is issued before the first store: the compiler may not move a load
+    // across a store that could alias it, which would serialise one round trip per chunk
 #pragma unroll
     for (int i = 0; i < NW; ++i) {
       const int64_t col = ((int64_t)i * 32 + lane) * 8;
       load_chunk<T>(reinterpret_cast<const T*>(a.x) + row * a.sx, col, N, hv[i]);
+      if (GATE != GATE_NONE) load_chunk<T>(reinterpret_cast<const T*>(a.y) + row * a.sy, col, N, yv[i % (GATE != GATE_NONE ? NW : 1)]);
+    }
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+      const int64_t col = ((int64_t)i * 32 + lane) * 8;
       if (GATE != GATE_NONE) {
-        float yv[8];
-        load_chunk<T>(reinterpret_cast<const T*>(a.y) + row * a.sy, col, N, yv);
+        const float* y8 = yv[i % (GATE != GATE_NONE ? NW : 1)];
         if (GATE == GATE_VEC) {
           float gv[8];
           load_chunk<T>(reinterpret_cast<const T*>(a.gate) + b * a.sg, col, N, gv);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) hv[i][j] += gv[j] * yv[j];
+          for (int j = 0; j < 8; ++j) hv[i][j] += gv[j] * y8[j];
         } else {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) hv[i][j] += yv[j];
+          for (int j = 0; j < 8; ++j) hv[i][j] += y8[j];
         }
         round8<T>(hv[i]);
         if (col < N) store8<T>(reinterpret_cast<T*>(a.h) + row * a.sh + col, hv[i]);
@@ -267,6 +295,18 @@ __global__ void __launch_bounds__(512, (GATE == GATE_VEC || MOD) ? 1 : 2) norm_b
     const float rstd = a.rstd[row];
     const T* dout_r = reinterpret_cast<const T*>(a.dout) + row * a.s_dout;
     const T* h_r = reinterpret_cast<const T*>(a.h) + row * a.s_h;
+    // Every HBM load of the row (dout, h, and pass 2's dh_up and y) is issued here, before the
+    // team barrier and before any store: a load may not be moved across a store that could alias
+    // it, so HBM loads issued after the first store would each cost a serial round trip.
+    // (kept as raw 16-byte vectors until used, to spare registers)
+    RawChunk<T> dhv[NV], yv[GATE == GATE_VEC ? NV : 1];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int64_t col = ((int64_t)i * K * 32 + tt) * 8;
+      dhv[i].load(a.dh_up != nullptr ? reinterpret_cast<const T*>(a.dh_up) + row * a.s_dhup : nullptr, col, N);
+      if (GATE == GATE_VEC)
+        yv[i % (GATE == GATE_VEC ? NV : 1)].load(reinterpret_cast<const T*>(a.y) + row * a.s_y, col, N);
+    }
     // pass 1: row dot product and the per-column accumulators
     float dot = 0.f;
 #pragma unroll
@@ -286,7 +326,7 @@ __global__ void __launch_bounds__(512, (GATE == GATE_VEC || MOD) ? 1 : 2) norm_b
     }
     dot = team_sum(dot, red, parity, wt, K, bar_id) * invN;
     parity ^= 1;
-    // pass 2: the row is re-read (L1-resident) rather than kept in registers
+    // pass 2: dout and h are re-read (L1-resident; a reload after a store costs an L1 round trip only)
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int64_t col = ((int64_t)i * K * 32 + tt) * 8;
@@ -294,11 +334,7 @@ __global__ void __launch_bounds__(512, (GATE == GATE_VEC || MOD) ? 1 : 2) norm_b
       float dv[8], hv[8], dh[8];
       load8<T>(dout_r + col, dv);
       load8<T>(h_r + col, hv);
-      if (a.dh_up != nullptr) load8<T>(reinterpret_cast<const T*>(a.dh_up) + row * a.s_dhup + col, dh);
-      else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) dh[j] = 0.f;
-      }
+      dhv[i].get(dh);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const float xh = hv[j] * rstd;
@@ -306,12 +342,12 @@ __global__ void __launch_bounds__(512, (GATE == GATE_VEC || MOD) ? 1 : 2) norm_b
       }
       store8<T>(reinterpret_cast<T*>(a.dx) + row * a.s_dx + col, dh);
       if (GATE == GATE_VEC) {
-        float yv[8], dyv[8];
-        load8<T>(reinterpret_cast<const T*>(a.y) + row * a.s_y + col, yv);
+        float dyv[8], y8[8];
+        yv[i % (GATE == GATE_VEC ? NV : 1)].get(y8);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           dyv[j] = dh[j] * gv_s[col + j];
-          accG[i * 8 + j] += dh[j] * yv[j];
+          accG[i * 8 + j] += dh[j] * y8[j];
         }
         store8<T>(reinterpret_cast<T*>(a.dy) + row * a.s_dy + col, dyv);
       } else if (GATE == GATE_ONE) {
