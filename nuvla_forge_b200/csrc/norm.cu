@@ -81,6 +81,20 @@ __device__ __forceinline__ void load_chunk(const T* base, int64_t col, int64_t N
   }
 }
 
+// 8 consecutive fp32 values of a shared-memory row as two 16-byte loads (zeros past N): with
+// each lane reading its own 32 bytes, scalar loads would hit the same banks 8 ways.
+__device__ __forceinline__ void lds8(const float* row, int64_t col, int64_t N, float* out) {
+  if (col < N) {
+    const float4 a = *reinterpret_cast<const float4*>(row + col);
+    const float4 b = *reinterpret_cast<const float4*>(row + col + 4);
+    out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+    out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) out[j] = 0.f;
+  }
+}
+
 // 8 elements held as raw loaded vectors (16 bytes for 16-bit types, 32 for fp32); zeros past N or
 // for a null row.
 template <typename T>
@@ -315,11 +329,12 @@ __global__ void __launch_bounds__(512, (GATE == GATE_VEC || MOD) ? 1 : 2) norm_b
       float dv[8], hv[8];
       load_chunk<T>(dout_r, col, N, dv);
       load_chunk<T>(h_r, col, N, hv);
+      float w8[8];
+      lds8(ws_s, col, N, w8);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const float xh = hv[j] * rstd;
-        const float w = (col < N) ? ws_s[col + j] : 0.f;
-        dot += dv[j] * w * xh;
+        dot += dv[j] * w8[j] * xh;
         accA[i * 8 + j] += dv[j] * xh;
         if (MOD) accD[i * 8 + j] += dv[j];
       }
@@ -335,18 +350,22 @@ __global__ void __launch_bounds__(512, (GATE == GATE_VEC || MOD) ? 1 : 2) norm_b
       load8<T>(dout_r + col, dv);
       load8<T>(h_r + col, hv);
       dhv[i].get(dh);
+      float w8[8];
+      lds8(ws_s, col, N, w8);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const float xh = hv[j] * rstd;
-        dh[j] += rstd * (dv[j] * ws_s[col + j] - xh * dot);
+        dh[j] += rstd * (dv[j] * w8[j] - xh * dot);
       }
       store8<T>(reinterpret_cast<T*>(a.dx) + row * a.s_dx + col, dh);
       if (GATE == GATE_VEC) {
         float dyv[8], y8[8];
         yv[i % (GATE == GATE_VEC ? NV : 1)].get(y8);
 #pragma unroll
+        float g8[8];
+        lds8(gv_s, col, N, g8);
         for (int j = 0; j < 8; ++j) {
-          dyv[j] = dh[j] * gv_s[col + j];
+          dyv[j] = dh[j] * g8[j];
           accG[i * 8 + j] += dh[j] * y8[j];
         }
         store8<T>(reinterpret_cast<T*>(a.dy) + row * a.s_dy + col, dyv);
