@@ -13,6 +13,8 @@ ranks, L2 flushed between iterations):
 * fused:    ``nfb_ag_gemm`` (gather of the whole unit + the GEMM, one kernel)
 * separate: ``nfb_allgather`` of the unit, then the same GEMM by cuBLAS
 * separate_ce: the unit gathered by the copy engines (one peer copy per shard), then cuBLAS
+* fused_w_ce: ``nfb_ag_gemm`` gathering only W while the copy engines move the rest of the
+  unit on a second stream (the FSDP runtime's steady state)
 * gemm:     the GEMM alone (cuBLAS, weights already local)
 
 Roofline of the fused kernel = max(GEMM FLOPs / measured bf16 peak, bytes
@@ -125,6 +127,24 @@ def main(argv=None):
         def gemm():
             torch.matmul(x, w.t(), out=y)
 
+        side = torch.cuda.Stream(device=dev)
+
+        def fused_w_ce():
+            # the fused kernel gathers only W; the copy engines move the rest of the unit meanwhile
+            side.wait_stream(torch.cuda.current_stream(dev))
+            hs = ctypes.c_void_p(side.cuda_stream)
+            w_lo, w_hi = pre * 2, pre * 2 + N * K * 2
+            for i in range(world):
+                q = (rank + 1 + i) % world
+                for lo, hi in ((0, w_lo), (w_hi, numel * 2)):
+                    f0, f1 = max(lo, q * shard * 2), min(hi, (q + 1) * shard * 2)
+                    if f1 > f0:
+                        nat.call("nfb_copy_async", ctypes.c_void_p(full.data_ptr() + f0),
+                                 ctypes.c_void_p(ws.bases[q] + off + (f0 - q * shard * 2)), f1 - f0, hs)
+            nat.call("nfb_ag_gemm", ws.bases_ptr(), rank, world, off, shard * 2, nat.ptr(full), w_lo, w_hi,
+                     pre * 2, N, K, nat.ptr(x), K, M, nat.ptr(y), N, nat.ptr(ready), nat.ptr(ws.status), s)
+            torch.cuda.current_stream(dev).wait_stream(side)
+
         def separate_ce():
             for i in range(world):
                 q = (rank + i) % world
@@ -144,6 +164,8 @@ def main(argv=None):
         ws.check()
         r["separate_ms"] = _timed(separate, args.iters, dev, flush)
         r["separate_ce_ms"] = _timed(separate_ce, args.iters, dev, flush)
+        r["fused_w_ce_ms"] = _timed(fused_w_ce, args.iters, dev, flush)
+        ws.check()
         r["gemm_ms"] = _timed(gemm, args.iters, dev, flush)
         r["allgather_ms"] = _timed(allgather, args.iters, dev, flush)
         ws.check()
@@ -159,7 +181,8 @@ def main(argv=None):
         if rank == 0:
             print(f"{c['case']:<26} M{M} N{N} K{K} unit {numel * 2 / 2**20:7.1f} MiB | fused {r['fused_ms']:.3f} ms"
                   f" | separate {r['separate_ms']:.3f} (AG {r['allgather_ms']:.3f} + GEMM {r['gemm_ms']:.3f})"
-                  f" | copy-engine AG + GEMM {r['separate_ce_ms']:.3f}"
+                  f" | copy-engine AG + GEMM {r['separate_ce_ms']:.3f} | fused W + copy-engine rest "
+                  f"{r['fused_w_ce_ms']:.3f}"
                   f" | roofline {r['roofline_ms']:.3f} ({r['roofline_bound']}) = {100 * r['frac_of_roofline']:.0f}%")
         dist.barrier()
         ws.close()

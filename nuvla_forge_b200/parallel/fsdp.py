@@ -18,8 +18,12 @@ clipping:
   and DiT blocks (``fuse_ag_gemm``) the gather is fused into the block's first
   linear layer: the 1-D parameters (norm weights, biases; laid out first in
   the unit) are copied ahead by the copy engine, and the block's first GEMM is
-  ``nfb_ag_gemm`` -- one kernel that pulls the whole unit over NVLink while
-  its tensor-core tiles consume the weight's row blocks as they land. Other
+  ``nfb_ag_gemm`` -- one kernel that pulls the weight it consumes over NVLink
+  while its tensor-core tiles consume the weight's row blocks as they land.
+  With more than two ranks (``ag_hybrid``), once the consuming weight is known
+  (after a unit's first forward) the kernel gathers only that weight and the
+  rest of the unit goes to the copy engines on the prefetch stream,
+  concurrently. Other
   units use ``nfb_allgather`` (each rank pulls its peers' shards). Backward: a
   hook on the unit's outputs gathers it again (``nfb_allgather``) before its
   backward runs.
@@ -94,6 +98,8 @@ class _Unit:
     ag_ok: bool = False        # the unit's first parameter consumer is a linear layer (fused gather allowed)
     ag_pending: bool = False   # storage allocated, prefix copied, the rest awaits the fused GEMM
     ready_event: object = None # prefetch all-gather in flight on the prefetch stream
+    first_w: tuple | None = None   # (byte offset, bytes) of the weight the first linear consumes
+    rest_event: object = None  # copy-engine gather of the unit minus first_w, in flight
 
 
 class FullyShardedDataParallel(nn.Module):
@@ -142,6 +148,12 @@ class FullyShardedDataParallel(nn.Module):
             self.ag_stream = torch.cuda.Stream(device=dev)
         self._ag_ready = torch.zeros(1024, dtype=torch.int32, device=dev) if self.fuse_ag_gemm else None
         self.ag_fused_launches = 0
+        # Measured on B200: with one peer the in-kernel gather of the whole unit is as fast as
+        # anything else; with more, every rank reads the consumed weight from the same one or two
+        # owners, so the kernel gathers only that weight and the copy engines the rest.
+        import os
+        env = os.environ.get("NFB_FSDP_AG_HYBRID")
+        self.ag_hybrid = (env == "1") if env is not None else self.world > 2
         self.fuse_rs_adamw = bool(fuse_rs_adamw and comm == "fused")
         self._opt = None
         self._fused_updates = 0
@@ -289,6 +301,8 @@ class FullyShardedDataParallel(nn.Module):
             st.resize_(nbytes)
         if lazy and u.ag_ok:
             self._copy_prefix(u)
+            if u.first_w is not None and self.ag_hybrid:
+                self._copy_rest(u)
             u.ag_pending = True
             u.gathered = True
             self._ag_unit = u
@@ -352,6 +366,30 @@ class FullyShardedDataParallel(nn.Module):
             nat.call("nfb_copy_async", ctypes.c_void_p(u.full.data_ptr() + f0),
                      ctypes.c_void_p(self.ws.bases[q] + src0), f1 - f0, stream)
 
+    def _copy_rest(self, u: _Unit) -> None:
+        """Copy-engine gather (prefetch stream) of the unit except its prefix and its first weight.
+
+        The fused GEMM then gathers only the weight it consumes, so its NVLink volume is that
+        weight's, and the copy engines move the other parameters at the same time.
+        """
+        S = u.shard * 2
+        src0 = self.param_off + u.shard_start * 2
+        w0, w1 = u.first_w[0], u.first_w[0] + u.first_w[1]
+        ranges = [(u.prefix * 2, w0), (w1, u.numel * 2)]
+        cs = self.ag_stream
+        cs.wait_stream(torch.cuda.current_stream(self.device))   # the storage may be reused memory
+        h = ctypes.c_void_p(cs.cuda_stream)
+        for i in range(self.world):
+            q = (self.rank + 1 + i) % self.world
+            for lo, hi in ranges:
+                f0, f1 = max(lo, q * S), min(hi, (q + 1) * S)
+                if f1 > f0:
+                    nat.call("nfb_copy_async", ctypes.c_void_p(u.full.data_ptr() + f0),
+                             ctypes.c_void_p(self.ws.bases[q] + src0 + (f0 - q * S)), f1 - f0, h)
+        ev = torch.cuda.Event()
+        ev.record(cs)
+        u.rest_event = ev
+
     def _consume_linear(self, x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None):
         """The pending unit's first linear layer: run it as the all-gather-fused GEMM."""
         u = self._ag_unit
@@ -370,17 +408,31 @@ class FullyShardedDataParallel(nn.Module):
                 and K % 8 == 0 and x.numel() > 0 and off % 16 == 0
                 and (w.shape[0] + 255) // 256 <= self._ag_ready.numel())
         if not fits:
+            if u.rest_event is not None:
+                torch.cuda.current_stream(self.device).wait_event(u.rest_event)
+                u.rest_event = None
             self._launch_allgather(u, barrier=False)
             return None
+        if u.first_w is None:
+            u.first_w = (off, w.numel() * 2)   # later forwards gather the rest by copy engine
         y = _AgLinear.apply(x, w, self, u)
+        if u.rest_event is not None:
+            # every later use of the unit sees the copy-engine part too
+            torch.cuda.current_stream(self.device).wait_event(u.rest_event)
+            u.rest_event = None
         return y if b is None else y + b
 
     def _launch_ag_gemm(self, u: _Unit, x2: torch.Tensor, w: torch.Tensor, y: torch.Tensor) -> None:
         ws = self.ws
         M, K = x2.shape
         N = w.shape[0]
+        off = w.data_ptr() - u.full.data_ptr()
+        # with the rest of the unit in flight on the copy engines, gather only this weight (if this is
+        # the weight those copies left out; otherwise the whole unit again, which rewrites equal bytes)
+        only_w = u.rest_event is not None and u.first_w == (off, N * K * 2)
+        lo, hi = (off, off + N * K * 2) if only_w else (u.prefix * 2, u.numel * 2)
         nat.call("nfb_ag_gemm", ws.bases_ptr(), ws.rank, ws.world, self.param_off + u.shard_start * 2, u.shard * 2,
-                 nat.ptr(u.full), u.prefix * 2, u.numel * 2, w.data_ptr() - u.full.data_ptr(), N, K, nat.ptr(x2),
+                 nat.ptr(u.full), lo, hi, off, N, K, nat.ptr(x2),
                  x2.stride(0), M, nat.ptr(y), y.stride(0), nat.ptr(self._ag_ready), nat.ptr(ws.status),
                  nat.stream(self.device))
         self.ag_fused_launches += 1
@@ -389,6 +441,9 @@ class FullyShardedDataParallel(nn.Module):
         if not u.gathered or u is self.root:
             return
         self._ensure_ready(u)   # no prefetch may still be writing the storage being released
+        if u.rest_event is not None:
+            torch.cuda.current_stream(self.device).wait_event(u.rest_event)
+            u.rest_event = None
         u.full.untyped_storage().resize_(0)
         u.gathered = False
 

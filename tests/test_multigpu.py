@@ -254,7 +254,10 @@ def _fsdp_model(rank, world, fuse, fuse_rs=True, clip=1.0):
 
 def test_fsdp_ag_gemm_matches_plain_gather():
     w = _world()
-    a = run_ranks(_fsdp_model, w, args=(True,), backend="nccl", env=ENV, timeout_s=240, join_s=400)
+    # hybrid forced on: after the first forward the fused kernel gathers only the consumed weight and
+    # the copy engines the rest of the unit (the default above two ranks)
+    a = run_ranks(_fsdp_model, w, args=(True,), backend="nccl", env={**ENV, "NFB_FSDP_AG_HYBRID": "1"},
+                  timeout_s=240, join_s=400)
     b = run_ranks(_fsdp_model, w, args=(False,), backend="nccl", env=ENV, timeout_s=240, join_s=400)
     assert all(st == "ok" for st, _ in a.values()) and all(st == "ok" for st, _ in b.values()), (a, b)
     assert a[0][1]["fused_launches"] > 0 and b[0][1]["fused_launches"] == 0
