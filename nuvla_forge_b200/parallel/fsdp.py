@@ -372,20 +372,13 @@ class FullyShardedDataParallel(nn.Module):
         The fused GEMM then gathers only the weight it consumes, so its NVLink volume is that
         weight's, and the copy engines move the other parameters at the same time.
         """
-        S = u.shard * 2
         src0 = self.param_off + u.shard_start * 2
-        w0, w1 = u.first_w[0], u.first_w[0] + u.first_w[1]
-        ranges = [(u.prefix * 2, w0), (w1, u.numel * 2)]
         cs = self.ag_stream
         cs.wait_stream(torch.cuda.current_stream(self.device))   # the storage may be reused memory
         h = ctypes.c_void_p(cs.cuda_stream)
-        for i in range(self.world):
-            q = (self.rank + 1 + i) % self.world
-            for lo, hi in ranges:
-                f0, f1 = max(lo, q * S), min(hi, (q + 1) * S)
-                if f1 > f0:
-                    nat.call("nfb_copy_async", ctypes.c_void_p(u.full.data_ptr() + f0),
-                             ctypes.c_void_p(self.ws.bases[q] + src0 + (f0 - q * S)), f1 - f0, h)
+        for q, f0, f1 in rest_copies(u.prefix * 2, u.first_w, u.numel * 2, u.shard * 2, self.world, self.rank):
+            nat.call("nfb_copy_async", ctypes.c_void_p(u.full.data_ptr() + f0),
+                     ctypes.c_void_p(self.ws.bases[q] + src0 + (f0 - q * u.shard * 2)), f1 - f0, h)
         ev = torch.cuda.Event()
         ev.record(cs)
         u.rest_event = ev
@@ -734,6 +727,23 @@ class FullyShardedDataParallel(nn.Module):
         opt.step_count = int(sd["step"])
         opt.m.copy_(sd["exp_avg_shards"][self.rank].to(opt.m.device))
         opt.v.copy_(sd["exp_avg_sq_shards"][self.rank].to(opt.v.device))
+
+
+def rest_copies(prefix_bytes: int, first_w: tuple, total_bytes: int, shard_bytes: int, world: int, rank: int):
+    """Copy-engine transfers (owner, flat byte start, end) for a unit minus its prefix and first weight.
+
+    The flat range [prefix_bytes, total_bytes) without [w0, w0 + wbytes) is split at shard
+    boundaries; owners are visited from rank+1 on, so ranks start on different peers.
+    """
+    w0, w1 = first_w[0], first_w[0] + first_w[1]
+    out = []
+    for i in range(world):
+        q = (rank + 1 + i) % world
+        for lo, hi in ((prefix_bytes, w0), (w1, total_bytes)):
+            f0, f1 = max(lo, q * shard_bytes), min(hi, (q + 1) * shard_bytes)
+            if f1 > f0:
+                out.append((q, f0, f1))
+    return out
 
 
 class _AgLinear(torch.autograd.Function):

@@ -122,3 +122,50 @@ def test_fsdp_checkpoint_roundtrip():
         assert out[0][1]["eq"] and out[1][1]["eq"] and out[0][1]["step"] == 1
         sd = torch.load(path, weights_only=False)["model"]
         assert set(sd) == set(Net().state_dict())
+
+
+def test_unit_layout_puts_1d_params_first():
+    """The prefix a fused gather copies ahead holds exactly the unit's 1-D parameters."""
+    from nuvla_forge_b200.models import NuVLA, NuVLAConfig
+    from nuvla_forge_b200.parallel.fsdp import FullyShardedDataParallel
+
+    model = NuVLA(NuVLAConfig.preset("tiny"))
+    f = FullyShardedDataParallel(model, comm="none")
+    for u in f.units[:-1]:
+        dims = [s.param.dim() for s in u.segs]
+        n1 = sum(1 for d in dims if d <= 1)
+        assert all(d <= 1 for d in dims[:n1]) and all(d > 1 for d in dims[n1:]), u.name
+        end = max((s.start + s.numel + 7) // 8 * 8 for s in u.segs if s.param.dim() <= 1)
+        assert u.prefix == end, (u.name, u.prefix, end)
+        assert all(s.start >= u.prefix for s in u.segs if s.param.dim() > 1)
+
+
+def test_rest_copies_cover_unit_minus_prefix_and_weight():
+    import random
+
+    from nuvla_forge_b200.parallel.fsdp import rest_copies
+
+    rng = random.Random(0)
+    for _ in range(200):
+        world = rng.choice([1, 2, 4, 8])
+        shard = 16 * rng.randint(1, 5000)
+        total = shard * world
+        prefix = 16 * rng.randint(0, total // 64)
+        wbytes = 16 * rng.randint(1, max(1, (total - prefix) // 32))
+        w0 = prefix + 16 * rng.randint(0, (total - prefix - wbytes) // 16)
+        for rank in range(world):
+            cov = []
+            for q, f0, f1 in rest_copies(prefix, (w0, wbytes), total, shard, world, rank):
+                assert q * shard <= f0 < f1 <= (q + 1) * shard
+                cov.append((f0, f1))
+            cov.sort()
+            want = [(a, b) for a, b in ((prefix, w0), (w0 + wbytes, total)) if b > a]
+            # merge the covered pieces and compare with the wanted ranges
+            merged = []
+            for a, b in cov:
+                if merged and merged[-1][1] == a:
+                    merged[-1] = (merged[-1][0], b)
+                else:
+                    assert not merged or merged[-1][1] < a, "overlap"
+                    merged.append((a, b))
+            assert merged == want, (merged, want)
