@@ -31,7 +31,7 @@ import torch
 import torch.distributed as dist
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-BASELINE_SAMPLES_PER_S = 158.05  # reference train samples/s (optimised preset, 1x H100 NVL, 77.3M)
+BASELINE_SAMPLES_PER_S = 158.05  # the reference's published train samples/s (optimised preset, 1x H100 NVL, 77.3M params)
 METRIC = "train samples/sec (device-timed, max over ranks)"
 
 
