@@ -130,10 +130,14 @@ class TrajectoryDiT(nn.Module):
         return F.mse_loss(pred.float(), traj - noise)
 
     @torch.no_grad()
-    def sample(self, context, steps: int = 10):
-        """Euler integration of the learned velocity from noise (s=0) to a trajectory (s=1)."""
+    def sample(self, context, steps: int = 10, z0: torch.Tensor | None = None):
+        """Euler integration of the learned velocity from noise (s=0) to a trajectory (s=1).
+
+        ``z0`` (optional) is the starting noise [B, horizon, traj_dim]; drawn here when omitted.
+        """
         b = context.shape[0]
-        z = torch.randn(b, self.horizon, self.traj_dim, device=context.device, dtype=torch.float32)
+        z = z0.float() if z0 is not None else torch.randn(b, self.horizon, self.traj_dim, device=context.device,
+                                                          dtype=torch.float32)
         ds = 1.0 / steps
         for i in range(steps):
             t = torch.full((b,), i * ds * self.t_max, device=z.device)

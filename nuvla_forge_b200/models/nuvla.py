@@ -319,6 +319,24 @@ class NuVLA(nn.Module):
         out["loss"] = total
         return out
 
+    @torch.no_grad()
+    def context(self, images, text_tokens=None):
+        """The states the DiT cross-attends to (backbone output over image and instruction tokens)."""
+        cfg = self.cfg
+        if cfg.backbone_over_images:
+            img = self.image_tokens(images)
+            h = img
+            if text_tokens is not None:
+                txt = self.text_embed(text_tokens) + self.text_pos[:, : text_tokens.shape[1]]
+                h = torch.cat([img, txt.to(img.dtype)], dim=1)
+            return run_blocks(self.text_blocks, h, self.text_norm)
+        return self.encode_scene(images)
+
+    @torch.no_grad()
+    def plan(self, images, text_tokens=None, steps: int = 10, z0: torch.Tensor | None = None):
+        """Sample waypoints [B, horizon, traj_dim] by Euler integration of the DiT's velocity."""
+        return self.dit.sample(self.context(images, text_tokens), steps=steps, z0=z0)
+
     def num_parameters(self) -> int:
         return sum(p.numel() for p in self.parameters())
 

@@ -71,3 +71,29 @@ def test_bf16_model_forward_backward_1b_layer_shapes():
     y = blk(x)
     y.float().square().mean().backward()
     assert torch.isfinite(x.grad).all()
+
+
+def test_graphed_planner_matches_eager():
+    """The DiT sampling loop captured in one CUDA graph gives the eager sampler's waypoints."""
+    from nuvla_forge_b200.models import NuVLA, NuVLAConfig
+    from nuvla_forge_b200.serve import GraphedPlanner
+
+    cfg = NuVLAConfig.preset("tiny")
+    torch.manual_seed(0)
+    model = NuVLA(cfg).cuda().to(torch.bfloat16).eval()
+    for p in model.dit.out.parameters():     # the zero-initialised head would make every plan zero
+        torch.nn.init.normal_(p, std=0.1)
+    b = _batch(cfg)
+    ctx = model.context(b["images"], b["text_tokens"])
+    z0 = torch.randn(2, model.dit.horizon, model.dit.traj_dim, device="cuda")
+    eager = model.dit.sample(ctx, 4, z0=z0)
+    planner = GraphedPlanner(model, batch_size=2, context_len=ctx.shape[1], steps=4)
+    assert planner.graph is not None
+    got = planner(ctx, z0=z0)
+    again = planner(ctx, z0=z0)
+    torch.cuda.synchronize()
+    assert torch.equal(got, again)
+    err = float((got - eager).norm() / (eager.norm() + 1e-6))
+    assert err < 2e-2, err
+    other = planner(ctx)                     # fresh noise
+    assert not torch.equal(other, got)

@@ -45,3 +45,27 @@ def test_train_cli_writes_report(tmp_path):
     ck = torch.load(tmp_path / "ck" / "step-0000001.pt", weights_only=False)
     assert ck["step"] == 1 and "encoder.patch.weight" in ck["model"]
     assert os.path.getsize(tmp_path / "ck" / "step-0000001.pt") > 1e6
+
+
+def test_planner_eager_matches_model_plan():
+    """GraphedPlanner (eager on CPU) and NuVLA.plan give the same waypoints for the same noise."""
+    import torch
+
+    from nuvla_forge_b200.data import SampleSpec, SyntheticBatchSource
+    from nuvla_forge_b200.models import NuVLA, NuVLAConfig
+    from nuvla_forge_b200.serve import GraphedPlanner
+
+    cfg = NuVLAConfig.preset("tiny", fused=False)
+    torch.manual_seed(0)
+    model = NuVLA(cfg).eval()
+    for p in model.dit.out.parameters():     # the zero-initialised head would make every plan zero
+        torch.nn.init.normal_(p, std=0.1)
+    b = SyntheticBatchSource(SampleSpec.for_model(cfg), 2, pin=False).batch(0)
+    ctx = model.context(b["images"], b["text_tokens"])
+    z0 = torch.randn(2, model.dit.horizon, model.dit.traj_dim)
+    want = model.plan(b["images"], b["text_tokens"], steps=4, z0=z0)
+    planner = GraphedPlanner(model, batch_size=2, context_len=ctx.shape[1], steps=4)
+    got = planner(ctx, z0=z0)
+    assert got.shape == (2, model.dit.horizon, model.dit.traj_dim)
+    assert torch.allclose(got, want, atol=1e-5), float((got - want).abs().max())
+    assert float(got.abs().sum()) > 0
