@@ -97,6 +97,48 @@ def section_train(lines, reports: Path):
     lines.append("")
 
 
+def section_ag_gemm(lines, reports: Path):
+    lines += ["## All-gather fused into the first consuming GEMM", ""]
+    found = sorted(reports.glob("ag_gemm_n*.json"))
+    if not found:
+        lines += ["_Not run._", ""]
+        return
+    lines += ["| GPUs | unit -> GEMM | fused ms | hybrid ms | separate ms | copy-engine + GEMM ms | roofline ms | "
+              "fused fraction of roofline |", "|---|---|---|---|---|---|---|---|"]
+    for p in found:
+        d = json.loads(p.read_text())
+        for r in d["rows"]:
+            lines.append(f"| {d['world_size']} | {r['case']} | {fmt(r.get('fused_ms'), '.3f')} | "
+                         f"{fmt(r.get('fused_w_ce_ms'), '.3f')} | {fmt(r.get('separate_ms'), '.3f')} | "
+                         f"{fmt(r.get('separate_ce_ms'), '.3f')} | {fmt(r.get('roofline_ms'), '.3f')} "
+                         f"({r.get('roofline_bound')}) | {fmt(100 * r['frac_of_roofline'], '.0f')}% |")
+    lines.append("")
+
+
+def section_attention(lines, d):
+    lines += ["## Attention forward (tcgen05 kernel vs PyTorch SDPA / cuDNN)", ""]
+    if not d:
+        lines += ["_Not run._", ""]
+        return
+    lines += ["| shape | native ms | native TFLOP/s | SDPA ms | SDPA TFLOP/s |", "|---|---|---|---|---|"]
+    for r in d["rows"]:
+        lines.append(f"| {r['shape']} | {fmt(r['native_ms'], '.3f')} | {fmt(r['native_tflops'], '.0f')} | "
+                     f"{fmt(r['sdpa_ms'], '.3f')} | {fmt(r['sdpa_tflops'], '.0f')} |")
+    lines.append("")
+
+
+def section_planner(lines, d):
+    lines += ["## Planning latency (DiT sampling loop, eager vs CUDA graph)", ""]
+    if not d:
+        lines += ["_Not run._", ""]
+        return
+    lines += [f"Model `{d['model']}`, {d['steps']} Euler steps.", "", "| batch | eager ms | graphed ms | speed-up |",
+              "|---|---|---|---|"]
+    for r in d["rows"]:
+        lines.append(f"| {r['batch']} | {fmt(r['eager_ms'])} | {fmt(r['graphed_ms'])} | {fmt(r['speedup'])}x |")
+    lines.append("")
+
+
 def section_loader(lines, d):
     lines += ["## Data loading", ""]
     if not d:
@@ -121,6 +163,9 @@ def main(argv=None):
     section_train(lines, d)
     section_kernels(lines, _load(d, "kernels.json"))
     section_comms(lines, d)
+    section_ag_gemm(lines, d)
+    section_attention(lines, _load(d, "attention.json"))
+    section_planner(lines, _load(d, "planner.json"))
     section_loader(lines, _load(d, "dataloader.json"))
     Path(args.out).write_text("\n".join(lines) + "\n")
     print(f"wrote {args.out}")
