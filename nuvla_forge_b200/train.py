@@ -12,7 +12,8 @@ Parity: nuvla_forge/train.py:41-271 — the same flags and presets
 <phase>_ms/_pct for data/fwd_bwd/optim, world_size, batch_size, global_batch,
 samples_per_sec, peak_mem_mib, flags, model). Added: ``--model-config``
 (ref/tiny/1b/3b), ``--comm``, checkpointing (``--save-every``, ``--ckpt-dir``,
-``--resume``), ``--max-grad-norm``, max-over-ranks throughput and exposed
+``--resume``), ``--max-grad-norm``, ``--native-attention``, ``--no-fused-gather``,
+max-over-ranks throughput and exposed
 communication in the report. Differences that fix reference bugs: the backend
 follows the device (gloo on CPU), each micro-step consumes its own batch,
 the gradient norm under FSDP is global, and nothing syncs the host inside a
@@ -56,7 +57,8 @@ class Trainer:
     def __init__(self, cfg: NuVLAConfig, info: DistInfo | None = None, *, lr: float = 3e-4,
                  weight_decay: float = 0.01, max_grad_norm: float = 1.0, bucket_mb: float = 25.0,
                  comm: str = "auto", fsdp: bool = False, grad_accum: int = 1, no_sync_accum: bool = True,
-                 bf16: bool = True, grad_checkpoint: bool = False, seed: int = 1234, compile: bool = False):
+                 bf16: bool = True, grad_checkpoint: bool = False, seed: int = 1234, compile: bool = False,
+                 fused_gather: bool | None = None):
         self.info = info or setup_distributed()
         self.cfg = cfg
         self.device = self.info.device
@@ -72,7 +74,8 @@ class Trainer:
         param_dtype = torch.bfloat16 if (bf16 and self.device.type == "cuda") else torch.float32
         if fsdp:
             from .parallel.fsdp import FullyShardedDataParallel
-            self.model = FullyShardedDataParallel(model, param_dtype=param_dtype, comm=comm)
+            self.model = FullyShardedDataParallel(model, param_dtype=param_dtype, comm=comm,
+                                                  fuse_ag_gemm=fused_gather)
             self.opt = self.model.make_optimizer(lr=lr, weight_decay=weight_decay, max_grad_norm=max_grad_norm)
         else:
             self.model = DistributedDataParallel(model, bucket_cap_mb=bucket_mb, comm=comm, param_dtype=param_dtype)
@@ -178,6 +181,10 @@ def build_args(argv=None):
     p.add_argument("--fsdp", action="store_true")
     p.add_argument("--compile", action="store_true")
     p.add_argument("--comm", default="auto", choices=["auto", "fused", "nccl", "nccl_fp32", "gloo", "none"])
+    p.add_argument("--native-attention", action="store_true",
+                   help="attention forward on the tcgen05 kernel (backward recomputes through SDPA)")
+    p.add_argument("--no-fused-gather", action="store_true",
+                   help="FSDP: a separate all-gather before each block instead of the gather-fused GEMM")
     p.add_argument("--synthetic-source", action="store_true",
                    help="feed from the native pinned-batch generator instead of a DataLoader")
     p.add_argument("--profile", action="store_true")
@@ -245,10 +252,13 @@ def main(argv=None):
     tag = args.tag or args.preset
     cfg = NuVLAConfig.preset(args.model_config, fused=args.fused_kernels)
     spec = SampleSpec.for_model(cfg)
+    if args.native_attention:
+        from .ops import flash_attn
+        flash_attn.enable(True)
     trainer = Trainer(cfg, info, lr=args.lr, max_grad_norm=args.max_grad_norm, bucket_mb=args.ddp_bucket_mb,
                       comm=args.comm, fsdp=args.fsdp, grad_accum=args.grad_accum,
                       no_sync_accum=args.no_sync_accum, bf16=args.bf16, grad_checkpoint=args.grad_checkpoint,
-                      seed=args.seed, compile=args.compile)
+                      seed=args.seed, compile=args.compile, fused_gather=False if args.no_fused_gather else None)
     start_step = 0
     if args.resume:
         start_step = load_checkpoint(args.resume, trainer.model, trainer.opt)
