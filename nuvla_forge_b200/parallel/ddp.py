@@ -32,6 +32,7 @@ import torch.distributed as dist
 from torch import nn
 
 from .. import _native as nat
+from ..profiling import trace
 from .flat import FlatParamSpace
 from .symm import SLOT_DDP, SLOT_DDP_SMALL, SymmetricWorkspace, symmetric_memory_available
 
@@ -168,6 +169,10 @@ class DistributedDataParallel(nn.Module):
             self._next_launch += 1
 
     def _launch(self, b: Bucket) -> None:
+        with trace(f"ddp.allreduce[{b.start}:{b.end}]"):
+            self._launch_impl(b)
+
+    def _launch_impl(self, b: Bucket) -> None:
         b.launched = True
         g = self.space.grads[b.start: b.end]
         if self.comm_stream is None:

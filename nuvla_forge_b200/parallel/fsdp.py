@@ -60,6 +60,7 @@ import torch.distributed as dist
 from torch import nn
 
 from .. import _native as nat
+from ..profiling import trace
 from .symm import SLOT_AG, SLOT_AG_PREFETCH, SLOT_RS, SLOT_SCALAR, SymmetricWorkspace, symmetric_memory_available
 
 
@@ -295,6 +296,13 @@ class FullyShardedDataParallel(nn.Module):
         if u.gathered:
             self._ensure_ready(u)
             return
+        with trace(f"fsdp.gather[{u.name}]"):
+            self._gather_impl(u, lazy)
+
+    def _gather_impl(self, u: _Unit, lazy: bool) -> None:
+        if u.gathered:
+            self._ensure_ready(u)
+            return
         st = u.full.untyped_storage()
         nbytes = u.numel * u.full.element_size()
         if st.nbytes() != nbytes:
@@ -514,6 +522,10 @@ class FullyShardedDataParallel(nn.Module):
             self._next_rs += 1
 
     def _reduce_scatter(self, u: _Unit) -> None:
+        with trace(f"fsdp.reduce_scatter[{u.name}]"):
+            self._reduce_scatter_impl(u)
+
+    def _reduce_scatter_impl(self, u: _Unit) -> None:
         u.launched = True
         if u.acc32 is None:
             u.acc32 = torch.zeros(u.numel, dtype=torch.float32, device=self.device)

@@ -142,6 +142,37 @@ def load_measured_peaks(path: str | Path | None = None) -> dict:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
+_NVTX = None
+
+
+def trace(name: str):
+    """A named range for traces: a torch.profiler range (shown by ``make_profiler``), plus an NVTX
+    range for external tools when ``NFB_NVTX=1``. Costs nothing measurable when no profiler runs."""
+    global _NVTX
+    if _NVTX is None:
+        import os
+        _NVTX = os.environ.get("NFB_NVTX", "0") == "1" and torch.cuda.is_available()
+    if not _NVTX:
+        return torch.profiler.record_function(name)
+    return _Both(name)
+
+
+class _Both:
+    def __init__(self, name: str):
+        self.name = name
+        self.rf = torch.profiler.record_function(name)
+
+    def __enter__(self):
+        torch.cuda.nvtx.range_push(self.name)
+        self.rf.__enter__()
+        return self
+
+    def __exit__(self, *exc):
+        self.rf.__exit__(*exc)
+        torch.cuda.nvtx.range_pop()
+        return False
+
+
 class CommTimer:
     """Exposed communication: how long the compute stream waited on the collective stream.
 

@@ -43,7 +43,7 @@ from .models.nuvla import NuVLA, NuVLAConfig
 from .optim.adamw import FlatAdamW
 from .parallel.ddp import DistributedDataParallel
 from .parallel.dist import DistInfo, max_over_ranks, setup_distributed, teardown_distributed
-from .profiling import CommTimer, StepTimer, make_profiler
+from .profiling import CommTimer, StepTimer, make_profiler, trace
 
 BATCH_KEYS = ("images", "trajectory", "text_tokens", "text_targets")
 
@@ -121,15 +121,18 @@ class Trainer:
         for m, b in enumerate(on_dev):
             ctx = self.model.no_sync() if (self.no_sync_accum and m < n - 1) else nullcontext()
             with ctx:
-                out = self.model(b["images"], trajectory=b["trajectory"], text_tokens=b["text_tokens"],
-                                 text_targets=b["text_targets"])
+                with trace(f"forward[{m}]"):
+                    out = self.model(b["images"], trajectory=b["trajectory"], text_tokens=b["text_tokens"],
+                                     text_targets=b["text_targets"])
                 loss = out["loss"]
-                (loss / n).backward()
+                with trace(f"backward[{m}]"):
+                    (loss / n).backward()
             total = loss.detach() if total is None else total + loss.detach()
         if timer is not None:
             timer.mark("fwd_bwd")
-        self.opt.step()
-        self.opt.zero_grad(set_to_none=True)
+        with trace("optimizer"):
+            self.opt.step()
+            self.opt.zero_grad(set_to_none=True)
         if timer is not None:
             timer.mark("optim")
         self.step_count += 1

@@ -69,3 +69,24 @@ def test_planner_eager_matches_model_plan():
     assert got.shape == (2, model.dit.horizon, model.dit.traj_dim)
     assert torch.allclose(got, want, atol=1e-5), float((got - want).abs().max())
     assert float(got.abs().sum()) > 0
+
+
+def test_trainer_step_emits_named_trace_ranges():
+    """forward / backward / optimizer ranges appear in a torch.profiler trace of one step."""
+    import torch
+
+    from nuvla_forge_b200.data import SampleSpec, SyntheticBatchSource
+    from nuvla_forge_b200.models import NuVLAConfig
+    from nuvla_forge_b200.parallel.dist import DistInfo
+    from nuvla_forge_b200.train import Trainer
+
+    cfg = NuVLAConfig.preset("tiny", fused=False)
+    info = DistInfo(0, 1, 0, torch.device("cpu"), "none")
+    tr = Trainer(cfg, info, grad_accum=2, bf16=False)
+    src = SyntheticBatchSource(SampleSpec.for_model(cfg), 1, pin=False)
+    mbs = [src.batch(0), src.batch(1)]
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CPU]) as prof:
+        tr.step(mbs)
+    names = {e.name for e in prof.events()}
+    for want in ("forward[0]", "backward[1]", "optimizer"):
+        assert want in names, want
