@@ -39,9 +39,11 @@ clipping:
   reduce-scattered by ``nfb_rs_push`` (one kernel: bf16 cast of the fp32
   accumulator pushed to each slice's owner over NVLink, reduction in fp32,
   1/world scale, fp32 shard output), in a fixed unit order on every rank. With clipping off
-  (``max_grad_norm`` <= 0), ``nfb_rs_adamw`` instead applies AdamW to the
-  shard inside the reduce-scatter (fp32 master, moments and the bf16 shard the
-  next all-gather reads), and the optimizer step has nothing left to do.
+  (``max_grad_norm`` <= 0) and ``final_backward`` set by the caller (the last
+  backward before the optimizer step), ``nfb_rs_adamw`` instead applies AdamW
+  to the shard inside the reduce-scatter (fp32 master, moments and the bf16
+  shard the next all-gather reads), and the optimizer step has nothing left
+  to do.
 * The gradient norm for clipping is global: shard norms^2 are summed over ranks
   on the device (``nfb_allreduce_scalar``) before the update.
 
@@ -155,9 +157,14 @@ class FullyShardedDataParallel(nn.Module):
         import os
         env = os.environ.get("NFB_FSDP_AG_HYBRID")
         self.ag_hybrid = (env == "1") if env is not None else self.world > 2
-        self.fuse_rs_adamw = bool(fuse_rs_adamw and comm == "fused")
+        self.fuse_rs_adamw = bool(fuse_rs_adamw and comm in ("fused", "gloo"))
         self._opt = None
         self._fused_updates = 0
+        # Set by the caller (the Trainer does) when the coming backward is the last one before the
+        # optimizer step: only then may AdamW run inside the reduce-scatter (with gradient
+        # accumulation over several syncing backwards it would update on a partial gradient).
+        self.final_backward = False
+        self.fused_steps = 0           # optimizer steps applied inside the reduce-scatters
         self.shard_numel = sum(u.shard for u in self.units)
         self.master = torch.zeros(self.shard_numel, dtype=torch.float32, device=dev)
         self.grads = torch.zeros(self.shard_numel, dtype=torch.float32, device=dev)
@@ -569,7 +576,11 @@ class FullyShardedDataParallel(nn.Module):
             dist.all_reduce(full, group=self.group)
             lo = self.rank * u.shard
             red = full[lo: lo + u.shard] * scale
-            if self._shard_fresh:
+            if self._rs_adamw_active():
+                # same schedule as the fused device path: the shard's AdamW runs with its reduce-scatter
+                self._adamw_shard(u.shard_start, u.shard_start + u.shard, red)
+                self._fused_updates += 1
+            elif self._shard_fresh:
                 out.copy_(red)
             else:
                 out.add_(red)
@@ -654,8 +665,22 @@ class FullyShardedDataParallel(nn.Module):
 
     def _rs_adamw_active(self) -> bool:
         opt = self._opt
-        return (self.fuse_rs_adamw and opt is not None and self.require_sync
-                and not (opt.max_grad_norm is not None and opt.max_grad_norm > 0))
+        return (self.fuse_rs_adamw and opt is not None and self.require_sync and self.final_backward
+                and self._shard_fresh and not (opt.max_grad_norm is not None and opt.max_grad_norm > 0))
+
+    def _adamw_shard(self, lo: int, hi: int, g: torch.Tensor) -> None:
+        """AdamW on shard elements [lo, hi) with gradient g (host path of the fused RS + AdamW)."""
+        import math
+
+        opt = self._opt
+        b1, b2 = opt.betas
+        step = opt.step_count + 1
+        p, m, v = self.master[lo:hi], opt.m[lo:hi], opt.v[lo:hi]
+        p.mul_(1 - opt.lr * opt.weight_decay)
+        m.mul_(b1).add_(g, alpha=1 - b1)
+        v.mul_(b2).addcmul_(g, g, value=1 - b2)
+        denom = (v.sqrt() / math.sqrt(1 - b2 ** step)).add_(opt.eps)
+        p.addcdiv_(m, denom, value=-opt.lr / (1 - b1 ** step))
 
     def take_fused_step(self) -> bool:
         """True when every unit's AdamW update already ran inside its reduce-scatter this window."""
@@ -664,6 +689,7 @@ class FullyShardedDataParallel(nn.Module):
             return False
         if n != len(self.units):
             raise RuntimeError(f"fused reduce-scatter + AdamW updated {n} of {len(self.units)} units")
+        self.fused_steps += 1
         return True
 
     def check_health(self) -> None:

@@ -120,6 +120,8 @@ class Trainer:
         total = None
         for m, b in enumerate(on_dev):
             ctx = self.model.no_sync() if (self.no_sync_accum and m < n - 1) else nullcontext()
+            if hasattr(self.model, "final_backward"):   # FSDP may fuse AdamW into this backward's reduce-scatters
+                self.model.final_backward = m == n - 1
             with ctx:
                 with trace(f"forward[{m}]"):
                     out = self.model(b["images"], trajectory=b["trajectory"], text_tokens=b["text_tokens"],

@@ -169,3 +169,36 @@ def test_rest_copies_cover_unit_minus_prefix_and_weight():
                     assert not merged or merged[-1][1] < a, "overlap"
                     merged.append((a, b))
             assert merged == want, (merged, want)
+
+
+def _fsdp_rs_adamw(rank, world, fused):
+    """Clipping off, no_sync accumulation: AdamW inside the reduce-scatter (host path) vs the flat step."""
+    from nuvla_forge_b200.parallel.fsdp import FullyShardedDataParallel
+
+    torch.manual_seed(0)
+    net = Net()
+    fsdp = FullyShardedDataParallel(net, comm="gloo", unit_types=(Block,), fuse_rs_adamw=fused)
+    opt = fsdp.make_optimizer(lr=1e-2, max_grad_norm=0.0)
+    for step in range(3):
+        for m in range(2):
+            x, y = _data(step, rank, m)
+            ctx = fsdp.no_sync() if m == 0 else torch.enable_grad()
+            fsdp.final_backward = m == 1
+            with ctx:
+                (((fsdp(x) - y) ** 2).mean() / 2).backward()
+        opt.step()
+        opt.zero_grad()
+    views = fsdp.full_master_views()
+    return ({n: views[id(p)].clone() for n, p in net.named_parameters()} if rank == 0 else None,
+            fsdp.fused_steps, opt.step_count)
+
+
+def test_fsdp_rs_adamw_host_path_matches_flat_step():
+    a = run_ranks(_fsdp_rs_adamw, 2, args=(True,))
+    b = run_ranks(_fsdp_rs_adamw, 2, args=(False,))
+    assert all(st == "ok" for st, _ in a.values()) and all(st == "ok" for st, _ in b.values()), (a, b)
+    pa, fused_a, steps_a = a[0][1]
+    pb, fused_b, steps_b = b[0][1]
+    assert steps_a == steps_b == 3 and fused_a == 3 and fused_b == 0
+    for n, t in pb.items():
+        assert torch.allclose(pa[n], t, rtol=1e-5, atol=1e-6), n

@@ -237,6 +237,7 @@ def _fsdp_model(rank, world, fuse, fuse_rs=True, clip=1.0):
         for m in range(2):
             b = {k: v.to(dev) for k, v in src.batch(2 * step + m).items()}
             ctx = fsdp.no_sync() if m == 0 else torch.enable_grad()
+            fsdp.final_backward = m == 1      # AdamW may run inside this backward's reduce-scatters
             torch.manual_seed(10 * step + m)
             with ctx:
                 out = fsdp(b["images"], b["trajectory"], b["text_tokens"], b["text_targets"])
@@ -249,7 +250,7 @@ def _fsdp_model(rank, world, fuse, fuse_rs=True, clip=1.0):
     views = fsdp.full_master_views()
     params = {n: views[id(p)].cpu() for n, p in model.named_parameters()} if rank == 0 else None
     return {"losses": losses, "fused_launches": fsdp.ag_fused_launches, "params": params,
-            "streams": fsdp.comm_stream is not None}
+            "streams": fsdp.comm_stream is not None, "fused_steps": fsdp.fused_steps}
 
 
 def test_fsdp_ag_gemm_matches_plain_gather():
@@ -274,6 +275,7 @@ def test_fsdp_rs_adamw_matches_unfused():
     a = run_ranks(_fsdp_model, w, args=(True, True, 0.0), backend="nccl", env=ENV, timeout_s=240, join_s=400)
     b = run_ranks(_fsdp_model, w, args=(True, False, 0.0), backend="nccl", env=ENV, timeout_s=240, join_s=400)
     assert all(st == "ok" for st, _ in a.values()) and all(st == "ok" for st, _ in b.values()), (a, b)
+    assert a[0][1]["fused_steps"] == 3 and b[0][1]["fused_steps"] == 0
     for la, lb in zip(a[0][1]["losses"], b[0][1]["losses"]):
         assert abs(la - lb) < 1e-2 * max(1.0, abs(lb)), (la, lb)
     for n, t in b[0][1]["params"].items():
