@@ -1,5 +1,6 @@
 """CPU checks of the op layer (reference paths, dispatch, API parity)."""
 
+import pytest
 import torch
 
 from nuvla_forge_b200.kernels import (HAS_NATIVE, chunked_cross_entropy, fused_adaln_residual_rmsnorm,
@@ -95,3 +96,22 @@ def test_patchify_matches_conv_layout():
     out = rows @ conv.weight.reshape(5, -1).t() + conv.bias
     assert torch.allclose(out, ref, atol=1e-4)
     assert torch.equal(patchify_ref(img, 16, 776, torch.float32)[..., 768:], torch.zeros(2, 6, 8))
+
+
+@pytest.mark.parametrize("preset,over", [("ref", {"image_size": 32}), ("tiny", {"image_size": 32})])
+def test_model_forward_backward_cpu(preset, over):
+    """Both layouts (reference scene-query pooling; BASELINE backbone over image tokens) train on CPU."""
+    from nuvla_forge_b200.data import SampleSpec, SyntheticBatchSource
+    from nuvla_forge_b200.models import NuVLA, NuVLAConfig
+
+    cfg = NuVLAConfig.preset(preset, fused=False, **over)
+    torch.manual_seed(0)
+    model = NuVLA(cfg)
+    b = SyntheticBatchSource(SampleSpec.for_model(cfg), 2, pin=False).batch(0)
+    out = model(b["images"], b["trajectory"], b["text_tokens"], b["text_targets"])
+    assert set(out) >= {"loss", "plan_loss", "reason_loss"}
+    assert torch.isfinite(out["loss"]) and float(out["loss"]) > 0
+    out["loss"].backward()
+    grads = [p.grad for p in model.parameters() if p.requires_grad]
+    assert sum(g is not None for g in grads) > 0.9 * len(grads)
+    assert all(torch.isfinite(g).all() for g in grads if g is not None)
