@@ -23,16 +23,16 @@ clipping:
   With more than two ranks (``ag_hybrid``), once the consuming weight is known
   (after a unit's first forward) the kernel gathers only that weight and the
   rest of the unit goes to the copy engines on the prefetch stream,
-  concurrently. Other
-  units use ``nfb_allgather`` (each rank pulls its peers' shards). Backward: a
-  hook on the unit's outputs gathers it again (``nfb_allgather``) before its
-  backward runs.
+  concurrently. The root unit's gather opens every step with the
+  ``nfb_allgather`` kernel, whose rank barrier is what makes every later
+  gather of the step safe without one (see ``_launch_allgather``); all other
+  gathers are copy-engine transfers, one per shard. Backward: a hook on the
+  unit's outputs gathers it again before its backward runs.
 * Overlap (fused comm): reduce-scatters run on a communication stream as
   soon as a unit's gradients are complete, and while a unit's backward runs
-  the next unit's parameters are gathered on a prefetch stream (its own flag
-  slot, so the two streams' collectives never share an epoch sequence); the
-  compute stream waits for the prefetch only when it needs the unit, and for
-  the reduce-scatters only at the end of backward.
+  the next unit's parameters are gathered by the copy engines on a prefetch
+  stream; the compute stream waits for the prefetch only when it needs the
+  unit, and for the reduce-scatters only at the end of backward.
 * Gradients: bf16 gradients are folded into a per-unit fp32 accumulator
   (exact across micro-steps); when a unit's gradients are complete on a
   syncing micro-step they are cast to bf16 into peer-mapped memory and
