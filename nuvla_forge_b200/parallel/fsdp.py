@@ -63,7 +63,7 @@ from torch import nn
 
 from .. import _native as nat
 from ..profiling import trace
-from .symm import SLOT_AG, SLOT_AG_PREFETCH, SLOT_RS, SLOT_SCALAR, SymmetricWorkspace, symmetric_memory_available
+from .symm import SLOT_AG, SLOT_RS, SLOT_SCALAR, SymmetricWorkspace, symmetric_memory_available
 
 
 def _round(n: int, a: int) -> int:
@@ -293,7 +293,7 @@ class FullyShardedDataParallel(nn.Module):
             st.resize_(nbytes)
         # the new storage may reuse memory the compute stream used until now
         self.ag_stream.wait_stream(torch.cuda.current_stream(self.device))
-        self._launch_allgather(u, stream=self.ag_stream, slot=SLOT_AG_PREFETCH, barrier=False)
+        self._launch_allgather(u, stream=self.ag_stream, barrier=False)
         ev = torch.cuda.Event()
         ev.record(self.ag_stream)
         u.ready_event = ev
