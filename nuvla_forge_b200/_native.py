@@ -69,6 +69,12 @@ _SIGS: dict[str, tuple] = {
     "nfb_ag_gemm": (I, [P, I, I, L, L, P, L, L, L, I, I, P, L, I, P, L, P, P, P]),
     "nfb_ag_gemm_max_nblocks": (I, []),
     "nfb_copy_async": (I, [P, P, L, P]),
+    "nfb_gemm": (I, [P, P, P, I, I, I, L, L, L, I, I, I, P, P, L, P, P]),
+    "nfb_gemm_acc": (I, [P, P, P, I, I, I, L, L, L, I, I, I, I, P, L, U32, P, P]),
+    "nfb_gemm_acc_splits": (I, [I, I, I]),
+    "nfb_gemm_max_clusters": (I, []),
+    "nfb_gemm_small": (I, [I, I, P, L, L, P, L, L, P, L, L, P, I, I, I, I, P]),
+    "nfb_gemm_last_error": (ctypes.c_char_p, []),
 }
 
 _lib = None
@@ -152,7 +158,10 @@ def call(name: str, *args) -> int:
     _launches[0] += 1
     rc = fn(*args)
     if rc != 0:
-        raise NativeError(f"{name} failed with CUDA error {rc} ({_err_name(rc)})")
+        detail = ""
+        if name.startswith("nfb_gemm"):
+            detail = f": {lib().nfb_gemm_last_error().decode()}"
+        raise NativeError(f"{name} failed with CUDA error {rc} ({_err_name(rc)}){detail}")
     return rc
 
 

@@ -95,6 +95,34 @@ def tc_gemm(iters):
 
 
 @case
+def gemm_pair(iters):
+    """CTA-pair tcgen05 GEMM, 8192 x 8192 x 8192 bf16 -> bf16 (forward layout)."""
+    from ..ops.linear import gemm
+    a, b = _bf(8192, 8192), _bf(8192, 8192, seed=1)
+    for _ in range(iters):
+        gemm(a, b)
+
+
+@case
+def gemm_pair_vit_qkv(iters):
+    """CTA-pair GEMM at the ViT qkv forward shape (K = 1024), 32768 tokens: y [32768, 3072]."""
+    from ..ops.linear import gemm
+    x, w = _bf(32768, 1024), _bf(3072, 1024, seed=1)
+    for _ in range(iters):
+        gemm(x, w)
+
+
+@case
+def gemm_pair_wgrad(iters):
+    """CTA-pair GEMM weight gradient at the backbone proj shape: dW [2048, 2048] fp32 over 27136 tokens."""
+    from ..ops.linear import gemm_acc
+    dy, x = _bf(27136, 2048), _bf(27136, 2048, seed=1)
+    dw = torch.zeros(2048, 2048, dtype=torch.float32, device="cuda")
+    for _ in range(iters):
+        gemm_acc(dy, x, dw, a_mn=True, b_mn=True)
+
+
+@case
 def ce_tc(iters):
     """Cross entropy on tcgen05 at BASELINE config 2: hidden [16384, 2048], W [32000, 2048]."""
     from ..ops.ce_tc import cross_entropy_tc

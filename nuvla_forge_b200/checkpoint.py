@@ -6,7 +6,11 @@ checkpoint written here loads into the reference's ``NuVLA`` with
 ``load_state_dict`` (for the default config). File layout::
 
     {"model": {name: fp32 tensor, ...},        # full, unsharded, reference key names
-     "optim": {...}, "step": int, "rng": {...}, "config": {...}}
+     "optim": {...}, "step": int, "rng": {...}, "rng_per_rank": [{...}, ...], "config": {...}}
+
+Every rank's RNG state is saved (ranks draw different noise: the trainer seeds
+rank r with seed + r), and each rank restores its own on resume; with a
+different world size a rank without an entry is reseeded from (seed, rank, step).
 
 Model tensors come from the fp32 master weights (not the bf16 compute copy).
 Under FSDP the shards are gathered to rank 0, which writes the file.
@@ -71,15 +75,38 @@ def save_checkpoint(path: str | Path, wrapper, optimizer, step: int, config: dic
     if hasattr(wrapper, "gather_optimizer_state"):
         optim_sd = wrapper.gather_optimizer_state(optimizer)
     rank = dist.get_rank() if dist.is_initialized() else 0
+    mine = rng_state()
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        per_rank = [None] * dist.get_world_size()
+        dist.all_gather_object(per_rank, mine)
+    else:
+        per_rank = [mine]
     if rank == 0:
         path = Path(path)
         path.parent.mkdir(parents=True, exist_ok=True)
         tmp = path.with_suffix(path.suffix + ".tmp")
-        torch.save({"model": sd, "optim": optim_sd, "step": int(step), "rng": rng_state(),
+        torch.save({"model": sd, "optim": optim_sd, "step": int(step), "rng": mine, "rng_per_rank": per_rank,
                     "config": config or {}}, tmp)
         os.replace(tmp, path)
     if dist.is_initialized():
         dist.barrier()
+
+
+def restore_rng(ck: dict, rank: int, world: int, seed: int = 1234) -> str:
+    """Restore this rank's RNG from checkpoint ``ck``. Returns "own", "reseeded" or "none"."""
+    per_rank = ck.get("rng_per_rank")
+    try:
+        if per_rank and len(per_rank) == world and per_rank[rank] is not None:
+            set_rng_state(per_rank[rank])
+            return "own"
+        if per_rank or ck.get("rng"):
+            # the world size changed: keep the Python/NumPy streams of rank 0, give torch a distinct seed
+            set_rng_state((per_rank or [ck["rng"]])[0])
+            torch.manual_seed(seed + rank + 1000003 * int(ck.get("step", 0)))
+            return "reseeded"
+    except Exception:  # noqa: BLE001 - RNG layout differs across versions: not fatal
+        pass
+    return "none"
 
 
 def load_checkpoint(path: str | Path, wrapper, optimizer=None) -> int:
@@ -92,11 +119,9 @@ def load_checkpoint(path: str | Path, wrapper, optimizer=None) -> int:
         _load_into_space(wrapper, ck["model"])
         if optimizer is not None and ck.get("optim"):
             optimizer.load_state_dict(ck["optim"])
-    if ck.get("rng"):
-        try:
-            set_rng_state(ck["rng"])
-        except Exception:  # noqa: BLE001 - RNG layout differs across versions: not fatal
-            pass
+    rank = dist.get_rank() if dist.is_initialized() else 0
+    world = dist.get_world_size() if dist.is_initialized() else 1
+    restore_rng(ck, rank, world)
     return int(ck.get("step", 0))
 
 

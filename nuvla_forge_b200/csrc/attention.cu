@@ -424,6 +424,8 @@ static int make_tmap_bshd(CUtensorMap* m, const void* base, int Bn, int Sn, int 
                           int64_t sh, int box_rows) {
   int rc = get_encode();
   if (rc) return rc;
+  rc = bind_device_of(base);
+  if (rc) return rc;
   if ((reinterpret_cast<uintptr_t>(base) & 15) || (sb * 2) % 16 || (ss * 2) % 16 || (sh * 2) % 16)
     return (int)cudaErrorInvalidValue;
   cuuint64_t dims[4] = {(cuuint64_t)Dn, (cuuint64_t)Hn, (cuuint64_t)Sn, (cuuint64_t)Bn};

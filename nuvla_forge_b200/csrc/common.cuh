@@ -12,6 +12,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include "nfb_api.h"
+
 #define NFB_API extern "C" __attribute__((visibility("default")))
 
 #ifndef NFB_CHECK_LAUNCH

@@ -1,0 +1,587 @@
+// Blackwell (sm_100a) CTA-pair tensor-core GEMM: cta_group::2 tcgen05.mma on 256 x 256 tiles.
+//
+//   C[m, n] = sum_k A[m, k] * B[n, k]          A, B bf16; fp32 accumulate in TMEM
+//
+// A cluster of two CTAs (one per SM) owns one 256 x 256 output tile at a time:
+//   * CTA r of the pair loads rows [m0 + 128 r, +128) of A and rows [n0 + 128 r, +128) of B
+//     (64 K columns per stage, 128-byte swizzle) into its own shared memory with plain TMA
+//     loads (no multicast); both CTAs' loads complete on the LEADER's (rank 0) stage barrier,
+//     which the leader arms with the bytes of both halves.
+//   * the leader's elected MMA thread issues tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16):
+//     the tensor cores of both SMs read A from their own CTA and the two B halves from both,
+//     and each CTA's TMEM receives its 128 rows x 256 fp32 columns of the tile.
+//   * tcgen05.commit with a CTA mask signals both CTAs' "stage empty" and "accumulator full"
+//     barriers; the epilogue warps of both CTAs release the accumulator on the leader's barrier
+//     with remote mbarrier arrives.
+// Per CTA per stage the shared-memory operand traffic is 32 KB for 2 * 128 * 256 * 64 FLOP
+// (the single-CTA 128 x 256 tile needs 48 KB for the same work), so the MMA is not bound by
+// shared-memory bandwidth, and each B tile is fetched from L2 once per pair.
+//
+// Each operand is K-major (A [M, K], B [N, K], K contiguous) or MN-major (A stored [K, M],
+// B stored [K, N]); MN-major tiles are loaded as 64-column boxes and described with the
+// instruction descriptor's transpose bits. The three GEMMs of a linear layer map onto it as
+//   forward  Y = X W^T:   A = X  (K-major),  B = W  (K-major)
+//   dgrad    dX = dY W:   A = dY (K-major),  B = W  (MN-major)
+//   wgrad    dW = dY^T X: A = dY (MN-major), B = X  (MN-major)
+//
+// Persistent: the grid is (co-resident clusters) x 2 CTAs, work items are taken round-robin.
+// A work item is (tile, split): with split-K, consecutive items are the K slices of one tile and
+// the epilogue accumulates them in order (split j waits, bounded, for split j-1's flag), so the
+// result does not depend on timing. Every item of the kernel only waits for items with smaller
+// indices, which co-resident clusters process in increasing order: no wait cycle exists.
+//
+// Roles per CTA (192 threads): warp 0 TMA producer, warp 1 MMA issuer (leader CTA) and TMEM
+// allocator (both CTAs), warps 2-5 epilogue (warp w reads TMEM lanes 32 (w % 4) .. +31: one
+// output row per thread). Two 256-column TMEM accumulators let the epilogue of one item
+// overlap the main loop of the next.
+//
+// Every wait is bounded by %globaltimer: a timeout records a code in the status word, raises
+// the CTA's abort flag (the other roles stop at their next wait), the producer waits (bounded)
+// for the copies it can observe, and both CTAs meet at the closing cluster barrier before the
+// TMEM is freed.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+#include "tc_gemm.cuh"
+
+namespace nfb {
+namespace g2 {
+
+
+using tc::mbar_arrive_expect_tx;
+using tc::mbar_init;
+using tc::mbar_try_wait;
+using tc::mbar_wait;
+using tc::prefetch_tmap;
+using tc::smem_u32;
+using tc::sw128_desc;
+using tc::sw128_mn_desc;
+using tc::tmem_fence_after;
+using tc::tmem_fence_before;
+using tc::tmem_ld32;
+
+constexpr int TM = 256;                   // tile rows (128 per CTA)
+constexpr int TN = 256;                   // tile columns (B rows: 128 per CTA)
+constexpr int HALF = 128;
+constexpr int BK = 64;
+constexpr int kStages = 6;
+constexpr int kABytes = HALF * BK * 2;    // 16 KB
+constexpr int kBBytes = HALF * BK * 2;    // 16 KB
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;       // two 256-column fp32 accumulators
+constexpr uint64_t kWaitNs = 2000000000ull;
+
+struct alignas(8) Shared {
+  uint64_t full[kStages];     // leader: both CTAs' bytes of a stage landed
+  uint64_t empty[kStages];    // every CTA: the MMAs reading a stage are done
+  uint64_t tmem_full[2];      // every CTA: an accumulator is complete
+  uint64_t tmem_empty[2];     // leader: the 8 epilogue warps of the pair read an accumulator
+  uint64_t mma_drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr size_t kSharedSlot = 1024;
+static_assert(sizeof(Shared) <= kSharedSlot, "Shared must fit its slot");
+// Epilogue staging: per epilogue warp two 32-row x 64-byte buffers (32 bf16 columns), written
+// with the 64-byte swizzle and drained by TMA stores.
+constexpr int kEpiBufBytes = 32 * 64;
+constexpr size_t kEpiSmem = 4 * 2 * kEpiBufBytes;
+constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + kSharedSlot + kEpiSmem + 1024;
+static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+
+__device__ __forceinline__ uint32_t cta_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+// TMA tile load into this CTA's shared memory whose completion is counted on an mbarrier that
+// may live in the peer CTA of the pair (cluster address).
+__device__ __forceinline__ void tma_load_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive (once the MMAs issued so far complete) on the mbarrier at this shared-memory offset
+// in both CTAs of the pair.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  const uint16_t mask = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+      ::"r"(smem_u32(bar)), "h"(mask)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit_local(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Arrive on an mbarrier of a CTA of the cluster. Only the TMEM reads before it need ordering, and
+// tcgen05.fence::before_thread_sync gives that, so no cluster-wide release of global stores.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+// 2-D TMA store of a shared-memory box to global memory (bulk async-group of this thread).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most one of this thread's bulk groups still reads shared memory.
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+struct Work {
+  int M, N, K;
+  int m_tiles, n_tiles;
+  int k_blocks;
+  int splits;          // K slices per tile (1: no split)
+  int kb_per_split;    // 64-wide K blocks per slice (the last slice may be shorter)
+  int group;           // tile raster: groups of `group` M tiles, N-major inside a group
+  int items;           // m_tiles * n_tiles * splits
+};
+
+struct Item {
+  int m_blk, n_blk, split, tile;
+  int kb0, kb1;        // K blocks [kb0, kb1)
+};
+
+__device__ __forceinline__ Item item_at(const Work& w, int it) {
+  Item r;
+  r.tile = it / w.splits;
+  r.split = it - r.tile * w.splits;
+  const int per_group = w.group * w.n_tiles;
+  const int g = r.tile / per_group;
+  const int within = r.tile - g * per_group;
+  const int rows_in_group = min(w.group, w.m_tiles - g * w.group);
+  r.n_blk = within / rows_in_group;
+  r.m_blk = g * w.group + within % rows_in_group;
+  r.kb0 = r.split * w.kb_per_split;
+  r.kb1 = min(w.k_blocks, r.kb0 + w.kb_per_split);
+  return r;
+}
+
+// What an epilogue warp gets: its 32 rows start at row0 (lane l owns row row0 + l), the tile's
+// columns start at n0; taddr is the TMEM address of (its first lane, the accumulator's column 0).
+struct EpiCtx {
+  int row0, n0;
+  int split, splits, tile;
+  int slot;            // (tile's warp slot) = cta * 4 + quarter, for per-warp split-K flags
+  uint32_t taddr;
+  int lane;
+  uint8_t* smem;            // this warp's two staging buffers (1024-byte aligned)
+  const CUtensorMap* tmap_c; // output tensor map (bf16 [M, N], 32 x 32 boxes, 64-byte swizzle) or null
+};
+
+// Epi must provide: __device__ bool warp(const EpiCtx&, const Work&, volatile int* abort, uint32_t* status)
+// (every lane of the warp calls it; false = a bounded wait gave up) and __device__ void finish(const
+// EpiCtx&) (every lane, after the warp's last tile: complete outstanding stores).
+template <bool A_MN, bool B_MN, class Epi>
+__device__ void gemm_pair_body(const CUtensorMap* tma_a, const CUtensorMap* tma_b, const CUtensorMap* tma_c,
+                               const Work& w, Epi& epi, uint32_t* status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Shared* S = reinterpret_cast<Shared*>(smem + (size_t)kStages * kStageBytes);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cta_rank();
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1;
+  const int n_clusters = gridDim.x >> 1;
+  volatile int* abort_flag = &S->abort;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&S->full[s], 1);
+      mbar_init(&S->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&S->tmem_full[a], 1);
+      mbar_init(&S->tmem_empty[a], 8);   // 4 epilogue warps x 2 CTAs
+    }
+    mbar_init(&S->mma_drain, 1);
+    S->abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(smem_u32(&S->tmem_base)), "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tmem_fence_before();
+  cluster_sync();          // barriers of both CTAs initialised, TMEM allocated in both
+  tmem_fence_after();
+  const uint32_t tmem_base = S->tmem_base;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      prefetch_tmap(tma_a);
+      prefetch_tmap(tma_b);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int it = cluster; it < w.items && ok; it += n_clusters) {
+        const Item I = item_at(w, it);
+        const int arow = I.m_blk * TM + HALF * (int)rank;
+        const int brow = I.n_blk * TN + HALF * (int)rank;
+        for (int kb = I.kb0; kb < I.kb1; ++kb) {
+          if (!mbar_wait(&S->empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
+          uint8_t* sa = smem + (size_t)stage * kStageBytes;
+          uint8_t* sb = sa + kABytes;
+          const uint32_t bar = map_to(smem_u32(&S->full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&S->full[stage], 2 * kStageBytes);
+          if (A_MN) {
+            tma_load_pair(sa, tma_a, bar, arow, kb * BK);
+            tma_load_pair(sa + BK * 128, tma_a, bar, arow + 64, kb * BK);
+          } else {
+            tma_load_pair(sa, tma_a, bar, kb * BK, arow);
+          }
+          if (B_MN) {
+            tma_load_pair(sb, tma_b, bar, brow, kb * BK);
+            tma_load_pair(sb + BK * 128, tma_b, bar, brow + 64, kb * BK);
+          } else {
+            tma_load_pair(sb, tma_b, bar, kb * BK, brow);
+          }
+          ++issued;
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (!ok) {
+        set_status(status, kTimeoutFlag, 200 + rank);
+        S->abort = 1;
+        // The leader can observe the stage barriers; wait (bounded) for its latest loads.
+        if (leader) {
+          const uint32_t first = issued > (uint32_t)kStages ? issued - (uint32_t)kStages : 0u;
+          for (uint32_t i = first; i < issued; ++i) {
+            const uint64_t t0 = globaltimer_ns();
+            while (!mbar_try_wait(&S->full[i % kStages], (i / kStages) & 1u)) {
+              if (globaltimer_ns() - t0 > kWaitNs) break;
+            }
+          }
+        } else {
+          // the peer's copies complete on the leader's barriers: give them a bounded moment to land
+          const uint64_t t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 200000ull) { }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader CTA only) ----------------
+    if (leader && lane == 0) {
+      const uint32_t idesc = tc::idesc_bf16(TM, TN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int it = cluster; it < w.items && ok; it += n_clusters) {
+        const Item I = item_at(w, it);
+        if (!mbar_wait(&S->tmem_empty[acc], acc_phase ^ 1u, abort_flag)) { ok = false; break; }
+        tmem_fence_after();
+        const uint32_t tmem_d = tmem_base + (uint32_t)(acc * TN);
+        for (int kb = I.kb0; kb < I.kb1; ++kb) {
+          if (!mbar_wait(&S->full[stage], phase, abort_flag)) { ok = false; break; }
+          tmem_fence_after();
+          const uint32_t sa = smem_u32(smem + (size_t)stage * kStageBytes);
+          const uint32_t sb = sa + kABytes;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? sw128_mn_desc(sa + kk * 16 * 128) : sw128_desc(sa + kk * 32);
+            const uint64_t bd = B_MN ? sw128_mn_desc(sb + kk * 16 * 128) : sw128_desc(sb + kk * 32);
+            umma_pair(tmem_d, ad, bd, idesc, (kb > I.kb0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit_pair(&S->empty[stage]);
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit_pair(&S->tmem_full[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+      if (!ok) {
+        set_status(status, kTimeoutFlag, 202);
+        S->abort = 1;
+      }
+      umma_commit_local(&S->mma_drain);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&S->mma_drain, 0u)) {
+        if (globaltimer_ns() - t0 > kWaitNs) break;
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5, both CTAs) ----------------
+    const int quarter = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const uint32_t empty_leader0 = map_to(smem_u32(&S->tmem_empty[0]), 0);
+    const uint32_t empty_leader1 = map_to(smem_u32(&S->tmem_empty[1]), 0);
+    EpiCtx c;
+    c.lane = lane;
+    c.smem = reinterpret_cast<uint8_t*>(S) + kSharedSlot + (size_t)quarter * 2 * kEpiBufBytes;
+    c.tmap_c = tma_c;
+    for (int it = cluster; it < w.items; it += n_clusters) {
+      bool ok = mbar_wait(&S->tmem_full[acc], acc_phase, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) {
+        if (lane == 0) {
+          set_status(status, kTimeoutFlag, 203);
+          S->abort = 1;
+        }
+        break;
+      }
+      tmem_fence_after();
+      const Item I = item_at(w, it);
+      c.row0 = I.m_blk * TM + HALF * (int)rank + quarter * 32;
+      c.n0 = I.n_blk * TN;
+      c.split = I.split;
+      c.splits = w.splits;
+      c.tile = I.tile;
+      c.slot = (int)rank * 4 + quarter;
+      c.taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * TN);
+      const bool eok = epi.warp(c, w, abort_flag, status);
+      tmem_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc ? empty_leader1 : empty_leader0);
+      if (!eok) break;
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+    epi.finish(c);
+  }
+
+  tmem_fence_before();
+  __syncthreads();
+  __syncwarp();
+  cluster_sync();          // the peer's MMAs and arrives that touch this CTA are over
+  tmem_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Epilogues
+// ---------------------------------------------------------------------------
+
+// Y = acc (+ bias[n]) (+ R[m, n]) stored as bf16 (or fp32 with out_f32).
+// bf16 output with a tensor map: each 32-column chunk of the warp's 32 rows is converted, written
+// to a staging buffer (64-byte rows, 64-byte swizzle: 16-byte chunk j of row r sits at chunk
+// j ^ ((r >> 1) & 3), so a warp's 16-byte writes hit every bank group evenly) and stored by one
+// TMA store (full lines, out-of-range rows and columns clipped by the TMA unit); two buffers per
+// warp alternate. Otherwise each thread stores its row directly.
+struct LinearEpi {
+  void* C;
+  int64_t ldc;
+  const __nv_bfloat16* bias;   // [N] or null
+  const __nv_bfloat16* R;      // [M, N] residual or null
+  int64_t ldr;
+  int out_f32;
+  int vec_ok;                  // C (and R) rows 16-byte aligned
+  int use_tma;                 // bf16 output through the staged TMA store
+  uint32_t chunk;              // chunks this warp has staged so far (buffer = chunk & 1)
+
+  __device__ __forceinline__ void add_bias_res(float* v, int m, int n, int N, bool full) const {
+    if (bias) {
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          float b[8];
+          load16<__nv_bfloat16>(bias + n + j, b);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) v[j + q] += b[q];
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) if (n + j < N) v[j] += __bfloat162float(bias[n + j]);
+      }
+    }
+    if (R) {
+      const __nv_bfloat16* r = R + (int64_t)m * ldr + n;
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          float b[8];
+          load16<__nv_bfloat16>(r + j, b);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) v[j + q] += b[q];
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) if (n + j < N) v[j] += __bfloat162float(r[j]);
+      }
+    }
+  }
+
+  __device__ bool warp(const EpiCtx& c, const Work& w, volatile int*, uint32_t*) {
+    const int m = c.row0 + c.lane;
+    const bool live = m < w.M;
+    if (use_tma) {
+#pragma unroll 1
+      for (int cc = 0; cc < TN; cc += 32) {
+        float v[32];
+        tmem_ld32(c.taddr + cc, v);
+        const int n = c.n0 + cc;
+        if (c.row0 >= w.M || n >= w.N) continue;        // whole chunk outside C (warp-uniform)
+        if (live) add_bias_res(v, m, n, w.N, vec_ok && n + 32 <= w.N);
+        uint8_t* buf = c.smem + (chunk & 1u) * kEpiBufBytes;
+        if (chunk >= 2) {
+          if (c.lane == 0) bulk_wait_read1();           // the store that last used this buffer read it
+          __syncwarp();
+        }
+        const int r = c.lane;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          Vec16<__nv_bfloat16> q;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) q.v[e] = __float2bfloat16_rn(v[8 * j + e]);
+          const int pj = j ^ ((r >> 1) & 3);
+          *reinterpret_cast<uint4*>(buf + r * 64 + pj * 16) = q.u;
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (c.lane == 0) {
+          tma_store_2d(c.tmap_c, buf, n, c.row0);
+          bulk_commit();
+        }
+        ++chunk;
+      }
+      return true;
+    }
+#pragma unroll 1
+    for (int cc = 0; cc < TN; cc += 32) {
+      float v[32];
+      tmem_ld32(c.taddr + cc, v);
+      const int n = c.n0 + cc;
+      if (!live || n >= w.N) continue;
+      const bool full = vec_ok && n + 32 <= w.N;
+      add_bias_res(v, m, n, w.N, full);
+      if (out_f32) {
+        float* dst = reinterpret_cast<float*>(C) + (int64_t)m * ldc + n;
+        if (full) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) if (n + j < w.N) dst[j] = v[j];
+        }
+      } else {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(C) + (int64_t)m * ldc + n;
+        if (full) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) store16<__nv_bfloat16>(dst + j, v + j);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) if (n + j < w.N) dst[j] = __float2bfloat16_rn(v[j]);
+        }
+      }
+    }
+    return true;
+  }
+
+  __device__ void finish(const EpiCtx& c) {
+    if (use_tma && c.lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+};
+
+// fp32 C = acc (overwrite) or C += acc (accumulate), with ordered split-K: split 0 writes (or
+// adds to the caller's C), split j > 0 waits for split j-1 of the same rows and adds.
+// flags: one 32-bit word per (tile, warp slot); a value (epoch << 8) | j means "splits < j done".
+struct AccumF32Epi {
+  float* C;
+  int64_t ldc;
+  int accumulate;
+  int vec_ok;
+  uint32_t* flags;
+  uint32_t epoch;
+
+  __device__ bool warp(const EpiCtx& c, const Work& w, volatile int* abort_flag, uint32_t* status) {
+    const int m = c.row0 + c.lane;
+    const bool live = m < w.M;
+    uint32_t* flag = flags ? flags + (int64_t)c.tile * 8 + c.slot : nullptr;
+    bool ok = true;
+    if (c.split > 0) {
+      if (c.lane == 0) {
+        const uint32_t want = (epoch << 8) | (uint32_t)c.split;
+        const uint64_t t0 = globaltimer_ns();
+        uint32_t spins = 0;
+        while (ld_acquire_gpu(flag) != want) {
+          if ((++spins & 63u) == 0 && (*abort_flag || globaltimer_ns() - t0 > kWaitNs)) { ok = false; break; }
+        }
+        if (!ok) set_status(status, kTimeoutFlag, 210);
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      __syncwarp();
+    }
+    const bool add = accumulate || c.split > 0;
+#pragma unroll 1
+    for (int cc = 0; cc < TN; cc += 32) {
+      float v[32];
+      tmem_ld32(c.taddr + cc, v);
+      const int n = c.n0 + cc;
+      if (!ok || !live || n >= w.N) continue;
+      float* dst = C + (int64_t)m * ldc + n;
+      if (vec_ok && n + 32 <= w.N) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          if (add) {
+            const float4 p = *reinterpret_cast<const float4*>(dst + j);
+            o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
+          }
+          *reinterpret_cast<float4*>(dst + j) = o;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (n + j < w.N) dst[j] = add ? dst[j] + v[j] : v[j];
+      }
+    }
+    if (ok && c.split + 1 < c.splits) {
+      __syncwarp();
+      if (c.lane == 0) {
+        __threadfence();
+        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"((epoch << 8) | (uint32_t)(c.split + 1))
+                     : "memory");
+      }
+    }
+    return ok;
+  }
+
+  __device__ void finish(const EpiCtx&) {}
+};
+
+}  // namespace g2
+}  // namespace nfb

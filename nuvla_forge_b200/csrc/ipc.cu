@@ -9,6 +9,8 @@
 #include <stdint.h>
 #include <string.h>
 
+#include "nfb_api.h"
+
 #define NFB_API extern "C" __attribute__((visibility("default")))
 
 NFB_API int nfb_ipc_handle_bytes() { return (int)sizeof(cudaIpcMemHandle_t); }

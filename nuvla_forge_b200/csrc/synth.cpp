@@ -13,6 +13,8 @@
 #include <thread>
 #include <vector>
 
+#include "nfb_api.h"
+
 #define NFB_HOST_API extern "C" __attribute__((visibility("default")))
 
 namespace {

@@ -22,9 +22,26 @@ static int get_encode() {
   return 0;
 }
 
+// Make the context of the device that owns `p` current in this host thread. Threads that torch
+// starts (the autograd engine's device threads, Python threads) may have no current context;
+// encoding a tensor map then fails, so every tensor-map builder binds the operand's device first.
+static int bind_device_of(const void* p) {
+  cudaPointerAttributes a;
+  cudaError_t e = cudaPointerGetAttributes(&a, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();   // not a pointer the runtime knows: leave the thread's context alone
+    return 0;
+  }
+  if (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged) return 0;
+  e = cudaSetDevice(a.device);
+  return e == cudaSuccess ? 0 : (int)e;
+}
+
 // 2-D bf16 row-major [rows, cols] with row stride `ld` elements; box = box_rows x 64 columns, 128B swizzle.
 static int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
   int rc = get_encode();
+  if (rc) return rc;
+  rc = bind_device_of(base);
   if (rc) return rc;
   if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * 2) % 16) || cols % 8) return (int)cudaErrorInvalidValue;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};

@@ -100,8 +100,8 @@ class TrajectoryDiT(nn.Module):
 
     def forward(self, z_t, t, context):
         wdt = self.in_proj.weight.dtype
-        x = self.in_proj(z_t.to(wdt)) + self.pos
-        c = self.t_embed(t) + self.scene_proj(context.mean(dim=1))
+        x = linear(z_t.to(wdt), self.in_proj.weight, self.in_proj.bias) + self.pos
+        c = self.t_embed(t) + linear(context.mean(dim=1), self.scene_proj.weight, self.scene_proj.bias)
         if self.fused:
             pending = None
             for blk in self.blocks:
@@ -116,7 +116,7 @@ class TrajectoryDiT(nn.Module):
             for blk in self.blocks:
                 x = blk(x, c, context)
             h = self.norm_out(x)
-        return self.out(h)
+        return linear(h, self.out.weight, self.out.bias)
 
     def flow_loss(self, trajectory, context):
         """Rectified flow: z_t = (1 - s) noise + s traj with s = t / t_max; regress traj - noise."""

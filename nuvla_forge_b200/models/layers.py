@@ -8,9 +8,10 @@ Parameter names follow the reference so ``state_dict`` keys match
 Compute differs from the reference where it saves memory traffic, never in
 the function computed:
 
-* Residual adds are fused into the output-projection GEMM epilogue
-  (``addmm(x, o, W.T)``: cuBLAS reads the residual as its C operand), and the
-  following RMSNorm is one native kernel.
+* Every linear layer runs its forward, input-gradient and weight-gradient
+  GEMMs on the native CTA-pair tcgen05 kernel (``ops.linear``); residual adds
+  are fused into the output-projection GEMM epilogue, and the following
+  RMSNorm is one native kernel.
 * The SwiGLU gate and up projections are one GEMM over a packed [2F, D]
   weight whose backward is one input-gradient GEMM; ``state_dict`` still
   exposes ``w_gate.weight`` and ``w_up.weight`` (split on save, joined on load).
@@ -29,6 +30,7 @@ from torch import nn
 
 from ..ops import add_rmsnorm
 from ..ops import attention as attention_op
+from ..ops import linear as linear_op
 from ..ops import rmsnorm as rmsnorm_op
 from ..ops import swiglu_packed
 from ..ops.reference import swiglu_ref
@@ -47,26 +49,21 @@ def set_pending_consumer(fn) -> None:
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None) -> torch.Tensor:
-    """F.linear, except that a pending parameter consumer may compute it first."""
+    """x @ w.T (+ b) on the native GEMM, unless a pending parameter consumer computes it first."""
     fn = _pending_consumer
     if fn is not None:
         y = fn(x, w, b)
         if y is not None:
             return y
-    return F.linear(x, w, b)
+    return linear_op.linear(x, w, b)
 
 
 def _linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None,
             residual: torch.Tensor | None = None) -> torch.Tensor:
-    """y = x @ w.T (+ b) (+ residual), with the residual read by the GEMM itself."""
+    """y = x @ w.T (+ b) (+ residual), with the residual read by the GEMM epilogue."""
     if residual is None:
         return linear(x, w, b)
-    shape = residual.shape
-    x2 = x.reshape(-1, x.shape[-1])
-    r2 = residual.reshape(-1, shape[-1])
-    if b is not None:
-        r2 = r2 + b
-    return torch.addmm(r2, x2, w.t()).view(shape)
+    return linear_op.linear(x, w, b, residual=residual)
 
 
 class RMSNorm(nn.Module):
@@ -102,7 +99,9 @@ class TimestepEmbedder(nn.Module):
         freqs = torch.exp(k * (-math.log(10000.0) / half))
         ang = t.to(torch.float32)[:, None] * freqs[None, :]
         emb = torch.cat([torch.cos(ang), torch.sin(ang)], dim=-1)
-        return self.mlp(emb.to(self.mlp[0].weight.dtype))
+        l0, l2 = self.mlp[0], self.mlp[2]
+        h = F.silu(linear(emb.to(l0.weight.dtype), l0.weight, l0.bias))
+        return linear(h, l2.weight, l2.bias)
 
 
 class Attention(nn.Module):

@@ -41,7 +41,7 @@ from ..ops import chunked_cross_entropy, patchify_images
 from ..ops import attention as attention_op
 from ..ops.image import patch_kpad
 from .dit import TrajectoryDiT
-from .layers import RMSNorm, TransformerBlock, _linear, run_blocks
+from .layers import RMSNorm, TransformerBlock, _linear, linear, run_blocks
 
 
 @dataclass
@@ -174,7 +174,7 @@ class MultiViewEncoder(nn.Module):
             w = self.patch.weight.reshape(d, -1)
             if kpad != w.shape[1]:
                 w = F.pad(w, (0, kpad - w.shape[1]))
-            x = F.linear(rows, w, self.patch.bias)  # [B*NI, P, D]
+            x = linear(rows, w, self.patch.bias)  # [B*NI, P, D]
         else:  # normalised float [B, NI, 3, H, W]
             b, ni = images.shape[:2]
             x = self.patch(images.flatten(0, 1).to(wdt))
@@ -214,11 +214,11 @@ class SceneQueryPool(nn.Module):
         dh = d // h
         wq, wkv = self.in_proj_weight[:d], self.in_proj_weight[d:]
         bq, bkv = self.in_proj_bias[:d], self.in_proj_bias[d:]
-        qq = F.linear(q, wq, bq).view(b, s, h, dh)
-        kv = F.linear(x, wkv, bkv).view(b, L, 2 * h, dh)
+        qq = linear(q, wq, bq).view(b, s, h, dh)
+        kv = linear(x, wkv, bkv).view(b, L, 2 * h, dh)
         k, v = kv.split([h, h], dim=2)
         o = attention_op(qq, k, v, causal=False, force_reference=not self.fused).reshape(b, s, d)
-        return F.linear(o, self.out_proj.weight, self.out_proj.bias)
+        return linear(o, self.out_proj.weight, self.out_proj.bias)
 
 
 class NuVLA(nn.Module):
@@ -276,7 +276,7 @@ class NuVLA(nn.Module):
             k = cfg.pool
             x = x.view(b * ni, g // k, k, g // k, k, d).mean(dim=(2, 4))
         x = x.reshape(b, -1, d)
-        return F.linear(x, self.vision_proj.weight)  # [B, NI*Pp, Dt]
+        return linear(x, self.vision_proj.weight)  # [B, NI*Pp, Dt]
 
     def forward(self, images, trajectory=None, text_tokens=None, text_targets=None):
         """Joint objective: flow-matching plan loss + reasoning cross entropy (summed)."""

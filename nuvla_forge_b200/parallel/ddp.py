@@ -114,6 +114,9 @@ class DistributedDataParallel(nn.Module):
         self.comm_timer = None   # profiling.CommTimer: brackets the end-of-backward wait
         for s in self.space.segments:
             s.param.register_post_accumulate_grad_hook(self._hook)
+            # linear layers on the native GEMM write this parameter's gradient straight into
+            # main_grad (grad_target / grad_done below) instead of handing autograd a bf16 tensor
+            s.param._nfb_grad_owner = self
 
     # ------------------------------------------------------------------
     def _make_buckets(self, cap_mb: float) -> list[Bucket]:
@@ -150,11 +153,30 @@ class DistributedDataParallel(nn.Module):
         self._fresh = True
 
     def _hook(self, p: nn.Parameter) -> None:
+        self._queue_finalize()
+        _accumulate(p.main_grad.view(-1), p.grad.view(-1), self._fresh and id(p) not in self._seen)
+        p.grad = None
+        self._mark_ready(p)
+
+    def _queue_finalize(self) -> None:
         if not self._callback_queued:
             self._callback_queued = True
             torch.autograd.Variable._execution_engine.queue_callback(self._finalize_backward)
-        _accumulate(p.main_grad.view(-1), p.grad.view(-1), self._fresh)
-        p.grad = None
+
+    # gradient owner protocol of ops.linear: the GEMM writes the fp32 gradient itself
+    def grad_target(self, p: nn.Parameter):
+        """(fp32 gradient buffer of ``p``, overwrite?) for a kernel that produces p's whole gradient."""
+        self._queue_finalize()
+        return p.main_grad, self._fresh and id(p) not in self._seen
+
+    def grad_done(self, p: nn.Parameter) -> None:
+        """``p``'s gradient of this backward is complete in its buffer."""
+        self._mark_ready(p)
+
+    def _mark_ready(self, p: nn.Parameter) -> None:
+        if id(p) in self._seen:
+            raise RuntimeError(f"parameter {self.space.segment(p).name} received a second gradient in one "
+                               "backward; its bucket may already be reduced")
         self._seen.add(id(p))
         b = self.bucket_of[id(p)]
         b.pending -= 1

@@ -803,13 +803,19 @@ class _AgLinear(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, gy):
+        from ..ops import linear as linear_op
+
         x, w = ctx.saved_tensors
         gy2 = gy.reshape(-1, gy.shape[-1])
+        x2 = x.reshape(-1, x.shape[-1])
+        native = linear_op.supported(x2, w)
+        if native:
+            gy2, x2 = linear_op._aligned_rows(gy2), linear_op._aligned_rows(x2)
         gx = gw = None
         if ctx.needs_input_grad[0]:
-            gx = (gy2 @ w).view(x.shape)
+            gx = (linear_op.input_grad(gy2, w) if native else gy2 @ w).view(x.shape)
         if ctx.needs_input_grad[1]:
-            gw = gy2.t() @ x.reshape(-1, x.shape[-1])
+            gw = linear_op.weight_grad(gy2, x2, w) if native else gy2.t() @ x2
         return gx, gw, None, None
 
 

@@ -39,6 +39,7 @@ from .checkpoint import load_checkpoint, save_checkpoint
 from .data.adapters import SampleSpec, build_dataset
 from .data.loader import (CudaPrefetcher, LoaderConfig, SyntheticBatchSource, build_fast_loader,
                           build_naive_loader, describe_environment)
+from .health import HealthMonitor
 from .models.nuvla import NuVLA, NuVLAConfig
 from .optim.adamw import FlatAdamW
 from .parallel.ddp import DistributedDataParallel
@@ -58,7 +59,7 @@ class Trainer:
                  weight_decay: float = 0.01, max_grad_norm: float = 1.0, bucket_mb: float = 25.0,
                  comm: str = "auto", fsdp: bool = False, grad_accum: int = 1, no_sync_accum: bool = True,
                  bf16: bool = True, grad_checkpoint: bool = False, seed: int = 1234, compile: bool = False,
-                 fused_gather: bool | None = None):
+                 fused_gather: bool | None = None, heartbeat_s: float = 0.5, peer_timeout_s: float = 30.0):
         self.info = info or setup_distributed()
         self.cfg = cfg
         self.device = self.info.device
@@ -87,6 +88,11 @@ class Trainer:
             self.model.comm_timer = self.comm_timer
         self.copy_stream = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
         self.step_count = 0
+        hb = None
+        if self.info.world > 1 and heartbeat_s > 0:
+            from .parallel.watchdog import Heartbeat
+            hb = Heartbeat(interval=heartbeat_s).start()
+        self.health = HealthMonitor(self.device, self.model, self.info.world, heartbeat=hb, max_age=peer_timeout_s)
 
     # ------------------------------------------------------------------
     def to_device(self, batch: dict) -> dict:
@@ -102,7 +108,11 @@ class Trainer:
 
         Host batches are copied on a side stream while earlier micro-steps
         compute. Returns the mean loss as a device tensor (no host sync).
+        Before any launch, raises ``PeerLost`` if a peer stopped its heartbeat
+        and ``DeviceFault`` if a native kernel's bounded wait gave up during an
+        earlier step (read from an asynchronous copy of the status words).
         """
+        self.health.before_step()
         n = len(micro_batches)
         on_dev = [self.to_device(b) if not b["images"].is_cuda else b for b in micro_batches] \
             if self.device.type == "cuda" else [{k: b[k] for k in BATCH_KEYS if k in b} for b in micro_batches]
@@ -138,11 +148,17 @@ class Trainer:
         if timer is not None:
             timer.mark("optim")
         self.step_count += 1
+        self.health.after_step()
         return total / n
 
     def check_health(self) -> None:
+        """Synchronous check of every device status word and of the peers' heartbeats."""
+        self.health.check_now()
         if hasattr(self.model, "check_health"):
             self.model.check_health()
+
+    def close(self) -> None:
+        self.health.close()
 
     def num_parameters(self) -> int:
         return sum(p.numel() for p in self.module.parameters())
@@ -197,6 +213,12 @@ def build_args(argv=None):
     p.add_argument("--ckpt-dir", default="checkpoints")
     p.add_argument("--resume", default=None)
     p.add_argument("--seed", type=int, default=1234)
+    p.add_argument("--peer-timeout", type=float, default=30.0,
+                   help="seconds without a heartbeat after which a peer counts as lost")
+    p.add_argument("--inject-failure", action="append", default=[], metavar="RANK:STEP:MODE",
+                   help="host-side fault injection for resilience tests: at the start of STEP, rank RANK "
+                        "raises (raise), exits without cleanup (exit), stops its heartbeat and hangs (stall), "
+                        "or waits N seconds (delayN)")
     p.add_argument("--out", default="reports")
     p.add_argument("--tag", default=None)
     return p.parse_args(argv)
@@ -218,6 +240,33 @@ def apply_preset(args):
         args.no_sync_accum = True
         args.ddp_bucket_mb = 100.0
     return args
+
+
+def _injected(args, rank: int, step: int) -> str | None:
+    for spec in args.inject_failure:
+        r, s, mode = spec.split(":", 2)
+        if int(r) == rank and int(s) == step:
+            return mode
+    return None
+
+
+def _inject(mode: str, trainer: "Trainer", rank: int, step: int) -> None:
+    """Host-side failure injection between steps (no kernel or collective is in flight)."""
+    import time
+
+    if mode == "raise":
+        raise RuntimeError(f"injected failure on rank {rank} at step {step}")
+    if mode == "exit":
+        os._exit(3)
+    if mode == "stall":
+        if trainer.health.heartbeat is not None:
+            trainer.health.heartbeat.stop()
+        while True:
+            time.sleep(1.0)
+    if mode.startswith("delay"):
+        time.sleep(float(mode[len("delay"):] or 1.0))
+        return
+    raise ValueError(f"unknown injection mode {mode!r}")
 
 
 def make_batches(args, cfg: NuVLAConfig, spec: SampleSpec, info: DistInfo):
@@ -263,7 +312,8 @@ def main(argv=None):
     trainer = Trainer(cfg, info, lr=args.lr, max_grad_norm=args.max_grad_norm, bucket_mb=args.ddp_bucket_mb,
                       comm=args.comm, fsdp=args.fsdp, grad_accum=args.grad_accum,
                       no_sync_accum=args.no_sync_accum, bf16=args.bf16, grad_checkpoint=args.grad_checkpoint,
-                      seed=args.seed, compile=args.compile, fused_gather=False if args.no_fused_gather else None)
+                      seed=args.seed, compile=args.compile, fused_gather=False if args.no_fused_gather else None,
+                      peer_timeout_s=args.peer_timeout)
     start_step = 0
     if args.resume:
         start_step = load_checkpoint(args.resume, trainer.model, trainer.opt)
@@ -276,8 +326,27 @@ def main(argv=None):
               f"| comm={getattr(trainer.model, 'comm', 'fsdp')}")
         print(f"[{tag}] env={describe_environment()}")
     total = args.steps + args.warmup_steps
+    try:
+        _train_loop(args, trainer, batches, timer, prof, info, cfg, start_step, total)
+    except BaseException as exc:
+        if trainer.health.heartbeat is not None:      # peers learn of it before their next launch
+            trainer.health.heartbeat.mark_failed(f"{type(exc).__name__}: {exc}")
+        trainer.close()
+        raise
+    stats = _report(args, trainer, timer, info, cfg, tag)
+    trainer.check_health()
+    trainer.close()
+    if info.world > 1:
+        teardown_distributed()
+    return stats
+
+
+def _train_loop(args, trainer, batches, timer, prof, info, cfg, start_step, total):
     with prof as p:
         for step in range(start_step, start_step + total):
+            mode = _injected(args, info.rank, step)
+            if mode:
+                _inject(mode, trainer, info.rank, step)
             timer.start()
             micro = [next(batches) for _ in range(trainer.grad_accum)]
             loss = trainer.step(micro, timer)
@@ -286,12 +355,14 @@ def main(argv=None):
                 p.step()
             if step % 25 == 0:
                 lv = float(loss.item())
-                trainer.check_health()
                 if info.is_main:
                     print(f"  step {step:5d}  loss {lv:.4f}  {timer.last_ms():.1f} ms")
             if args.save_every and (step + 1) % args.save_every == 0:
                 save_checkpoint(Path(args.ckpt_dir) / f"step-{step + 1:07d}.pt", trainer.model, trainer.opt,
                                 step + 1, cfg.to_dict())
+
+
+def _report(args, trainer, timer, info, cfg, tag):
     stats = timer.summary()
     step_ms_max = max_over_ranks(stats["step_ms"], info.device)
     gb = args.batch_size * info.world * trainer.grad_accum
@@ -317,8 +388,6 @@ def main(argv=None):
         print(f"\n[{tag}] step {stats['step_ms']:.2f} ms | {stats['samples_per_sec']:.1f} samples/s | "
               f"peak {stats['peak_mem_mib']:.0f} MiB")
         print(f"[{tag}] wrote {path}")
-    if info.world > 1:
-        teardown_distributed()
     return stats
 
 
