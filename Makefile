@@ -1,4 +1,4 @@
-.PHONY: build test test-gpu bench bench-comms train-ab report probe clean
+.PHONY: build test test-gpu bench bench-all bench-comms train-ab report probe clean
 NGPU ?= 2
 
 build:
@@ -14,6 +14,9 @@ bench: build
 	python bench.py
 	python -m nuvla_forge_b200.bench.bench_kernels
 	python -m nuvla_forge_b200.bench.bench_dataloader
+
+bench-all: build
+	python -m nuvla_forge_b200.bench.run_all
 
 bench-comms: build
 	python -m torch.distributed.run --nproc-per-node $(NGPU) --master-addr 127.0.0.1 -m nuvla_forge_b200.bench.bench_comms
