@@ -96,7 +96,7 @@ class ClockSampler:
             self.proc.kill()
         if self.th:
             self.th.join(timeout=2)
-        sm, mx, reasons = [], [], set()
+        sm, mx, pw, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in self.rows:
             if len(r) < 9:
@@ -106,12 +106,17 @@ class ClockSampler:
                 mx.append(float(r[2]))
             except ValueError:
                 continue
+            try:
+                pw.append(float(r[3]))
+            except ValueError:
+                pass
             for name, v in zip(names, r[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(name)
         load = [s for s in sm if mx and s > 0.3 * max(mx)] or sm
         return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w": statistics.median(pw) if pw else None}
 
 
 def visible_gpu_ids() -> list[str]:

@@ -75,6 +75,8 @@ _SIGS: dict[str, tuple] = {
     "nfb_gemm_max_clusters": (I, []),
     "nfb_gemm_small": (I, [I, I, P, L, L, P, L, L, P, L, L, P, I, I, I, I, P]),
     "nfb_gemm_last_error": (ctypes.c_char_p, []),
+    "nfb_gemm_swiglu_fwd": (I, [P, P, P, P, I, I, I, L, L, L, L, P, P]),
+    "nfb_gemm_swiglu_bwd": (I, [P, P, P, P, I, I, I, L, L, L, L, P, P]),
 }
 
 _lib = None

@@ -51,12 +51,57 @@ def _time(fn, iters, flush):
     return statistics.median(ts)
 
 
+def sustained(seconds: float, out_path: str | None) -> None:
+    """Back-to-back GEMMs for ``seconds`` per implementation, with SM clock and power sampled:
+    under the 1 kW cap the sustained rate depends on energy per FLOP, not only on burst speed."""
+    import sys
+    sys.path.insert(0, str(Path(__file__).resolve().parents[2]))
+    from bench import ClockSampler, visible_gpu_ids
+
+    from ..ops import linear as L
+
+    rows = []
+    for name, M, N, K in (SHAPES[0], SHAPES[1]):
+        g = torch.Generator(device="cuda").manual_seed(0)
+        x = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
+        w = torch.randn(N, K, generator=g, device="cuda").to(torch.bfloat16)
+        y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        for impl, fn in (("native", lambda: L.gemm(x, w, out=y)), ("cublas", lambda: torch.mm(x, w.t(), out=y))):
+            for _ in range(5):
+                fn()
+            torch.cuda.synchronize()
+            one = _time(fn, 3, torch.empty(1, device="cuda"))
+            n = max(1, int(seconds * 1e3 / one))
+            smp = ClockSampler(visible_gpu_ids())
+            smp.start()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(n):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            clk = smp.stop()
+            ms = e0.elapsed_time(e1) / n
+            row = {"shape": name, "impl": impl, "iters": n, "ms": ms, "tflops": 2.0 * M * N * K / ms / 1e9,
+                   "clocks": clk}
+            rows.append(row)
+            print(f"sustained {name:14s} {impl:6s} {row['tflops']:7.1f} TF/s  sm {clk.get('sm_mhz')} MHz "
+                  f"power {clk.get('power_w')} W  {clk.get('reasons')}", flush=True)
+    if out_path:
+        Path(out_path).write_text(json.dumps({"sustained_s": seconds, "rows": rows}, indent=1))
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default="reports/gemm.json")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--quick", action="store_true", help="first three shapes only")
+    ap.add_argument("--sustained", type=float, default=0.0,
+                    help="instead: run each implementation back to back for this many seconds (clock/power)")
     args = ap.parse_args(argv)
+    if args.sustained > 0:
+        sustained(args.sustained, args.out)
+        return
     from ..ops import linear as L
 
     peaks = load_measured_peaks()

@@ -14,14 +14,23 @@ import argparse
 import torch
 
 
+NATIVE_GEMM = ("gemm_pair_kernel", "gemm_small_kernel", "tc_kernel", "ag_gemm")
+NATIVE_ATTN = ("attn_fwd", "attn_bwd", "attn_pre", "attn_dq")
+
+
 def category(name: str) -> str:
+    """Kernel class: native (this library's) or library GEMM / attention, other native, other."""
     n = name.lower()
+    if any(k in n for k in NATIVE_GEMM):
+        return "native gemm"
+    if any(k in n for k in NATIVE_ATTN):
+        return "native attention"
     if "nfb::" in n or n.startswith("nfb") or "adamw_kernel" in n:
-        return "native"
+        return "native other"
     if "sdpa" in n or "flash" in n or "fmha" in n or "attention" in n:
-        return "attention"
+        return "library attention"
     if "nvjet" in n or "gemm" in n or "cutlass" in n or "xmma" in n or "cublas" in n:
-        return "gemm"
+        return "library gemm"
     return "other"
 
 

@@ -32,9 +32,10 @@ namespace {
 template <class Epi, bool A_MN, bool B_MN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
-                     const __grid_constant__ CUtensorMap tc, Work w, Epi epi, uint32_t* status) {
+                     const __grid_constant__ CUtensorMap tc, const __grid_constant__ CUtensorMap td, Work w,
+                     Epi epi, uint32_t* status) {
   Epi e = epi;
-  gemm_pair_body<A_MN, B_MN>(&ta, &tb, &tc, w, e, status);
+  gemm_pair_body<A_MN, B_MN>(&ta, &tb, &tc, &td, w, e, status);
 }
 
 // Co-resident clusters of a kernel (cached per device and kernel).
@@ -138,10 +139,12 @@ static int output_map(CUtensorMap* m, const void* C, int M, int N, int64_t ldc) 
 
 template <class Epi, bool A_MN, bool B_MN>
 static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Work w, const Epi& epi, uint32_t* status,
-                  cudaStream_t st, const CUtensorMap* tc_map = nullptr) {
-  CUtensorMap ta, tb, tcm;
+                  cudaStream_t st, const CUtensorMap* tc_map = nullptr, const CUtensorMap* td_map = nullptr) {
+  CUtensorMap ta, tb, tcm, tdm;
   if (tc_map) tcm = *tc_map;
   else memset(&tcm, 0, sizeof(tcm));
+  if (td_map) tdm = *td_map;
+  else memset(&tdm, 0, sizeof(tdm));
   int rc = operand_map(&ta, A, w.M, w.K, lda, A_MN);
   if (rc) return gemm_fail(rc, "tensor map of A");
   rc = operand_map(&tb, B, w.N, w.K, ldb, B_MN);
@@ -153,7 +156,7 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Work w
   const int grid_clusters = w.items < clusters ? w.items : clusters;
   cudaError_t pending = cudaGetLastError();     // an error left by an earlier call of this thread
   if (pending != cudaSuccess) return gemm_fail((int)pending, "error pending before the launch");
-  kern<<<2 * grid_clusters, kThreads, kSmemBytes, st>>>(ta, tb, tcm, w, epi, status);
+  kern<<<2 * grid_clusters, kThreads, kSmemBytes, st>>>(ta, tb, tcm, tdm, w, epi, status);
   rc = (int)cudaGetLastError();
   return rc ? gemm_fail(rc, "kernel launch") : 0;
 }
@@ -221,6 +224,42 @@ NFB_API int nfb_gemm_acc(const void* A, const void* B, float* C, int M, int N, i
   epi.flags = flags;
   epi.epoch = epoch & 0xFFFFFFu;
   return dispatch(A, lda, B, ldb, w, epi, a_mn, b_mn, status, (cudaStream_t)stream);
+}
+
+// act [M, F] = silu(gate) * up with (gate | up) = X W^T, W [2F, K] interleaved in 128-row blocks
+// (gate rows of hidden units [128 b, 128 b + 128), then their up rows); the pre-activations go to
+// ab [M, 2F] in the same interleaved order. F must be a multiple of 128.
+NFB_API int nfb_gemm_swiglu_fwd(const void* X, const void* W, void* ab, void* act, int M, int F, int K, int64_t ldx,
+                                int64_t ldw, int64_t ldab, int64_t ldact, uint32_t* status, void* stream) {
+  if (M <= 0) return 0;
+  if (K <= 0 || F <= 0 || F % 128) return gemm_fail((int)cudaErrorInvalidValue, "swiglu: F must be a multiple of 128");
+  CUtensorMap tab, tact;
+  int rc = output_map(&tab, ab, M, 2 * F, ldab);
+  if (rc) return gemm_fail(rc, "tensor map of ab");
+  rc = output_map(&tact, act, M, F, ldact);
+  if (rc) return gemm_fail(rc, "tensor map of act");
+  SwiGluFwdEpi epi;
+  epi.chunk = 0;
+  return launch<SwiGluFwdEpi, false, false>(X, ldx, W, ldw, make_work(M, 2 * F, K), epi, status,
+                                            (cudaStream_t)stream, &tab, &tact);
+}
+
+// d_ab [M, 2F] (interleaved like ab) from dY [M, D] and the down projection W_down [D, F]:
+// d_act = dY W_down on the tensor cores, then the SwiGLU backward in the epilogue (reads ab).
+NFB_API int nfb_gemm_swiglu_bwd(const void* dY, const void* Wd, const void* ab, void* dab, int M, int F, int D,
+                                int64_t ldy, int64_t ldw, int64_t ldab, int64_t lddab, uint32_t* status, void* stream) {
+  if (M <= 0) return 0;
+  if (D <= 0 || F <= 0 || F % 128) return gemm_fail((int)cudaErrorInvalidValue, "swiglu: F must be a multiple of 128");
+  if (!al16(ab) || (ldab * 2) % 16) return gemm_fail((int)cudaErrorInvalidValue, "swiglu: ab rows not 16-byte aligned");
+  CUtensorMap tdab;
+  int rc = output_map(&tdab, dab, M, 2 * F, lddab);
+  if (rc) return gemm_fail(rc, "tensor map of d_ab");
+  SwiGluBwdEpi epi;
+  epi.ab = reinterpret_cast<const __nv_bfloat16*>(ab);
+  epi.ldab = ldab;
+  epi.chunk = 0;
+  return launch<SwiGluBwdEpi, false, true>(dY, ldy, Wd, ldw, make_work(M, F, D), epi, status, (cudaStream_t)stream,
+                                           &tdab);
 }
 
 // Split count nfb_gemm_acc picks for this shape when given splits = 0 (for callers sizing flags).

@@ -53,7 +53,7 @@ namespace g2 {
 using tc::mbar_arrive_expect_tx;
 using tc::mbar_init;
 using tc::mbar_try_wait;
-using tc::mbar_wait;
+using tc::mbar_wait_sleep;
 using tc::prefetch_tmap;
 using tc::smem_u32;
 using tc::sw128_desc;
@@ -201,6 +201,7 @@ struct EpiCtx {
   int lane;
   uint8_t* smem;            // this warp's two staging buffers (1024-byte aligned)
   const CUtensorMap* tmap_c; // output tensor map (bf16 [M, N], 32 x 32 boxes, 64-byte swizzle) or null
+  const CUtensorMap* tmap_d; // second output map of the same kind (epilogues with two outputs) or null
 };
 
 // Epi must provide: __device__ bool warp(const EpiCtx&, const Work&, volatile int* abort, uint32_t* status)
@@ -208,7 +209,7 @@ struct EpiCtx {
 // EpiCtx&) (every lane, after the warp's last tile: complete outstanding stores).
 template <bool A_MN, bool B_MN, class Epi>
 __device__ void gemm_pair_body(const CUtensorMap* tma_a, const CUtensorMap* tma_b, const CUtensorMap* tma_c,
-                               const Work& w, Epi& epi, uint32_t* status) {
+                               const CUtensorMap* tma_d, const Work& w, Epi& epi, uint32_t* status) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Shared* S = reinterpret_cast<Shared*>(smem + (size_t)kStages * kStageBytes);
@@ -258,7 +259,7 @@ __device__ void gemm_pair_body(const CUtensorMap* tma_a, const CUtensorMap* tma_
         const int arow = I.m_blk * TM + HALF * (int)rank;
         const int brow = I.n_blk * TN + HALF * (int)rank;
         for (int kb = I.kb0; kb < I.kb1; ++kb) {
-          if (!mbar_wait(&S->empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
+          if (!mbar_wait_sleep(&S->empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
           uint8_t* sa = smem + (size_t)stage * kStageBytes;
           uint8_t* sb = sa + kABytes;
           const uint32_t bar = map_to(smem_u32(&S->full[stage]), 0);
@@ -309,11 +310,11 @@ __device__ void gemm_pair_body(const CUtensorMap* tma_a, const CUtensorMap* tma_
       bool ok = true;
       for (int it = cluster; it < w.items && ok; it += n_clusters) {
         const Item I = item_at(w, it);
-        if (!mbar_wait(&S->tmem_empty[acc], acc_phase ^ 1u, abort_flag)) { ok = false; break; }
+        if (!mbar_wait_sleep(&S->tmem_empty[acc], acc_phase ^ 1u, abort_flag)) { ok = false; break; }
         tmem_fence_after();
         const uint32_t tmem_d = tmem_base + (uint32_t)(acc * TN);
         for (int kb = I.kb0; kb < I.kb1; ++kb) {
-          if (!mbar_wait(&S->full[stage], phase, abort_flag)) { ok = false; break; }
+          if (!mbar_wait_sleep(&S->full[stage], phase, abort_flag)) { ok = false; break; }
           tmem_fence_after();
           const uint32_t sa = smem_u32(smem + (size_t)stage * kStageBytes);
           const uint32_t sb = sa + kABytes;
@@ -351,8 +352,9 @@ __device__ void gemm_pair_body(const CUtensorMap* tma_a, const CUtensorMap* tma_
     c.lane = lane;
     c.smem = reinterpret_cast<uint8_t*>(S) + kSharedSlot + (size_t)quarter * 2 * kEpiBufBytes;
     c.tmap_c = tma_c;
+    c.tmap_d = tma_d;
     for (int it = cluster; it < w.items; it += n_clusters) {
-      bool ok = mbar_wait(&S->tmem_full[acc], acc_phase, abort_flag);
+      bool ok = mbar_wait_sleep(&S->tmem_full[acc], acc_phase, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) {
         if (lane == 0) {
@@ -394,6 +396,38 @@ __device__ void gemm_pair_body(const CUtensorMap* tma_a, const CUtensorMap* tma_
 // ---------------------------------------------------------------------------
 // Epilogues
 // ---------------------------------------------------------------------------
+
+// Stage 32 fp32 values of row `r` (this lane) of a 32 x 32 bf16 box into the warp's next staging
+// buffer and store the box at (x, y) of `map` with one TMA store. `chunk` counts the warp's
+// staged boxes (the buffer alternates); every lane calls it.
+__device__ __forceinline__ void stage_store(const EpiCtx& c, uint32_t& chunk, const float* v,
+                                            const CUtensorMap* map, int x, int y) {
+  uint8_t* buf = c.smem + (chunk & 1u) * kEpiBufBytes;
+  if (chunk >= 2) {
+    if (c.lane == 0) bulk_wait_read1();           // the store that last used this buffer has read it
+    __syncwarp();
+  }
+  const int r = c.lane;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    Vec16<__nv_bfloat16> q;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) q.v[e] = __float2bfloat16_rn(v[8 * j + e]);
+    const int pj = j ^ ((r >> 1) & 3);             // 64-byte swizzle
+    *reinterpret_cast<uint4*>(buf + r * 64 + pj * 16) = q.u;
+  }
+  fence_async_smem();
+  __syncwarp();
+  if (c.lane == 0) {
+    tma_store_2d(map, buf, x, y);
+    bulk_commit();
+  }
+  ++chunk;
+}
+
+__device__ __forceinline__ void round_bf16(float* v, int n) {
+  for (int i = 0; i < n; ++i) v[i] = __bfloat162float(__float2bfloat16_rn(v[i]));
+}
 
 // Y = acc (+ bias[n]) (+ R[m, n]) stored as bf16 (or fp32 with out_f32).
 // bf16 output with a tensor map: each 32-column chunk of the warp's 32 rows is converted, written
@@ -455,27 +489,7 @@ struct LinearEpi {
         const int n = c.n0 + cc;
         if (c.row0 >= w.M || n >= w.N) continue;        // whole chunk outside C (warp-uniform)
         if (live) add_bias_res(v, m, n, w.N, vec_ok && n + 32 <= w.N);
-        uint8_t* buf = c.smem + (chunk & 1u) * kEpiBufBytes;
-        if (chunk >= 2) {
-          if (c.lane == 0) bulk_wait_read1();           // the store that last used this buffer read it
-          __syncwarp();
-        }
-        const int r = c.lane;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          Vec16<__nv_bfloat16> q;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) q.v[e] = __float2bfloat16_rn(v[8 * j + e]);
-          const int pj = j ^ ((r >> 1) & 3);
-          *reinterpret_cast<uint4*>(buf + r * 64 + pj * 16) = q.u;
-        }
-        fence_async_smem();
-        __syncwarp();
-        if (c.lane == 0) {
-          tma_store_2d(c.tmap_c, buf, n, c.row0);
-          bulk_commit();
-        }
-        ++chunk;
+        stage_store(c, chunk, v, c.tmap_c, n, c.row0);
       }
       return true;
     }
@@ -538,6 +552,7 @@ struct AccumF32Epi {
         const uint64_t t0 = globaltimer_ns();
         uint32_t spins = 0;
         while (ld_acquire_gpu(flag) != want) {
+          __nanosleep(128);
           if ((++spins & 63u) == 0 && (*abort_flag || globaltimer_ns() - t0 > kWaitNs)) { ok = false; break; }
         }
         if (!ok) set_status(status, kTimeoutFlag, 210);
@@ -581,6 +596,102 @@ struct AccumF32Epi {
   }
 
   __device__ void finish(const EpiCtx&) {}
+};
+
+// SwiGLU fused into the gate/up projection. The weight's rows are interleaved in 128-row blocks
+// (block b of the output = 128 gate columns of hidden units [128 b, 128 b + 128), then the 128
+// up columns of the same units), so each 256-column tile holds matching gate and up columns.
+// The epilogue stores the pre-activations (the tile itself, bf16, needed by the backward) with
+// the first map and act = silu(gate) * up for the tile's 128 hidden units with the second.
+// Gate and up are rounded to bf16 before act is formed, as when act is computed from stored ab.
+struct SwiGluFwdEpi {
+  uint32_t chunk;
+
+  __device__ bool warp(const EpiCtx& c, const Work& w, volatile int*, uint32_t*) {
+    if (c.row0 >= w.M) {
+      // every TMEM load is warp-collective: still read the accumulator, store nothing
+#pragma unroll 1
+      for (int cc = 0; cc < TN; cc += 32) { float v[32]; tmem_ld32(c.taddr + cc, v); }
+      return true;
+    }
+    const int h0 = c.n0 / 2;                       // first hidden unit of this tile
+#pragma unroll 1
+    for (int cc = 0; cc < TN / 2; cc += 32) {
+      if (c.n0 + cc >= w.N) {
+        float v[32];
+        tmem_ld32(c.taddr + cc, v);
+        tmem_ld32(c.taddr + 128 + cc, v);
+        continue;
+      }
+      float g[32], u[32];
+      tmem_ld32(c.taddr + cc, g);
+      tmem_ld32(c.taddr + 128 + cc, u);
+      stage_store(c, chunk, g, c.tmap_c, c.n0 + cc, c.row0);
+      stage_store(c, chunk, u, c.tmap_c, c.n0 + 128 + cc, c.row0);
+      round_bf16(g, 32);
+      round_bf16(u, 32);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) g[j] = g[j] * sigmoidf_fast(g[j]) * u[j];
+      stage_store(c, chunk, g, c.tmap_d, h0 + cc, c.row0);
+    }
+    return true;
+  }
+
+  __device__ void finish(const EpiCtx& c) {
+    if (c.lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+};
+
+// SwiGLU backward fused into the down projection's input gradient: the accumulator tile is
+// d_act[m, j] for 256 hidden units j; the epilogue reads the stored pre-activations (gate, up)
+// of those units from the interleaved ab [M, 2F] and stores
+//   d_gate = d_act * up * s * (1 + gate (1 - s)),  d_up = d_act * gate * s,  s = sigmoid(gate)
+// into d_ab (same interleaved layout) through the output map, so d_act never reaches memory.
+struct SwiGluBwdEpi {
+  const __nv_bfloat16* ab;
+  int64_t ldab;
+  uint32_t chunk;
+
+  __device__ bool warp(const EpiCtx& c, const Work& w, volatile int*, uint32_t*) {
+    const int m = c.row0 + c.lane;
+    const bool live = m < w.M;
+#pragma unroll 1
+    for (int cc = 0; cc < TN; cc += 32) {
+      float d[32];
+      tmem_ld32(c.taddr + cc, d);
+      const int j = c.n0 + cc;
+      if (c.row0 >= w.M || j >= w.N) continue;
+      const int gcol = 256 * (j >> 7) + (j & 127);
+      float g[32], u[32];
+      if (live) {
+        const __nv_bfloat16* gr = ab + (int64_t)m * ldab + gcol;
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+          load16<__nv_bfloat16>(gr + e, g + e);
+          load16<__nv_bfloat16>(gr + 128 + e, u + e);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) { g[e] = 0.f; u[e] = 0.f; }
+      }
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const float sg = sigmoidf_fast(g[e]);
+        const float du = d[e] * g[e] * sg;
+        d[e] = d[e] * u[e] * sg * (1.f + g[e] * (1.f - sg));
+        u[e] = du;
+      }
+      stage_store(c, chunk, d, c.tmap_c, gcol, c.row0);
+      stage_store(c, chunk, u, c.tmap_c, gcol + 128, c.row0);
+    }
+    return true;
+  }
+
+  __device__ void finish(const EpiCtx& c) {
+    if (c.lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
 };
 
 }  // namespace g2

@@ -124,6 +124,16 @@ NFB_EXPORT int nfb_gemm_acc(const void* A, const void* B, float* C, int M, int N
                             int64_t ldc, int a_mn, int b_mn, int accumulate, int splits, uint32_t* flags,
                             int64_t flag_words, uint32_t epoch, uint32_t* status, void* stream);
 NFB_EXPORT int nfb_gemm_acc_splits(int M, int N, int K);
+/* SwiGLU fused into the gate/up projection: W [2F, K] with gate and up rows interleaved in 128-row
+ * blocks; writes the pre-activations ab [M, 2F] (same interleaving) and act = silu(gate) * up [M, F]. */
+NFB_EXPORT int nfb_gemm_swiglu_fwd(const void* X, const void* W, void* ab, void* act, int M, int F, int K,
+                                   int64_t ldx, int64_t ldw, int64_t ldab, int64_t ldact, uint32_t* status,
+                                   void* stream);
+/* SwiGLU backward fused into the down projection's input gradient: d_ab [M, 2F] (interleaved) from
+ * dY [M, D], W_down [D, F] and the forward's ab. */
+NFB_EXPORT int nfb_gemm_swiglu_bwd(const void* dY, const void* Wd, const void* ab, void* dab, int M, int F, int D,
+                                   int64_t ldy, int64_t ldw, int64_t ldab, int64_t lddab, uint32_t* status,
+                                   void* stream);
 /* Why the last failing nfb_gemm / nfb_gemm_acc call of this host thread failed ("" if none). */
 NFB_EXPORT const char* nfb_gemm_last_error(void);
 /* CUDA-core GEMM for widths the tensor-core kernel cannot tile: C[m, n] (+)= sum_k A[m, k] B[n, k]

@@ -103,6 +103,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete sleeps in the barrier
+// unit until the phase completes or `ns` elapse, instead of re-polling (less issue activity and
+// power while a role idles, e.g. the epilogue during a main loop).
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait with the suspend hint (same contract as mbar_wait below).
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                uint32_t hint_ns = 20000u) {
+  if (mbar_try_wait_sleep(bar, parity, hint_ns)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait_sleep(bar, parity, hint_ns)) return true;
+    if ((++spins & 15u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitNs) return false;
+    }
+  }
+}
+
 // Bounded wait for the phase with the given parity. Returns false on timeout
 // or when another role has raised the abort flag.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {

@@ -32,7 +32,7 @@ from ..ops import add_rmsnorm
 from ..ops import attention as attention_op
 from ..ops import linear as linear_op
 from ..ops import rmsnorm as rmsnorm_op
-from ..ops import swiglu_packed
+from ..ops import fused_swiglu, swiglu_packed
 from ..ops.reference import swiglu_ref
 
 
@@ -152,37 +152,57 @@ class Attention(nn.Module):
 
 
 class SwiGLUMLP(nn.Module):
-    """w_down(silu(w_gate x) * w_up x) with the gate/up weights packed in one tensor."""
+    """w_down(silu(w_gate x) * w_up x) with the gate/up weights packed in one tensor.
+
+    When the hidden width is a multiple of 128 the packed weight stores gate and up rows
+    interleaved in 128-row blocks, the layout of the native fused MLP (gate/up GEMM with the
+    SwiGLU in its epilogue, down-projection input gradient with the SwiGLU backward in its
+    epilogue); otherwise it is [gate; up]. ``state_dict`` always exposes the reference's
+    ``w_gate.weight`` / ``w_up.weight`` (split on save, joined on load).
+    """
 
     def __init__(self, dim: int, hidden: int, fused: bool = True):
         super().__init__()
         self.hidden = hidden
         self.fused = fused
+        self.interleaved = hidden % 128 == 0
         self.w_gate_up = nn.Parameter(torch.empty(2 * hidden, dim))
         self.w_down = nn.Linear(hidden, dim, bias=False)
         bound = 1.0 / math.sqrt(dim)
         nn.init.uniform_(self.w_gate_up, -bound, bound)
         self._register_state_dict_hook(SwiGLUMLP._split_on_save)
-        self._register_load_state_dict_pre_hook(SwiGLUMLP._join_on_load)
+        self._register_load_state_dict_pre_hook(self._join_on_load)
 
     @staticmethod
     def _split_on_save(module, state_dict, prefix, local_metadata):
         key = prefix + "w_gate_up"
         if key in state_dict:
             w = state_dict.pop(key)
-            state_dict[prefix + "w_gate.weight"] = w[: module.hidden]
-            state_dict[prefix + "w_up.weight"] = w[module.hidden:]
+            if module.interleaved:
+                g, u = linear_op.split_gate_up_rows(w)
+            else:
+                g, u = w[: module.hidden], w[module.hidden:]
+            state_dict[prefix + "w_gate.weight"] = g
+            state_dict[prefix + "w_up.weight"] = u
         return state_dict
 
-    @staticmethod
-    def _join_on_load(state_dict, prefix, *args, **kwargs):
+    def _join_on_load(self, state_dict, prefix, *args, **kwargs):
         g, u = prefix + "w_gate.weight", prefix + "w_up.weight"
         if g in state_dict and u in state_dict:
-            state_dict[prefix + "w_gate_up"] = torch.cat([state_dict.pop(g), state_dict.pop(u)], dim=0)
+            gw, uw = state_dict.pop(g), state_dict.pop(u)
+            state_dict[prefix + "w_gate_up"] = (linear_op.interleave_gate_up(gw, uw) if self.interleaved
+                                                else torch.cat([gw, uw], dim=0))
 
     def forward(self, x, residual=None):
-        ab = linear(x, self.w_gate_up)
-        if self.fused:
+        w = self.w_gate_up
+        if self.fused and self.interleaved and _pending_consumer is None and \
+                linear_op.swiglu_supported(x, w, self.w_down.weight):
+            return linear_op.swiglu_mlp(x, w, self.w_down.weight, residual)
+        ab = linear(x, w)
+        if self.interleaved:
+            a, b = linear_op.split_gate_up_cols(ab)
+            act = fused_swiglu(a, b) if self.fused else swiglu_ref(a, b)
+        elif self.fused:
             act = swiglu_packed(ab)
         else:
             act = swiglu_ref(ab[..., : self.hidden], ab[..., self.hidden:])

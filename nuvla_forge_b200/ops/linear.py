@@ -192,6 +192,92 @@ class _LinearFn(torch.autograd.Function):
         return dx, dw, db, dr
 
 
+# ----------------------------------------------------------------------------- SwiGLU MLP
+def interleave_gate_up(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    """[gate; up] rows -> 128-row blocks (gate block b, up block b, ...), the fused kernel's layout."""
+    F, D = g.shape
+    return torch.stack([g.reshape(F // 128, 128, D), u.reshape(F // 128, 128, D)], dim=1).reshape(2 * F, D)
+
+
+def split_gate_up_rows(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Inverse of :func:`interleave_gate_up`: (gate rows, up rows) of an interleaved weight."""
+    F2, D = w.shape
+    v = w.reshape(F2 // 256, 2, 128, D)
+    return v[:, 0].reshape(F2 // 2, D), v[:, 1].reshape(F2 // 2, D)
+
+
+def split_gate_up_cols(ab: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(gate, up) columns of a pre-activation computed with an interleaved weight (copies)."""
+    F2 = ab.shape[-1]
+    v = ab.reshape(*ab.shape[:-1], F2 // 256, 2, 128)
+    return v[..., 0, :].reshape(*ab.shape[:-1], F2 // 2), v[..., 1, :].reshape(*ab.shape[:-1], F2 // 2)
+
+
+def swiglu_supported(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor) -> bool:
+    return (supported(x, w_gu) and supported(x, w_down) and w_gu.shape[0] % 256 == 0 and x.numel() > 0
+            and w_down.shape[1] * 2 == w_gu.shape[0] and w_gu.is_contiguous() and w_down.is_contiguous())
+
+
+class _SwiGluMLPFn(torch.autograd.Function):
+    """y = W_down (silu(gate) * up) (+ residual), gate/up = x W_gu^T, W_gu interleaved in 128-row blocks.
+
+    Forward: one GEMM whose epilogue writes the pre-activations and the activation, then the down
+    projection (residual in its epilogue). Backward: the down projection's input gradient with the
+    SwiGLU backward in its epilogue (d_act never stored), then the weight gradients and the input
+    gradient of the gate/up projection.
+    """
+
+    @staticmethod
+    def forward(ctx, x, w_gu, w_down, residual):
+        K = x.shape[-1]
+        F2 = w_gu.shape[0]
+        F = F2 // 2
+        D = w_down.shape[0]
+        x2 = _aligned_rows(x.reshape(-1, K))
+        M = x2.shape[0]
+        ab = torch.empty((M, F2), dtype=x.dtype, device=x.device)
+        act = torch.empty((M, F), dtype=x.dtype, device=x.device)
+        st = status_word(x.device)
+        nat.call("nfb_gemm_swiglu_fwd", nat.ptr(x2), nat.ptr(w_gu), nat.ptr(ab), nat.ptr(act), M, F, K, x2.stride(0),
+                 w_gu.stride(0), ab.stride(0), act.stride(0), nat.ptr(st), nat.stream(x.device))
+        r2 = _aligned_rows(residual.reshape(-1, D)) if residual is not None else None
+        y = gemm(act, w_down, residual=r2)
+        ctx.save_for_backward(x2, w_gu, w_down, ab, act)
+        ctx.w_refs = (w_gu, w_down)
+        ctx.x_shape = x.shape
+        ctx.has_res = residual is not None
+        return y.view(*x.shape[:-1], D)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w_gu, w_down, ab, act = ctx.saved_tensors
+        w_gu_ref, w_down_ref = ctx.w_refs
+        M, F2 = ab.shape
+        F = F2 // 2
+        D = w_down.shape[0]
+        dy2 = _aligned_rows(dy.reshape(-1, D))
+        dab = torch.empty_like(ab)
+        nat.call("nfb_gemm_swiglu_bwd", nat.ptr(dy2), nat.ptr(w_down), nat.ptr(ab), nat.ptr(dab), M, F, D,
+                 dy2.stride(0), w_down.stride(0), ab.stride(0), dab.stride(0), nat.ptr(status_word(dy.device)),
+                 nat.stream(dy.device))
+        dx = dw_gu = dw_down = dr = None
+        if ctx.needs_input_grad[2]:
+            dw_down = weight_grad(dy2, act, w_down_ref)
+        if ctx.needs_input_grad[0]:
+            dx = input_grad(dab, w_gu).view(ctx.x_shape)
+        if ctx.needs_input_grad[1]:
+            dw_gu = weight_grad(dab, x2, w_gu_ref)
+        if ctx.has_res and ctx.needs_input_grad[3]:
+            dr = dy
+        return dx, dw_gu, dw_down, dr
+
+
+def swiglu_mlp(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor,
+               residual: torch.Tensor | None = None) -> torch.Tensor:
+    """SwiGLU MLP with the activation fused into the GEMM epilogues (see :class:`_SwiGluMLPFn`)."""
+    return _SwiGluMLPFn.apply(x, w_gu, w_down, residual)
+
+
 def gemm_small(a: torch.Tensor, sa: tuple, b: torch.Tensor, sb: tuple, c: torch.Tensor, sc: tuple,
                M: int, N: int, K: int, bias: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
     """C[m, n] (+)= sum_k A[m, k] B[n, k] (+ bias) on CUDA cores; s* = (row, column) element strides."""

@@ -153,6 +153,10 @@ class DistributedDataParallel(nn.Module):
         self._fresh = True
 
     def _hook(self, p: nn.Parameter) -> None:
+        if p.grad is None:
+            # autograd still runs this hook when the layer handed its gradient to grad_target /
+            # grad_done (it returned None for the weight): nothing left to accumulate
+            return
         self._queue_finalize()
         _accumulate(p.main_grad.view(-1), p.grad.view(-1), self._fresh and id(p) not in self._seen)
         p.grad = None

@@ -502,6 +502,8 @@ class FullyShardedDataParallel(nn.Module):
                 self._prefetch(self._order[i - 1])
 
     def _grad_hook(self, p: nn.Parameter) -> None:
+        if p.grad is None:
+            return
         if not self._callback_queued:
             self._callback_queued = True
             self._rs_order = list(reversed(self._order)) + [self.root]

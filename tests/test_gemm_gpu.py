@@ -199,3 +199,54 @@ def test_small_linear_autograd(K, N):
     assert rel_err(x.grad, xf.grad) < 5e-3
     assert rel_err(w.grad, wf.grad) < 5e-3
     assert rel_err(b.grad, bf.grad) < 5e-3
+
+
+@pytest.mark.parametrize("M,D,F", [(300, 256, 384), (1024, 512, 1024), (4096, 1024, 4096), (130, 2048, 5632)])
+@pytest.mark.parametrize("residual", [False, True])
+def test_fused_swiglu_mlp_matches_fp32(M, D, F, residual):
+    """Gate/up GEMM with SwiGLU in its epilogue, down projection, and the fused backward, against fp32."""
+    from nuvla_forge_b200.ops import linear as L
+
+    g = torch.Generator(device=DEV).manual_seed(M + D + F)
+    x = (_rand(g, M, D)).requires_grad_(True)
+    wg, wu = _rand(g, F, D) * 0.05, _rand(g, F, D) * 0.05
+    wd = (_rand(g, D, F) * 0.05).requires_grad_(True)
+    w_gu = L.interleave_gate_up(wg, wu).contiguous().requires_grad_(True)
+    r = _rand(g, M, D).requires_grad_(True) if residual else None
+    y = L.swiglu_mlp(x, w_gu, wd, r)
+    dy = _rand(g, M, D)
+    y.backward(dy)
+    torch.cuda.synchronize()
+    L.check_status()
+    xf = x.detach().float().requires_grad_(True)
+    wgf, wuf = wg.float().requires_grad_(True), wu.float().requires_grad_(True)
+    wdf = wd.detach().float().requires_grad_(True)
+    a, b = xf @ wgf.t(), xf @ wuf.t()
+    yf = (torch.nn.functional.silu(a) * b) @ wdf.t()
+    if residual:
+        rf = r.detach().float().requires_grad_(True)
+        yf = yf + rf
+    yf.backward(dy.float())
+    assert rel_err(y, yf) < 1e-2
+    assert rel_err(x.grad, xf.grad) < 1e-2
+    assert rel_err(wd.grad, wdf.grad) < 1e-2
+    gg, gu = L.split_gate_up_rows(w_gu.grad)
+    assert rel_err(gg, wgf.grad) < 1e-2 and rel_err(gu, wuf.grad) < 1e-2
+    if residual:
+        assert rel_err(r.grad, rf.grad) < 1e-6
+
+
+def test_swiglu_mlp_module_state_dict_keeps_reference_layout():
+    """The interleaved weight is split back into w_gate / w_up on save and re-interleaved on load."""
+    from nuvla_forge_b200.models.layers import SwiGLUMLP
+
+    m = SwiGLUMLP(256, 512).cuda().to(torch.bfloat16)
+    sd = m.state_dict()
+    assert set(sd) == {"w_gate.weight", "w_up.weight", "w_down.weight"}
+    m2 = SwiGLUMLP(256, 512).cuda().to(torch.bfloat16)
+    m2.load_state_dict(sd)
+    assert torch.equal(m2.w_gate_up, m.w_gate_up)
+    x = _rand(torch.Generator(device=DEV).manual_seed(1), 64, 256)
+    ref = (torch.nn.functional.silu(x.float() @ sd["w_gate.weight"].float().t())
+           * (x.float() @ sd["w_up.weight"].float().t())) @ sd["w_down.weight"].float().t()
+    assert rel_err(m(x), ref) < 1e-2
