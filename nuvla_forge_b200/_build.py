@@ -8,6 +8,11 @@ library can be loaded by any process (Python through ctypes, or C/C++).
 
     python -m nuvla_forge_b200._build            # incremental
     python -m nuvla_forge_b200._build --clean    # full rebuild
+    python -m nuvla_forge_b200._build --debug    # libnfb200_debug.so: device bounds checks (-DNFB_DEBUG)
+
+The debug library reports a failed device-side check (an out-of-range label, a
+bad stride, ...) in a status word read by ``nfb_debug_status()`` instead of
+faulting; ``NFB_DEBUG=1`` makes ``nuvla_forge_b200._native`` load it.
 """
 
 from __future__ import annotations
@@ -25,6 +30,7 @@ CSRC = PKG / "csrc"
 LIBDIR = PKG / "_lib"
 OBJDIR = LIBDIR / "obj"
 LIBNAME = "libnfb200.so"
+DEBUG_LIBNAME = "libnfb200_debug.so"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
@@ -41,8 +47,8 @@ def nvcc_path() -> str:
     raise RuntimeError("nvcc not found; set NVCC or put CUDA's bin/ on PATH")
 
 
-def lib_path() -> Path:
-    return LIBDIR / LIBNAME
+def lib_path(debug: bool = False) -> Path:
+    return LIBDIR / (DEBUG_LIBNAME if debug else LIBNAME)
 
 
 def _sources() -> list[Path]:
@@ -54,36 +60,43 @@ def _headers_mtime() -> float:
     return max((h.stat().st_mtime for h in hs), default=0.0)
 
 
-def _compile(src: Path, nvcc: str, extra: list[str]) -> tuple[Path, str]:
-    obj = OBJDIR / (src.stem + ".o")
+def _compile(src: Path, nvcc: str, extra: list[str], objdir: Path = OBJDIR) -> tuple[Path, str]:
+    obj = objdir / (src.stem + ".o")
     if obj.exists() and obj.stat().st_mtime >= max(src.stat().st_mtime, _headers_mtime()):
         return obj, ""
     cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, *extra, "-I", str(CSRC), "-c", str(src), "-o", str(obj)]
     if src.suffix == ".cpp":
         cmd = [nvcc, "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
-               "-Xcompiler", "-pthread", "-I", str(CSRC), "-c", str(src), "-o", str(obj)]
+               "-Xcompiler", "-pthread", *extra, "-I", str(CSRC), "-c", str(src), "-o", str(obj)]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"nvcc failed for {src.name}:\n{' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
     return obj, r.stderr
 
 
-def build(clean: bool = False, verbose: bool = False, extra: list[str] | None = None) -> Path:
-    """Compile every source for sm_100a and link the shared library. Returns its path."""
+def build(clean: bool = False, verbose: bool = False, extra: list[str] | None = None, debug: bool = False) -> Path:
+    """Compile every source for sm_100a and link the shared library. Returns its path.
+
+    ``debug`` builds ``libnfb200_debug.so`` (-DNFB_DEBUG, separate objects) instead.
+    """
     extra = list(extra or [])
-    if clean and OBJDIR.exists():
-        shutil.rmtree(OBJDIR)
-    OBJDIR.mkdir(parents=True, exist_ok=True)
+    objdir = OBJDIR
+    if debug:
+        extra.append("-DNFB_DEBUG")
+        objdir = LIBDIR / "obj_debug"
+    if clean and objdir.exists():
+        shutil.rmtree(objdir)
+    objdir.mkdir(parents=True, exist_ok=True)
     nvcc = nvcc_path()
     srcs = _sources()
     with ThreadPoolExecutor(max_workers=max(1, min(len(srcs), os.cpu_count() or 4))) as ex:
-        results = list(ex.map(lambda s: _compile(s, nvcc, extra), srcs))
+        results = list(ex.map(lambda s: _compile(s, nvcc, extra, objdir), srcs))
     objs = [o for o, _ in results]
     if verbose:
         for o, log in results:
             if log.strip():
                 print(f"--- {o.name}\n{log}")
-    out = lib_path()
+    out = lib_path(debug)
     newest = max(o.stat().st_mtime for o in objs)
     if clean or not out.exists() or out.stat().st_mtime < newest:
         tmp = out.with_suffix(".so.tmp")
@@ -99,8 +112,9 @@ def main(argv: list[str] | None = None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--clean", action="store_true")
     ap.add_argument("-v", "--verbose", action="store_true")
+    ap.add_argument("--debug", action="store_true", help="build libnfb200_debug.so (device bounds checks)")
     args = ap.parse_args(argv)
-    path = build(clean=args.clean, verbose=args.verbose)
+    path = build(clean=args.clean, verbose=args.verbose, debug=args.debug)
     print(path)
     return 0
 

@@ -9,6 +9,8 @@ device pointers, sizes, strides and a ``cudaStream_t`` and returns a
 visible and the library loaded. On a machine with a GPU a missing or broken
 library is an error, not a silent fallback, unless ``NFB_ALLOW_REFERENCE=1``
 is set; ``NUVLA_FORGE_DISABLE_NATIVE=1`` forces the pure-PyTorch reference.
+``NFB_DEBUG=1`` loads the debug build (device bounds checks that report through
+:func:`debug_status` instead of faulting).
 """
 
 from __future__ import annotations
@@ -75,6 +77,9 @@ _SIGS: dict[str, tuple] = {
     "nfb_gemm_max_clusters": (I, []),
     "nfb_gemm_small": (I, [I, I, P, L, L, P, L, L, P, L, L, P, I, I, I, I, P]),
     "nfb_gemm_last_error": (ctypes.c_char_p, []),
+    "nfb_debug_status": (U32, []),
+    "nfb_debug_reset": (None, []),
+    "nfb_is_debug_build": (I, []),
     "nfb_gemm_swiglu_fwd": (I, [P, P, P, P, I, I, I, L, L, L, L, P, P]),
     "nfb_gemm_swiglu_bwd": (I, [P, P, P, P, I, I, I, L, L, L, L, P, P]),
 }
@@ -87,14 +92,17 @@ def _want_native() -> bool:
     return os.environ.get("NUVLA_FORGE_DISABLE_NATIVE", "0") != "1"
 
 
+DEBUG = os.environ.get("NFB_DEBUG", "0") == "1"
+
+
 def _load():
     global _lib, _load_error
     if _lib is not None or _load_error is not None:
         return _lib
-    path = lib_path()
+    path = lib_path(DEBUG)
     try:
         if not path.exists() and os.environ.get("NFB_NO_AUTOBUILD", "0") != "1":
-            build()
+            build(debug=DEBUG)
         lib = ctypes.CDLL(str(path))
         for name, (res, args) in _SIGS.items():
             fn = getattr(lib, name, None)
@@ -195,4 +203,13 @@ def num_sms() -> int:
 
 
 def loaded_library_path() -> str | None:
-    return str(lib_path()) if _lib is not None else None
+    return str(lib_path(DEBUG)) if _lib is not None else None
+
+
+def debug_status() -> int:
+    """First failed device check of the debug build ((4 << 24) | site), 0 if none (always 0 in release)."""
+    return int(lib().nfb_debug_status())
+
+
+def debug_reset() -> None:
+    lib().nfb_debug_reset()

@@ -9,6 +9,8 @@
 // processed with 16-byte vectors, and the chunk may be bf16 or fp32.
 #include "common.cuh"
 
+NFB_DEBUG_TU(ce_rows)
+
 namespace nfb {
 
 struct MS { float m, s; };
@@ -37,6 +39,8 @@ __global__ void __launch_bounds__(512) ce_rows_kernel(T* logits, int64_t ld, con
     if (threadIdx.x == 0) loss_rows[row] = 0.f;
     return;
   }
+  // debug build: a label outside [0, V) would read (and later write) past the row
+  NFB_DCHECK(tgt >= 0 && tgt < V, 1001, return);
   MS acc{-INFINITY, 0.f};
   for (int64_t i = threadIdx.x; i < nv; i += blockDim.x) {
     float v[8];

@@ -21,6 +21,8 @@
 #include "tc_gemm.cuh"
 #include "tc_host.cuh"
 
+NFB_DEBUG_TU(ce_tc)
+
 namespace nfb {
 namespace tc {
 
@@ -73,6 +75,9 @@ struct CeStatsEpi {
   __device__ void row(int m0, int n0, int r, uint32_t taddr, const GemmShape& sh) {
     const int m = m0 + r;
     const int64_t tgt = m < sh.M ? targets[m] : -1;
+    // debug build: a label outside [0, V) (other than the ignore value, < 0) never matches a column,
+    // so its target logit would silently stay unset
+    if (n0 == 0 && m < sh.M) NFB_DCHECK(tgt < (int64_t)sh.N, 1101, (void)0);
     float mx = -INFINITY, sum = 0.f;
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32) {

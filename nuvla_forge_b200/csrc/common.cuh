@@ -150,6 +150,46 @@ __device__ __forceinline__ void set_status(uint32_t* status, uint32_t code, uint
   }
 }
 
+// ---------------------------------------------------------------------------
+// Debug build (-DNFB_DEBUG, libnfb200_debug.so): device-side bounds and argument checks that a
+// host cannot make cheaply (label values, peer addresses, derived indices). A failed check
+// records (kDebugCheck << 24 | site) in this translation unit's debug word -- the first failure
+// wins -- and the guarded access is skipped; no trap, so the context stays usable and the host
+// reads the word with nfb_debug_status(). In release builds NFB_DCHECK compiles to nothing.
+// NFB_DEBUG_TU(name) defines the word and its host accessors once per .cu file.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kDebugCheck = 4;
+
+#ifdef NFB_DEBUG
+#define NFB_DEBUG_TU(name)                                                                          \
+  static __device__ uint32_t g_nfb_dbg_word;                                                        \
+  __device__ __forceinline__ void nfb_dbg_fail(uint32_t site) {                                     \
+    atomicCAS(&g_nfb_dbg_word, 0u, (nfb::kDebugCheck << 24) | (site & 0xFFFFFFu));                  \
+  }                                                                                                 \
+  extern "C" __attribute__((visibility("default"))) uint32_t nfb_debug_word_##name() {             \
+    uint32_t v = 0;                                                                                 \
+    cudaMemcpyFromSymbol(&v, g_nfb_dbg_word, sizeof(v));                                            \
+    return v;                                                                                       \
+  }                                                                                                 \
+  extern "C" __attribute__((visibility("default"))) void nfb_debug_reset_##name() {                \
+    const uint32_t z = 0;                                                                           \
+    cudaMemcpyToSymbol(g_nfb_dbg_word, &z, sizeof(z));                                              \
+  }
+// Evaluate `cond`; if false, record `site` and run `on_fail` (e.g. `return` or `continue`).
+#define NFB_DCHECK(cond, site, on_fail) \
+  do {                                  \
+    if (!(cond)) {                      \
+      nfb_dbg_fail(site);               \
+      on_fail;                          \
+    }                                   \
+  } while (0)
+#else
+#define NFB_DEBUG_TU(name)
+#define NFB_DCHECK(cond, site, on_fail) \
+  do {                                  \
+  } while (0)
+#endif
+
 // Spin until *flag >= target (wrap-safe comparison of epochs), at most
 // timeout_ns. Returns true on success.
 __device__ __forceinline__ bool wait_flag_geq(const uint32_t* flag, uint32_t target, uint64_t timeout_ns) {

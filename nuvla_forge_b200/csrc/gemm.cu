@@ -19,6 +19,8 @@
 using namespace nfb;
 using namespace nfb::g2;
 
+NFB_DEBUG_TU(gemm)
+
 // Where the last failing GEMM call of this host thread stopped ("" if none).
 static thread_local char g_gemm_err[160] = "";
 
@@ -292,6 +294,8 @@ __global__ void gemm_small_kernel(const TA* __restrict__ A, int64_t sam, int64_t
   if (idx >= (int64_t)M * N) return;
   const int m = (int)(idx / N);
   const int n = (int)(idx - (int64_t)m * N);
+  // debug build: strides that would make an operand walk backwards past its base
+  NFB_DCHECK(sam >= 0 && sak >= 0 && sbn >= 0 && sbk >= 0 && scm >= 0 && scn >= 0, 1201, return);
   const TA* a = A + m * sam;
   const TA* b = B + n * sbn;
   float s = 0.f;

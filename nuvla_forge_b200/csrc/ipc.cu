@@ -49,3 +49,42 @@ NFB_API int nfb_copy_async(void* dst, const void* src, int64_t bytes, void* stre
   if (bytes <= 0) return 0;
   return (int)cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDefault, (cudaStream_t)stream);
 }
+
+// Debug words of the translation units that carry device checks (all zero in release builds).
+#ifdef NFB_DEBUG
+extern "C" uint32_t nfb_debug_word_ce_rows();
+extern "C" uint32_t nfb_debug_word_ce_tc();
+extern "C" uint32_t nfb_debug_word_gemm();
+extern "C" void nfb_debug_reset_ce_rows();
+extern "C" void nfb_debug_reset_ce_tc();
+extern "C" void nfb_debug_reset_gemm();
+#endif
+
+// First failed device check of the debug build (kDebugCheck << 24 | site), 0 if none or release.
+NFB_API uint32_t nfb_debug_status() {
+#ifdef NFB_DEBUG
+  uint32_t v = nfb_debug_word_ce_rows();
+  if (!v) v = nfb_debug_word_ce_tc();
+  if (!v) v = nfb_debug_word_gemm();
+  return v;
+#else
+  return 0;
+#endif
+}
+
+NFB_API void nfb_debug_reset() {
+#ifdef NFB_DEBUG
+  nfb_debug_reset_ce_rows();
+  nfb_debug_reset_ce_tc();
+  nfb_debug_reset_gemm();
+#endif
+}
+
+// 1 in the debug build (device checks compiled in), 0 otherwise.
+NFB_API int nfb_is_debug_build() {
+#ifdef NFB_DEBUG
+  return 1;
+#else
+  return 0;
+#endif
+}

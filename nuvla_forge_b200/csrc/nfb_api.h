@@ -31,6 +31,12 @@ extern "C" {
 NFB_EXPORT int nfb_num_sms(void);
 NFB_EXPORT int nfb_device_synchronize(void);
 
+/* ---- debug build (libnfb200_debug.so, compiled with -DNFB_DEBUG) ------------------------- */
+/* Device-side bounds checks record the first failure as (4 << 24 | site) instead of faulting. */
+NFB_EXPORT uint32_t nfb_debug_status(void);
+NFB_EXPORT void nfb_debug_reset(void);
+NFB_EXPORT int nfb_is_debug_build(void);
+
 /* ---- gated residual + RMSNorm + adaLN modulate (norm.cu) -------------------------------- */
 /* gate_mode: 0 no gate / residual, 1 residual add, 2 per-sample gate [B, N]; mod: 1 applies
  * (1 + scale) and shift per sample. T = tokens per sample. */
