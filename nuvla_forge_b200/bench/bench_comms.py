@@ -33,7 +33,7 @@ import torch.distributed as dist
 
 from .. import _native as nat
 from ..parallel.dist import setup_distributed
-from ..parallel.symm import SLOT_AG, SLOT_DDP, SLOT_RS, SymmetricWorkspace
+from ..parallel.symm import SLOT_AG, SLOT_DDP, SLOT_DDP_B, SLOT_RS, SymmetricWorkspace
 
 NVLINK_GBS = 770.0
 
@@ -62,6 +62,7 @@ def main(argv=None):
     ap.add_argument("--max-mb", type=float, default=1024.0)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--ctas", type=int, default=0, help="CTAs for the fused kernels (0 = by size)")
+    ap.add_argument("--chunk", type=int, default=2048, help="pipelined all-reduce: vectors per slice per step")
     args = ap.parse_args(argv)
     info = setup_distributed()
     rank, world, dev = info.rank, info.world, info.device
@@ -103,13 +104,19 @@ def main(argv=None):
         t32 = src32[:n].clone()
         r = {"bytes": nbytes, "elements": n, "ctas": ctas}
         r["ar_fused_twoshot_ms"] = _time(ar_fused, it, 3, dev)
+
+        def ar_pipe():
+            nat.call("nfb_ar_pipelined", ws.bases_ptr(), rank, world, nat.ptr(src32), nat.ptr(out32), n, send, recv,
+                     ws.flag_off, SLOT_DDP, SLOT_DDP_B, 1.0 / world, ws.next_epoch(SLOT_DDP), ws.timeout_ns,
+                     nat.ptr(ws.status), args.chunk, ctas, s)
+        r["ar_fused_pipelined_ms"] = _time(ar_pipe, it, 3, dev)
         if n <= small_cap:
             def ar_one():
                 nat.call("nfb_ar_oneshot", ws.bases_ptr(), rank, world, nat.ptr(src32), nat.ptr(out32), n, box,
                          small_cap, ws.flag_off, 5, 1.0 / world, ws.next_epoch(5), ws.timeout_ns, nat.ptr(ws.status),
                          min(ctas, 16), s)
             r["ar_fused_oneshot_ms"] = _time(ar_one, it, 3, dev)
-        r["ar_fused_ms"] = min(r["ar_fused_twoshot_ms"], r.get("ar_fused_oneshot_ms", 1e9))
+        r["ar_fused_ms"] = min(r["ar_fused_twoshot_ms"], r["ar_fused_pipelined_ms"], r.get("ar_fused_oneshot_ms", 1e9))
         r["ar_nccl_bf16_ms"] = _time(lambda: dist.all_reduce(t16), it, 3, dev)
         r["ar_nccl_fp32_ms"] = _time(lambda: dist.all_reduce(t32), it, 3, dev)
         nat.call("nfb_cast", 0, 1, __import__("ctypes").c_void_p(ws.local_ptr(send)), nat.ptr(src32), n, 1.0, s)
@@ -132,14 +139,16 @@ def main(argv=None):
         ws.check()
         b16 = n * 2
         ar_f, rs_f = 2 * (world - 1) / world, (world - 1) / world
-        for k, f in (("ar_fused", ar_f), ("ar_nccl_bf16", ar_f), ("rs_fused", rs_f), ("rs_nccl", rs_f),
-                     ("ag_fused", rs_f), ("ag_nccl", rs_f)):
+        for k, f in (("ar_fused", ar_f), ("ar_fused_twoshot", ar_f), ("ar_fused_pipelined", ar_f),
+                     ("ar_nccl_bf16", ar_f), ("rs_fused", rs_f), ("rs_nccl", rs_f), ("ag_fused", rs_f),
+                     ("ag_nccl", rs_f)):
             r[f"{k}_busbw"] = f * b16 / (r[f"{k}_ms"] * 1e-3) / 1e9
         r["ar_nccl_fp32_busbw"] = ar_f * n * 4 / (r["ar_nccl_fp32_ms"] * 1e-3) / 1e9
         rows.append(r)
         if rank == 0:
             print(f"{nbytes:12d} | {r['ar_fused_busbw']:10.1f} {r['ar_nccl_bf16_busbw']:10.1f} {r['ar_nccl_fp32_busbw']:10.1f} | "
                   f"{r['rs_fused_busbw']:10.1f} {r['rs_nccl_busbw']:10.1f} | {r['ag_fused_busbw']:10.1f} {r['ag_nccl_busbw']:10.1f}"
+                  f"   AR twoshot {r['ar_fused_twoshot_busbw']:6.1f} pipelined {r['ar_fused_pipelined_busbw']:6.1f}"
                   f"   fused AR {r['ar_fused_ms']*1e3:8.1f} us vs nccl {r['ar_nccl_bf16_ms']*1e3:8.1f} us")
     if rank == 0:
         rep = {"world_size": world, "device": torch.cuda.get_device_name(dev),

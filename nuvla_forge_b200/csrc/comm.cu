@@ -205,6 +205,102 @@ __global__ void __launch_bounds__(512) ar_twoshot_kernel(ArArgs a) {
   }
 }
 
+// Chunk-pipelined two-shot all-reduce. Each CTA walks its slice range in chunks of `chunk`
+// vectors; per chunk k: (A) push the bf16 cast of chunk k of every slice into its owner's inbox
+// and post progress k+1 on slot_a; (B) once every peer posted chunk k on slot_a, reduce this
+// rank's slice chunk k, push the scaled bf16 result into every rank's outbox and post on slot_b;
+// (C) once every owner posted chunk k on slot_b, unpack chunk k of every slice into fp32. The loop
+// issues A(k), B(k-1), C(k-2) in one iteration, so a chunk's push, reduce and unpack overlap the
+// neighbouring chunks' and no CTA waits for the whole range of any phase. Progress values are
+// epoch * 4096 + chunks done (monotonic across launches, compared wrap-safe). Reuse across
+// launches is safe: a peer's next launch can only start after its unpack waited for this rank's
+// last reduce, and its reduce waits for this rank's pushes of the new launch.
+__device__ __forceinline__ void post_progress(const ArArgs& a, int slot, uint32_t value) {
+  __syncthreads();
+  if ((int)threadIdx.x < a.world) {
+    __threadfence_system();
+    st_release_sys(flag_ptr(a.peers.base[threadIdx.x], a.flag_off, slot, blockIdx.x, a.rank), value);
+  }
+}
+
+__device__ __forceinline__ bool wait_progress(const ArArgs& a, int slot, uint32_t value, uint32_t where) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) s_ok = 1;
+  __syncthreads();
+  if ((int)threadIdx.x < a.world) {
+    const int q = threadIdx.x;
+    if (!wait_flag_geq(flag_ptr(a.peers.base[a.rank], a.flag_off, slot, blockIdx.x, q), value, a.timeout_ns)) {
+      set_status(a.status, kTimeoutBarrier, where | ((uint32_t)q << 16));
+      s_ok = 0;
+    }
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+__global__ void __launch_bounds__(512, 2) ar_pipe_kernel(ArArgs a, int slot_b, int64_t chunk) {
+  const int64_t slice_vecs = a.n / 8 / a.world;
+  const int64_t per_cta = (slice_vecs + gridDim.x - 1) / gridDim.x;
+  const int64_t v0 = (int64_t)blockIdx.x * per_cta;
+  const int64_t v1 = v0 + per_cta < slice_vecs ? v0 + per_cta : slice_vecs;
+  const int nchunks = v1 > v0 ? (int)((v1 - v0 + chunk - 1) / chunk) : 0;
+  const uint32_t base = a.epoch * 4096u;
+  const uint4* outbox = reinterpret_cast<const uint4*>(a.peers.base[a.rank] + a.recv_off);
+  for (int k = 0; k < nchunks + 2; ++k) {
+    if (k < nchunks) {                                   // (A) push chunk k
+      const int64_t c0 = v0 + (int64_t)k * chunk;
+      const int64_t c1 = c0 + chunk < v1 ? c0 + chunk : v1;
+      push_slices(a, slice_vecs, c0, c1);
+      post_progress(a, a.slot, base + (uint32_t)k + 1u);
+    }
+    if (k >= 1 && k - 1 < nchunks) {                     // (B) reduce chunk k-1 and push the result
+      const int kk = k - 1;
+      if (!wait_progress(a, a.slot, base + (uint32_t)kk + 1u, 31)) return;
+      const int64_t c0 = v0 + (int64_t)kk * chunk;
+      const int64_t c1 = c0 + chunk < v1 ? c0 + chunk : v1;
+      for (int64_t v = c0 + threadIdx.x; v < c1; v += (int64_t)blockDim.x * kU) {
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int64_t w = v + (int64_t)u * blockDim.x;
+          if (w < c1) {
+            float acc[8];
+            reduce_inbox(a, slice_vecs, w, acc);
+            uint4 o;
+            f32x8_to_bf16(acc, o);
+#pragma unroll
+            for (int q = 0; q < kMaxWorld; ++q)
+              if (q < a.world)
+                reinterpret_cast<uint4*>(a.peers.base[q] + a.recv_off)[(int64_t)a.rank * slice_vecs + w] = o;
+          }
+        }
+      }
+      post_progress(a, slot_b, base + (uint32_t)kk + 1u);
+    }
+    if (k >= 2) {                                        // (C) unpack chunk k-2
+      const int kk = k - 2;
+      if (!wait_progress(a, slot_b, base + (uint32_t)kk + 1u, 32)) return;
+      const int64_t c0 = v0 + (int64_t)kk * chunk;
+      const int64_t c1 = c0 + chunk < v1 ? c0 + chunk : v1;
+      for (int s = 0; s < a.world; ++s) {
+        for (int64_t v = c0 + threadIdx.x; v < c1; v += (int64_t)blockDim.x * kU) {
+#pragma unroll
+          for (int u = 0; u < kU; ++u) {
+            const int64_t w = v + (int64_t)u * blockDim.x;
+            if (w < c1) {
+              const int64_t idx = (int64_t)s * slice_vecs + w;
+              float f[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) f[j] = 0.f;
+              bf16x8_add(__ldcg(outbox + idx), f);
+              store_f32x8(a.dst + idx * 8, f, false);
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
 // One-shot all-reduce for small buffers (latency-bound): every rank pushes its
 // whole bf16 buffer into every peer's inbox [parity][rank], one barrier, then
 // each rank sums the inboxes locally. Inboxes alternate by epoch parity, so a
@@ -470,6 +566,30 @@ NFB_API int nfb_ar_twoshot(const uint64_t* bases, int rank, int world, const flo
   a.rank = rank; a.world = world; a.slot = slot; a.scale = scale; a.epoch = epoch; a.timeout_ns = timeout_ns;
   a.status = status;
   ar_twoshot_kernel<<<ctas, 512, 0, (cudaStream_t)stream>>>(a);
+  return (int)cudaGetLastError();
+}
+
+// Chunk-pipelined two-shot all-reduce (same buffers and result as nfb_ar_twoshot); progress flags
+// on slot (pushes) and slot_b (reduced results); chunk = vectors of 8 elements per slice per step.
+NFB_API int nfb_ar_pipelined(const uint64_t* bases, int rank, int world, const float* src, float* dst, int64_t n,
+                             int64_t send_off, int64_t recv_off, int64_t flag_off, int slot, int slot_b, float scale,
+                             uint32_t epoch, uint64_t timeout_ns, uint32_t* status, int64_t chunk, int ctas,
+                             void* stream) {
+  if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || slot < 0 || slot >= kSlots || slot_b < 0 ||
+      slot_b >= kSlots || slot_b == slot)
+    return (int)cudaErrorInvalidValue;
+  if (n % (8 * world) || ctas < 1 || ctas > kMaxCtas || chunk < 1) return (int)cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) return (int)cudaErrorInvalidValue;
+  if (n == 0) return 0;
+  const int64_t slice_vecs = n / 8 / world;
+  const int64_t per_cta = (slice_vecs + ctas - 1) / ctas;
+  if ((per_cta + chunk - 1) / chunk >= 4096) return (int)cudaErrorInvalidValue;   // progress counter range
+  ArArgs a;
+  a.peers = make_peers(bases, world);
+  a.src = src; a.dst = dst; a.n = n; a.send_off = send_off; a.recv_off = recv_off; a.flag_off = flag_off;
+  a.rank = rank; a.world = world; a.slot = slot; a.scale = scale; a.epoch = epoch; a.timeout_ns = timeout_ns;
+  a.status = status;
+  ar_pipe_kernel<<<ctas, 512, 0, (cudaStream_t)stream>>>(a, slot_b, chunk);
   return (int)cudaGetLastError();
 }
 

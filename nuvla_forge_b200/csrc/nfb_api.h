@@ -170,6 +170,12 @@ NFB_EXPORT int nfb_comm_flag_bytes(void);
 NFB_EXPORT int nfb_ar_twoshot(const uint64_t* bases, int rank, int world, const float* src, float* dst, int64_t n,
                               int64_t send_off, int64_t recv_off, int64_t flag_off, int slot, float scale,
                               uint32_t epoch, uint64_t timeout_ns, uint32_t* status, int ctas, void* stream);
+/* Chunk-pipelined two-shot all-reduce: same buffers and result as nfb_ar_twoshot; progress flags on
+ * slot and slot_b; chunk = 8-element vectors per slice per pipeline step. */
+NFB_EXPORT int nfb_ar_pipelined(const uint64_t* bases, int rank, int world, const float* src, float* dst, int64_t n,
+                                int64_t send_off, int64_t recv_off, int64_t flag_off, int slot, int slot_b,
+                                float scale, uint32_t epoch, uint64_t timeout_ns, uint32_t* status, int64_t chunk,
+                                int ctas, void* stream);
 NFB_EXPORT int nfb_ar_oneshot(const uint64_t* bases, int rank, int world, const float* src, float* dst, int64_t n,
                               int64_t box_off, int64_t cap_elems, int64_t flag_off, int slot, float scale,
                               uint32_t epoch, uint64_t timeout_ns, uint32_t* status, int ctas, void* stream);

@@ -25,6 +25,7 @@ and owns the data path:
 from __future__ import annotations
 
 import contextlib
+import os
 from dataclasses import dataclass
 
 import torch
@@ -34,9 +35,10 @@ from torch import nn
 from .. import _native as nat
 from ..profiling import trace
 from .flat import FlatParamSpace
-from .symm import SLOT_DDP, SLOT_DDP_SMALL, SymmetricWorkspace, symmetric_memory_available
+from .symm import SLOT_DDP, SLOT_DDP_B, SLOT_DDP_SMALL, SymmetricWorkspace, symmetric_memory_available
 
 ONESHOT_MAX_ELEMS = 256 * 1024   # buckets up to 512 KB of bf16 use the one-barrier all-reduce
+AR_CHUNK_VECS = 2048             # pipelined all-reduce: 16 K elements per slice per pipeline step
 
 
 @dataclass
@@ -98,6 +100,8 @@ class DistributedDataParallel(nn.Module):
         self._callback_queued = False
         self.comm_stream = torch.cuda.Stream(device=dev) if dev.type == "cuda" else None
         self.ctas = ctas
+        # "pipelined" (chunked phases, default) or "twoshot" (whole-range phases) for large buckets
+        self.ar_impl = os.environ.get("NFB_AR_IMPL", "pipelined")
         self.ws = None
         if comm == "fused":
             maxb = max(b.end - b.start for b in self.buckets)
@@ -223,6 +227,11 @@ class DistributedDataParallel(nn.Module):
                 nat.call("nfb_ar_oneshot", ws.bases_ptr(), ws.rank, ws.world, nat.ptr(g), nat.ptr(g), g.numel(),
                          self.box_off, self.small_cap, ws.flag_off, SLOT_DDP_SMALL, scale,
                          ws.next_epoch(SLOT_DDP_SMALL), ws.timeout_ns, nat.ptr(ws.status), 8,
+                         nat.stream(self.device))
+            elif self.ar_impl == "pipelined":
+                nat.call("nfb_ar_pipelined", ws.bases_ptr(), ws.rank, ws.world, nat.ptr(g), nat.ptr(g), g.numel(),
+                         self.send_off, self.recv_off, ws.flag_off, SLOT_DDP, SLOT_DDP_B, scale,
+                         ws.next_epoch(SLOT_DDP), ws.timeout_ns, nat.ptr(ws.status), AR_CHUNK_VECS, self.ctas,
                          nat.stream(self.device))
             else:
                 nat.call("nfb_ar_twoshot", ws.bases_ptr(), ws.rank, ws.world, nat.ptr(g), nat.ptr(g), g.numel(),

@@ -7,9 +7,11 @@ the wire. Running every rank and every CTA of a phase before the next phase
 starts is exactly what the kernels' CTA-pairwise barriers guarantee, so the
 emulated result must equal a plain reduction of the bf16-rounded inputs; the
 tests check that for many shapes, and check the all-gather GEMM's chunk
-schedule for coverage and order. (Device counterparts: ``ar_twoshot_kernel``,
-``ar_oneshot_kernel``, ``rs_push_kernel`` in csrc/comm.cu and
-``AgGate::worker`` in csrc/ag_gemm.cu.)
+schedule for coverage and order. The chunk-pipelined all-reduce is emulated
+with ranks and CTAs interleaved at random, so its flag protocol (and buffer
+reuse across launches) is checked for deadlocks and stale reads. (Device
+counterparts: ``ar_twoshot_kernel``, ``ar_pipe_kernel``, ``ar_oneshot_kernel``,
+``rs_push_kernel`` in csrc/comm.cu and ``AgGate::worker`` in csrc/ag_gemm.cu.)
 """
 
 from __future__ import annotations
@@ -102,6 +104,117 @@ def reduce_scatter_push(srcs: list[np.ndarray], ctas: int, scale: float) -> list
             out[v0 * 8: v1 * 8] = acc * np.float32(scale)
         shards.append(out)
     return shards
+
+
+def pipelined_allreduce(launches: list[list[np.ndarray]], ctas: int, chunk: int, scale: float,
+                        seed: int = 0, epoch0: int = 1) -> list[list[np.ndarray]]:
+    """Emulate ``ar_pipe_kernel`` for consecutive launches, with ranks and CTAs interleaved at random.
+
+    Every (launch, rank, CTA) is a program of steps A(k) push / B(k) reduce / C(k) unpack in the
+    kernel's order (A(k), B(k-1), C(k-2) per iteration) that waits on the same progress flags
+    (slot A and slot B, value epoch * 4096 + chunks done). A scheduler repeatedly runs a random
+    program whose next step is not blocked; a launch of a rank starts only after that rank's
+    previous launch finished (stream order). Raises RuntimeError on a deadlock and on any read of
+    an inbox / outbox cell that a different launch or chunk wrote last (a reuse race).
+    Returns the fp32 outputs per launch and rank.
+    """
+    rnd = np.random.default_rng(seed)
+    world = len(launches[0])
+    n = launches[0][0].size
+    slice_vecs = n // 8 // world
+    sv = slice_vecs * 8
+    per = (slice_vecs + ctas - 1) // ctas
+    inbox = [np.zeros(n, np.float32) for _ in range(world)]
+    outbox = [np.zeros(n, np.float32) for _ in range(world)]
+    in_tag = [np.full(n // 8, -1, np.int64) for _ in range(world)]      # which (launch, chunk) wrote it
+    out_tag = [np.full(n // 8, -1, np.int64) for _ in range(world)]
+    flag_a = np.zeros((world, ctas, world), np.int64)                   # [owner][cta][src]
+    flag_b = np.zeros((world, ctas, world), np.int64)
+    outs = [[np.zeros(n, np.float32) for _ in range(world)] for _ in launches]
+
+    def program(li, r, b):
+        v0 = b * per
+        v1 = min(v0 + per, slice_vecs)
+        nch = (v1 - v0 + chunk - 1) // chunk if v1 > v0 else 0
+        base = (epoch0 + li) * 4096
+        steps = []
+        for k in range(nch + 2):
+            if k < nch:
+                steps.append(("A", k))
+            if 1 <= k <= nch:
+                steps.append(("B", k - 1))
+            if k >= 2:
+                steps.append(("C", k - 2))
+        return {"li": li, "r": r, "b": b, "v0": v0, "v1": v1, "base": base, "steps": steps, "pc": 0}
+
+    def rng_of(p, k):
+        c0 = p["v0"] + k * chunk
+        return c0, min(c0 + chunk, p["v1"])
+
+    def blocked(p):
+        op, k = p["steps"][p["pc"]]
+        want = p["base"] + k + 1
+        if op == "B":
+            return bool((flag_a[p["r"], p["b"], :] < want).any())
+        if op == "C":
+            return bool((flag_b[p["r"], p["b"], :] < want).any())
+        return False
+
+    def run(p):
+        op, k = p["steps"][p["pc"]]
+        li, r, b = p["li"], p["r"], p["b"]
+        c0, c1 = rng_of(p, k)
+        tag = li * 100000 + k
+        src = launches[li][r]
+        if op == "A":
+            for s_ in range(world):
+                seg = src[s_ * sv + c0 * 8: s_ * sv + c1 * 8]
+                inbox[s_][r * sv + c0 * 8: r * sv + c1 * 8] = bf16_round(seg)
+                in_tag[s_][r * slice_vecs + c0: r * slice_vecs + c1] = tag
+            flag_a[:, b, r] = p["base"] + k + 1
+        elif op == "B":
+            acc = np.zeros((c1 - c0) * 8, np.float32)
+            for q in range(world):
+                if (in_tag[r][q * slice_vecs + c0: q * slice_vecs + c1] != tag).any():
+                    raise RuntimeError(f"stale inbox read: launch {li} rank {r} cta {b} chunk {k} from {q}")
+                acc += inbox[r][q * sv + c0 * 8: q * sv + c1 * 8]
+            res = bf16_round(acc * np.float32(scale))
+            for q in range(world):
+                outbox[q][r * sv + c0 * 8: r * sv + c1 * 8] = res
+                out_tag[q][r * slice_vecs + c0: r * slice_vecs + c1] = tag
+            flag_b[:, b, r] = p["base"] + k + 1
+        else:
+            for s_ in range(world):
+                if (out_tag[r][s_ * slice_vecs + c0: s_ * slice_vecs + c1] != tag).any():
+                    raise RuntimeError(f"stale outbox read: launch {li} rank {r} cta {b} chunk {k} slice {s_}")
+                outs[li][r][s_ * sv + c0 * 8: s_ * sv + c1 * 8] = outbox[r][s_ * sv + c0 * 8: s_ * sv + c1 * 8]
+        p["pc"] += 1
+
+    # per rank: the queue of launches; a rank's launch li+1 starts when all its CTAs finished li
+    pending = {r: list(range(len(launches))) for r in range(world)}
+    active: list[dict] = []
+
+    def start_next(r):
+        while pending[r]:
+            li = pending[r].pop(0)
+            progs = [pr for pr in (program(li, r, b) for b in range(ctas)) if pr["steps"]]   # empty CTAs exit
+            if progs:
+                active.extend(progs)
+                return
+
+    for r in range(world):
+        start_next(r)
+    while active:
+        ready = [p for p in active if not blocked(p)]
+        if not ready:
+            raise RuntimeError("deadlock: every active CTA waits on a progress flag")
+        p = ready[int(rnd.integers(len(ready)))]
+        run(p)
+        if p["pc"] == len(p["steps"]):
+            active.remove(p)
+            if not any(q["r"] == p["r"] and q["li"] == p["li"] for q in active):
+                start_next(p["r"])
+    return outs
 
 
 # ------------------------------------------------------- all-gather GEMM chunk schedule

@@ -26,7 +26,7 @@ import torch.distributed as dist
 
 from .. import _native as nat
 
-SLOT_DDP, SLOT_RS, SLOT_AG, SLOT_SCALAR, SLOT_TEST, SLOT_DDP_SMALL = 0, 1, 2, 3, 4, 5
+SLOT_DDP, SLOT_RS, SLOT_AG, SLOT_SCALAR, SLOT_TEST, SLOT_DDP_SMALL, SLOT_DDP_B = 0, 1, 2, 3, 4, 5, 6
 
 
 class CommTimeout(RuntimeError):

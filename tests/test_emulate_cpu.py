@@ -23,6 +23,20 @@ def test_two_shot_allreduce_schedule(world, n, ctas):
         np.testing.assert_allclose(o, ref, rtol=0, atol=1e-6)
 
 
+@pytest.mark.parametrize("world,n,ctas,chunk", [(2, 8 * 2 * 100, 3, 7), (4, 8 * 4 * 64, 5, 4), (8, 8 * 8 * 40, 4, 3),
+                                                (3, 8 * 3 * 10, 16, 1)])
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_pipelined_allreduce_random_interleavings(world, n, ctas, chunk, seed):
+    """Three back-to-back launches, ranks and CTAs interleaved at random: no deadlock, no stale read."""
+    rng = np.random.default_rng(seed + world)
+    launches = [[rng.standard_normal(n).astype(np.float32) for _ in range(world)] for _ in range(3)]
+    outs = em.pipelined_allreduce(launches, ctas, chunk, 1.0 / world, seed=seed)
+    for srcs, got in zip(launches, outs):
+        ref = em.bf16_round(_ref_sum(srcs, 1.0 / world))
+        for o in got:
+            np.testing.assert_allclose(o, ref, rtol=0, atol=1e-6)
+
+
 @pytest.mark.parametrize("world,n,ctas", [(2, 64, 3), (8, 8 * 8 * 77, 16)])
 def test_one_shot_allreduce_schedule(world, n, ctas):
     rng = np.random.default_rng(world)

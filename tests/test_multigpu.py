@@ -22,11 +22,11 @@ def _world():
     return min(torch.cuda.device_count(), int(os.environ.get("NFB_TEST_MAX_WORLD", "4")))
 
 
-def _fused_ar(rank, world, sizes):
+def _fused_ar(rank, world, sizes, impl="twoshot"):
     import torch.distributed as dist
 
     from nuvla_forge_b200 import _native as nat
-    from nuvla_forge_b200.parallel.symm import SLOT_DDP, SymmetricWorkspace
+    from nuvla_forge_b200.parallel.symm import SLOT_DDP, SLOT_DDP_B, SymmetricWorkspace
 
     dev = torch.device("cuda", rank)
     maxn = max(sizes)
@@ -42,9 +42,14 @@ def _fused_ar(rank, world, sizes):
         y = x.clone()
         for _ in range(2):
             y.copy_(x)
-            nat.call("nfb_ar_twoshot", ws.bases_ptr(), rank, world, nat.ptr(y), nat.ptr(y), n, send, recv,
-                     ws.flag_off, SLOT_DDP, 1.0 / world, ws.next_epoch(SLOT_DDP), ws.timeout_ns, nat.ptr(ws.status),
-                     32, nat.stream(dev))
+            if impl == "pipelined":
+                nat.call("nfb_ar_pipelined", ws.bases_ptr(), rank, world, nat.ptr(y), nat.ptr(y), n, send, recv,
+                         ws.flag_off, SLOT_DDP, SLOT_DDP_B, 1.0 / world, ws.next_epoch(SLOT_DDP), ws.timeout_ns,
+                         nat.ptr(ws.status), 512, 32, nat.stream(dev))
+            else:
+                nat.call("nfb_ar_twoshot", ws.bases_ptr(), rank, world, nat.ptr(y), nat.ptr(y), n, send, recv,
+                         ws.flag_off, SLOT_DDP, 1.0 / world, ws.next_epoch(SLOT_DDP), ws.timeout_ns,
+                         nat.ptr(ws.status), 32, nat.stream(dev))
         torch.cuda.synchronize(dev)
         ws.check()
         err = float((y.double() - ref).norm() / ref.norm())
@@ -54,10 +59,11 @@ def _fused_ar(rank, world, sizes):
     return worst
 
 
-def test_fused_allreduce_matches_reference():
+@pytest.mark.parametrize("impl", ["twoshot", "pipelined"])
+def test_fused_allreduce_matches_reference(impl):
     w = _world()
     sizes = [8 * w, 8 * w * 1000, 8 * w * 131071, 8 * w * 1048576]
-    out = run_ranks(_fused_ar, w, args=(sizes,), backend="nccl", env=ENV, timeout_s=60)
+    out = run_ranks(_fused_ar, w, args=(sizes, impl), backend="nccl", env=ENV, timeout_s=60)
     assert len(out) == w and all(st == "ok" for st, _ in out.values()), out
     assert max(r for _, r in out.values()) < 4e-3
 
