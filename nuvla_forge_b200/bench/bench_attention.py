@@ -2,6 +2,7 @@
 
     python -m nuvla_forge_b200.bench.bench_attention [--out reports/attention.json]
 
+Forward and backward are both timed (backward FLOPs = 2.5x the forward's).
 Shapes are the attention calls of one BASELINE config-3 micro-batch (8 samples):
 the ViT self-attention over 96 images of 1024 patches (16 heads, D 64), the
 causal GQA backbone over 3392 tokens (16 q / 8 kv heads, D 128) and the DiT
@@ -67,9 +68,21 @@ def main(argv=None):
         r = {"shape": name, "native_ms": native, "sdpa_ms": sdpa, "flops": flops,
              "native_tflops": flops / native / 1e9, "sdpa_tflops": flops / sdpa / 1e9,
              "native_frac_of_measured_bf16": flops / native / 1e9 / peaks["bf16_tflops"]}
+        # backward: native (pre + main + dQ convert) vs SDPA's backward (autograd of cuDNN SDPA),
+        # 2.5x the forward FLOPs (five GEMMs of the forward's size)
+        out, lse = flash_attn.attention_fwd(q, k, v, causal)
+        dout = torch.randn_like(out)
+        nb = _time(lambda: flash_attn.attention_bwd(q, k, v, out, dout, lse, causal), args.iters, flush)
+        qr, kr, vr = (t.detach().requires_grad_(True) for t in (qt, kt, vt))
+        o_ref = F.scaled_dot_product_attention(qr, kr, vr, is_causal=causal, enable_gqa=Hkv != Hq)
+        go = dout.transpose(1, 2)
+        sb = _time(lambda: torch.autograd.grad(o_ref, (qr, kr, vr), go, retain_graph=True), args.iters, flush)
+        r.update(native_bwd_ms=nb, sdpa_bwd_ms=sb, native_bwd_tflops=2.5 * flops / nb / 1e9,
+                 sdpa_bwd_tflops=2.5 * flops / sb / 1e9)
         rows.append(r)
-        print(f"{name:<40} native {native:8.3f} ms ({r['native_tflops']:6.0f} TF/s) | SDPA {sdpa:8.3f} ms "
-              f"({r['sdpa_tflops']:6.0f} TF/s)")
+        print(f"{name:<40} fwd native {native:8.3f} ms ({r['native_tflops']:6.0f} TF/s) | SDPA {sdpa:8.3f} ms "
+              f"({r['sdpa_tflops']:6.0f} TF/s) || bwd native {nb:8.3f} ms ({r['native_bwd_tflops']:6.0f} TF/s) | "
+              f"SDPA {sb:8.3f} ms ({r['sdpa_bwd_tflops']:6.0f} TF/s)", flush=True)
         flash_attn.check_status()
     out = Path(args.out)
     out.parent.mkdir(parents=True, exist_ok=True)

@@ -156,6 +156,15 @@ NFB_EXPORT int nfb_attn_fwd(const void* q, const void* k, const void* v, void* o
                             int64_t sk_s, int64_t sk_h, int64_t sv_b, int64_t sv_s, int64_t sv_h, int64_t so_b,
                             int64_t so_s, int64_t so_h, int causal, float scale, uint32_t* status, void* stream);
 
+/* Backward of nfb_attn_fwd: dq, dk, dv ([B, S, H, D], any 16-byte-aligned strides) from q, k, v, o, do and
+ * the forward's lse. strides: 24 element strides, (batch, token, head) of q, k, v, o, do, dq, dk, dv.
+ * scratch: nfb_attn_bwd_scratch_bytes(B, Sq, Hq, D) bytes (16-byte aligned). Three launches. */
+NFB_EXPORT int64_t nfb_attn_bwd_scratch_bytes(int B, int Sq, int Hq, int D);
+NFB_EXPORT int nfb_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                            const float* lse, void* dq, void* dk, void* dv, void* scratch, int B, int Sq, int Sk,
+                            int Hq, int Hkv, int D, const int64_t* strides, int causal, float scale,
+                            uint32_t* status, void* stream);
+
 /* ---- peer memory (ipc.cu) --------------------------------------------------------------- */
 NFB_EXPORT int nfb_ipc_handle_bytes(void);
 NFB_EXPORT int nfb_ipc_alloc(uint64_t bytes, void** ptr, void* handle_out);

@@ -1,19 +1,20 @@
-"""Native flash-attention forward on tcgen05 (csrc/attention.cu).
+"""Native flash attention on tcgen05: forward (csrc/attention.cu) and backward (csrc/attention_bwd.cu).
 
-``attention_fwd(q, k, v, causal, scale)`` runs the sm_100a kernel on the
+``attention_fwd(q, k, v, causal, scale)`` runs the sm_100a forward on the
 projection-native [B, S, H, D] layout and returns (out [B, S, Hq, D], lse
-[B, Hq, S]) or None when the inputs are outside what it supports (bf16, D in
-{64, 128}, 16-byte-aligned rows, Hkv dividing Hq).
+[B, Hq, S]); ``attention_bwd`` returns (dq, dk, dv) from the saved inputs, the
+output, its gradient and lse. Both return None when the inputs are outside what
+the kernels support (bf16, D in {64, 128}, 16-byte-aligned rows, Hkv dividing
+Hq, and for a causal mask Sq == Sk: the kernels align the mask to the bottom
+right, which only equals PyTorch's top-left ``is_causal`` for square masks).
 
 ``enable()`` (or ``NFB_ATTN_NATIVE=1`` at import) routes ``ops.attention``
-through it. Its backward recomputes the forward with PyTorch SDPA and
-differentiates that, so training is correct but pays one extra attention
-forward; the cuDNN path stays the default for training until the native
-backward exists.
+through them (forward and backward).
 """
 
 from __future__ import annotations
 
+import ctypes
 import os
 
 import torch
@@ -23,6 +24,8 @@ from .. import _native as nat
 from .attention import register_native
 
 _status: dict[int, torch.Tensor] = {}
+# NFB_ATTN_NATIVE_BWD=0 keeps the native forward but differentiates through SDPA (for A/B comparisons)
+_NATIVE_BWD = os.environ.get("NFB_ATTN_NATIVE_BWD", "1") == "1"
 
 
 def _status_word(device: torch.device) -> torch.Tensor:
@@ -39,8 +42,10 @@ def check_status(device: torch.device | None = None) -> None:
         raise RuntimeError(f"native attention gave up waiting (status {v:#x})")
 
 
-def supported(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> bool:
+def supported(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False) -> bool:
     if not (nat.HAS_NATIVE and q.is_cuda and q.dtype == torch.bfloat16 and k.dtype == q.dtype and v.dtype == q.dtype):
+        return False
+    if causal and q.shape[1] != k.shape[1]:
         return False
     if q.dim() != 4 or q.shape[-1] not in (64, 128) or k.shape[-1] != q.shape[-1] or v.shape[-1] != q.shape[-1]:
         return False
@@ -54,7 +59,7 @@ def supported(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> bool:
 
 def attention_fwd(q, k, v, causal: bool = False, scale: float | None = None):
     """(out, lse) from the native kernel, or None when unsupported."""
-    if not supported(q, k, v):
+    if not supported(q, k, v, causal):
         return None
     B, Sq, Hq, D = q.shape
     Sk, Hkv = k.shape[1], k.shape[2]
@@ -68,17 +73,44 @@ def attention_fwd(q, k, v, causal: bool = False, scale: float | None = None):
     return out, lse
 
 
+def attention_bwd(q, k, v, out, dout, lse, causal: bool = False, scale: float | None = None):
+    """(dq, dk, dv) from the native backward (3 launches), or None when unsupported."""
+    if not supported(q, k, v, causal) or dout.dtype != q.dtype or dout.stride(-1) != 1 or dout.data_ptr() % 16 \
+            or any(s % 8 for s in dout.stride()[:3]):
+        return None
+    B, Sq, Hq, D = q.shape
+    Sk, Hkv = k.shape[1], k.shape[2]
+    dq = torch.empty((B, Sq, Hq, D), dtype=q.dtype, device=q.device)
+    dk = torch.empty((B, Sk, Hkv, D), dtype=q.dtype, device=q.device)
+    dv = torch.empty((B, Sk, Hkv, D), dtype=q.dtype, device=q.device)
+    nbytes = int(nat.lib().nfb_attn_bwd_scratch_bytes(B, Sq, Hq, D))
+    scratch = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+    st = []
+    for t in (q, k, v, out, dout, dq, dk, dv):
+        st += [t.stride(0), t.stride(1), t.stride(2)]
+    strides = (ctypes.c_int64 * 24)(*st)
+    sc = float(scale) if scale is not None else D ** -0.5
+    nat.call("nfb_attn_bwd", nat.ptr(q), nat.ptr(k), nat.ptr(v), nat.ptr(out), nat.ptr(dout), nat.ptr(lse),
+             nat.ptr(dq), nat.ptr(dk), nat.ptr(dv), nat.ptr(scratch), B, Sq, Sk, Hq, Hkv, D, strides, int(causal), sc,
+             nat.ptr(_status_word(q.device)), nat.stream(q.device))
+    return dq, dk, dv
+
+
 class _NativeAttention(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, causal, scale):
-        out, _ = attention_fwd(q, k, v, causal, scale)
-        ctx.save_for_backward(q, k, v)
+        out, lse = attention_fwd(q, k, v, causal, scale)
+        ctx.save_for_backward(q, k, v, out, lse)
         ctx.causal, ctx.scale = causal, scale
         return out
 
     @staticmethod
     def backward(ctx, g):
-        q, k, v = ctx.saved_tensors
+        q, k, v, out, lse = ctx.saved_tensors
+        if _NATIVE_BWD:
+            res = attention_bwd(q, k, v, out, g.contiguous() if g.stride(-1) != 1 else g, lse, ctx.causal, ctx.scale)
+            if res is not None:
+                return res[0], res[1], res[2], None, None
         with torch.enable_grad():
             qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
             o = F.scaled_dot_product_attention(qq.transpose(1, 2), kk.transpose(1, 2), vv.transpose(1, 2),
@@ -89,7 +121,7 @@ class _NativeAttention(torch.autograd.Function):
 
 
 def _native(q, k, v, causal, scale):
-    if not supported(q, k, v):
+    if not supported(q, k, v, causal):
         return None
     if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
         return _NativeAttention.apply(q, k, v, causal, scale)

@@ -100,8 +100,8 @@ class DistributedDataParallel(nn.Module):
         self._callback_queued = False
         self.comm_stream = torch.cuda.Stream(device=dev) if dev.type == "cuda" else None
         self.ctas = ctas
-        # "pipelined" (chunked phases, default) or "twoshot" (whole-range phases) for large buckets
-        self.ar_impl = os.environ.get("NFB_AR_IMPL", "pipelined")
+        # "twoshot" (whole-range phases, default: faster on B200) or "pipelined" (chunked phases)
+        self.ar_impl = os.environ.get("NFB_AR_IMPL", "twoshot")
         self.ws = None
         if comm == "fused":
             maxb = max(b.end - b.start for b in self.buckets)
