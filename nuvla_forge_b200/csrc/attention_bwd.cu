@@ -416,26 +416,23 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       bool w = mbar_wait_sleep(&S->acc_full, 0u, abort_flag);
       if (compute_all(w)) {
         tmem_fence_after();
-        if (key < a.Sk) {
-          __nv_bfloat16* dkr = a.dk + (int64_t)b * a.sdk_b + (int64_t)key * a.sdk_s + (int64_t)hk * a.sdk_h;
-          __nv_bfloat16* dvr = a.dv + (int64_t)b * a.sdv_b + (int64_t)key * a.sdv_s + (int64_t)hk * a.sdv_h;
+        // tcgen05.ld is warp-collective: every lane loads, only rows of real keys are stored
+        const bool live = key < a.Sk;
+        __nv_bfloat16* dkr = a.dk + (int64_t)b * a.sdk_b + (int64_t)key * a.sdk_s + (int64_t)hk * a.sdk_h;
+        __nv_bfloat16* dvr = a.dv + (int64_t)b * a.sdv_b + (int64_t)key * a.sdv_s + (int64_t)hk * a.sdv_h;
 #pragma unroll
-          for (int c = 0; c < D / 2; c += 32) {
-            float g[32];
-            const int col = half * (D / 2) + c;
-            tmem_ld32(tmem + lane_off + L::cDK + (uint32_t)col, g);
+        for (int c = 0; c < D / 2; c += 32) {
+          float g[32];
+          const int col = half * (D / 2) + c;
+          tmem_ld32(tmem + lane_off + L::cDK + (uint32_t)col, g);
+          if (live) {
 #pragma unroll
             for (int j = 0; j < 32; j += 8) store16<__nv_bfloat16>(dkr + col + j, g + j);
-            tmem_ld32(tmem + lane_off + L::cDV + (uint32_t)col, g);
+          }
+          tmem_ld32(tmem + lane_off + L::cDV + (uint32_t)col, g);
+          if (live) {
 #pragma unroll
             for (int j = 0; j < 32; j += 8) store16<__nv_bfloat16>(dvr + col + j, g + j);
-          }
-        } else {
-          float g[32];
-#pragma unroll
-          for (int c = 0; c < D / 2; c += 32) {                 // keep the warp-collective loads uniform
-            tmem_ld32(tmem + lane_off + L::cDK + (uint32_t)(half * (D / 2) + c), g);
-            tmem_ld32(tmem + lane_off + L::cDV + (uint32_t)(half * (D / 2) + c), g);
           }
         }
       } else {
