@@ -55,6 +55,7 @@ _SIGS: dict[str, tuple] = {
     "nfb_ar_oneshot": (I, [P, I, I, P, P, L, L, L, L, I, F, U32, U64, P, I, P]),
     "nfb_ar_pipelined": (I, [P, I, I, P, P, L, L, L, L, I, I, F, U32, U64, P, L, I, P]),
     "nfb_rs_push": (I, [P, I, I, P, L, L, L, I, F, U32, U64, P, P, I, I, P]),
+    "nfb_rs_push_sumsq": (I, [P, I, I, P, L, L, L, I, F, U32, U64, P, P, I, P, P, P, I, P]),
     "nfb_rs_f32": (I, [P, I, I, L, L, L, I, F, U32, U64, P, P, P, P, P, I, I, I, P]),
     "nfb_rs_adamw": (I, [P, I, I, L, L, L, I, F, U32, U64, P, P, P, P, L, F, F, F, F, F, L, F, I, I, P]),
     "nfb_allgather": (I, [P, I, I, L, L, P, L, I, U32, U64, P, I, P]),

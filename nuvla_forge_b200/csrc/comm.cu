@@ -335,17 +335,48 @@ __global__ void __launch_bounds__(512) ar_oneshot_kernel(ArArgs a, int64_t cap_v
   }
 }
 
+// Deterministic block sum of `v` added into *out by the last CTA to finish (fixed CTA order);
+// partials [gridDim], ticket zeroed before the first launch and re-zeroed by the last CTA.
+__device__ void grid_sum_into(float v, float* partials, uint32_t* ticket, float* out) {
+  __shared__ float red[32];
+  __shared__ uint32_t s_t;
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) {
+      partials[blockIdx.x] = t;
+      __threadfence();
+      s_t = atomicAdd(ticket, 1u);
+    }
+  }
+  __syncthreads();
+  if (s_t == gridDim.x - 1 && threadIdx.x == 0) {
+    __threadfence();
+    float tot = 0.f;
+    for (unsigned b = 0; b < gridDim.x; ++b) tot += __ldcg(partials + b);
+    *out += tot;
+    *ticket = 0u;
+  }
+}
+
 // Reduce-scatter by pushes, taking the local fp32 gradient directly (the bf16
 // cast is fused): push slices, one barrier, reduce the local inbox into the
 // fp32 shard (overwrite or accumulate), a trailing barrier so the inbox may be
-// reused by the next launch.
-__global__ void __launch_bounds__(512) rs_push_kernel(ArArgs a, int accumulate) {
+// reused by the next launch. With sumsq_out, the shard's sum of squares (of the
+// reduced, scaled values) is added into *sumsq_out: the first phase of the
+// global gradient-norm clip, so the optimizer needs no separate pass.
+__global__ void __launch_bounds__(512) rs_push_kernel(ArArgs a, int accumulate, float* sumsq_partials,
+                                                      uint32_t* ticket, float* sumsq_out) {
   const int64_t slice_vecs = a.n / 8 / a.world;
   const int64_t per_cta = (slice_vecs + gridDim.x - 1) / gridDim.x;
   const int64_t v0 = (int64_t)blockIdx.x * per_cta;
   const int64_t v1 = v0 + per_cta < slice_vecs ? v0 + per_cta : slice_vecs;
   push_slices(a, slice_vecs, v0, v1);
   if (!cta_barrier(a.peers, a.rank, a.world, a.flag_off, a.slot, 2u * a.epoch + 1u, a.timeout_ns, a.status, 11)) return;
+  float ss = 0.f;
   for (int64_t v = v0 + threadIdx.x; v < v1; v += (int64_t)blockDim.x * kU) {
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
@@ -353,10 +384,13 @@ __global__ void __launch_bounds__(512) rs_push_kernel(ArArgs a, int accumulate) 
       if (w < v1) {
         float acc[8];
         reduce_inbox(a, slice_vecs, w, acc);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss += acc[j] * acc[j];
         store_f32x8(a.dst + w * 8, acc, accumulate != 0);
       }
     }
   }
+  if (sumsq_out) grid_sum_into(ss, sumsq_partials, ticket, sumsq_out);
   cta_barrier(a.peers, a.rank, a.world, a.flag_off, a.slot, 2u * a.epoch + 2u, a.timeout_ns, a.status, 12);
 }
 
@@ -615,6 +649,17 @@ NFB_API int nfb_ar_oneshot(const uint64_t* bases, int rank, int world, const flo
 NFB_API int nfb_rs_push(const uint64_t* bases, int rank, int world, const float* src, int64_t n, int64_t inbox_off,
                         int64_t flag_off, int slot, float scale, uint32_t epoch, uint64_t timeout_ns, uint32_t* status,
                         float* out, int accumulate, int ctas, void* stream) {
+  return nfb_rs_push_sumsq(bases, rank, world, src, n, inbox_off, flag_off, slot, scale, epoch, timeout_ns, status,
+                           out, accumulate, nullptr, nullptr, nullptr, ctas, stream);
+}
+
+// nfb_rs_push that also adds the shard's sum of squares into *sumsq_out (overwrite mode only):
+// sumsq_partials [>= ctas] fp32, ticket a zeroed uint32 (left zeroed).
+NFB_API int nfb_rs_push_sumsq(const uint64_t* bases, int rank, int world, const float* src, int64_t n,
+                              int64_t inbox_off, int64_t flag_off, int slot, float scale, uint32_t epoch,
+                              uint64_t timeout_ns, uint32_t* status, float* out, int accumulate,
+                              float* sumsq_partials, uint32_t* ticket, float* sumsq_out, int ctas, void* stream) {
+  if (sumsq_out && (accumulate || !sumsq_partials || !ticket)) return (int)cudaErrorInvalidValue;
   if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || slot < 0 || slot >= kSlots) return (int)cudaErrorInvalidValue;
   if (n % (8 * world) || ctas < 1 || ctas > kMaxCtas) return (int)cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(out)) & 15) return (int)cudaErrorInvalidValue;
@@ -624,7 +669,7 @@ NFB_API int nfb_rs_push(const uint64_t* bases, int rank, int world, const float*
   a.src = src; a.dst = out; a.n = n; a.send_off = inbox_off; a.recv_off = 0; a.flag_off = flag_off;
   a.rank = rank; a.world = world; a.slot = slot; a.scale = scale; a.epoch = epoch; a.timeout_ns = timeout_ns;
   a.status = status;
-  rs_push_kernel<<<ctas, 512, 0, (cudaStream_t)stream>>>(a, accumulate);
+  rs_push_kernel<<<ctas, 512, 0, (cudaStream_t)stream>>>(a, accumulate, sumsq_partials, ticket, sumsq_out);
   return (int)cudaGetLastError();
 }
 

@@ -191,6 +191,12 @@ NFB_EXPORT int nfb_ar_oneshot(const uint64_t* bases, int rank, int world, const 
 NFB_EXPORT int nfb_rs_push(const uint64_t* bases, int rank, int world, const float* src, int64_t n,
                            int64_t inbox_off, int64_t flag_off, int slot, float scale, uint32_t epoch,
                            uint64_t timeout_ns, uint32_t* status, float* out, int accumulate, int ctas, void* stream);
+/* nfb_rs_push that also adds the shard's sum of squares into *sumsq_out (first phase of the global
+ * gradient-norm clip; overwrite mode only). sumsq_partials >= ctas floats, ticket a zeroed word. */
+NFB_EXPORT int nfb_rs_push_sumsq(const uint64_t* bases, int rank, int world, const float* src, int64_t n,
+                                 int64_t inbox_off, int64_t flag_off, int slot, float scale, uint32_t epoch,
+                                 uint64_t timeout_ns, uint32_t* status, float* out, int accumulate,
+                                 float* sumsq_partials, uint32_t* ticket, float* sumsq_out, int ctas, void* stream);
 NFB_EXPORT int nfb_rs_f32(const uint64_t* bases, int rank, int world, int64_t shard, int64_t send_off,
                           int64_t flag_off, int slot, float scale, uint32_t epoch, uint64_t timeout_ns,
                           uint32_t* status, float* out, float* sumsq_partials, uint32_t* ticket, float* sumsq_out,

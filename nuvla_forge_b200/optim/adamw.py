@@ -70,7 +70,14 @@ class FlatAdamW:
             return
         clip = self.max_grad_norm is not None and self.max_grad_norm > 0
         if clip:
-            self.compute_norm2()
+            take = getattr(owner, "take_norm2", None) if owner is not None else None
+            if take is not None and take():
+                # the reduce-scatters already summed this rank's squared gradient shard (clip phase 1);
+                # only the sum over ranks remains
+                if self.norm_allreduce is not None:
+                    self.norm_allreduce(self.norm2)
+            else:
+                self.compute_norm2()
         b1, b2 = self.betas
         if self.native:
             import ctypes

@@ -55,6 +55,7 @@ from __future__ import annotations
 
 import contextlib
 import ctypes
+import os
 from dataclasses import dataclass, field
 
 import torch
@@ -160,6 +161,14 @@ class FullyShardedDataParallel(nn.Module):
         self.fuse_rs_adamw = bool(fuse_rs_adamw and comm in ("fused", "gloo"))
         self._opt = None
         self._fused_updates = 0
+        # clip phase 1 inside the reduce-scatters: per-CTA partials and the last-CTA ticket
+        self._norm_units = 0
+        self.norm_fused_steps = 0      # optimizer steps whose norm^2 came out of the reduce-scatters
+        self.fuse_rs_norm = os.environ.get("NFB_FSDP_RS_NORM", "1") != "0"
+        self._ss_partials = self._ss_ticket = None
+        if comm == "fused":
+            self._ss_partials = torch.zeros(256, dtype=torch.float32, device=dev)
+            self._ss_ticket = torch.zeros(1, dtype=torch.int32, device=dev)
         # Set by the caller (the Trainer does) when the coming backward is the last one before the
         # optimizer step: only then may AdamW run inside the reduce-scatter (with gradient
         # accumulation over several syncing backwards it would update on a partial gradient).
@@ -562,10 +571,24 @@ class FullyShardedDataParallel(nn.Module):
             # on the communication stream, after the unit's gradients are complete on the compute stream
             cs = self.comm_stream
             cs.wait_stream(torch.cuda.current_stream(self.device))
-            # one kernel: bf16 cast of the fp32 accumulator, pushed to the slice owners, reduced into the shard
-            nat.call("nfb_rs_push", ws.bases_ptr(), ws.rank, ws.world, nat.ptr(u.acc32), u.numel, u.grad_off,
-                     ws.flag_off, SLOT_RS, scale, ws.next_epoch(SLOT_RS), ws.timeout_ns, nat.ptr(ws.status),
-                     nat.ptr(out), int(not self._shard_fresh), self.ctas, ctypes.c_void_p(cs.cuda_stream))
+            hs = ctypes.c_void_p(cs.cuda_stream)
+            if self._rs_norm_active():
+                # clip phase 1 fused into the reduce-scatter: each unit's kernel adds its shard's sum of
+                # squares into the optimizer's norm^2 (zeroed on this stream before the first unit)
+                opt = self._opt
+                if self._norm_units == 0:
+                    with torch.cuda.stream(cs):
+                        opt.norm2.zero_()
+                nat.call("nfb_rs_push_sumsq", ws.bases_ptr(), ws.rank, ws.world, nat.ptr(u.acc32), u.numel,
+                         u.grad_off, ws.flag_off, SLOT_RS, scale, ws.next_epoch(SLOT_RS), ws.timeout_ns,
+                         nat.ptr(ws.status), nat.ptr(out), 0, nat.ptr(self._ss_partials), nat.ptr(self._ss_ticket),
+                         nat.ptr(opt.norm2), self.ctas, hs)
+                self._norm_units += 1
+            else:
+                # one kernel: bf16 cast of the fp32 accumulator, pushed to the slice owners, reduced into the shard
+                nat.call("nfb_rs_push", ws.bases_ptr(), ws.rank, ws.world, nat.ptr(u.acc32), u.numel, u.grad_off,
+                         ws.flag_off, SLOT_RS, scale, ws.next_epoch(SLOT_RS), ws.timeout_ns, nat.ptr(ws.status),
+                         nat.ptr(out), int(not self._shard_fresh), self.ctas, hs)
         elif self.comm == "nccl":
             red = torch.empty(u.shard, dtype=torch.bfloat16, device=self.device)
             dist.reduce_scatter_tensor(red, u.acc32.to(torch.bfloat16), group=self.group)
@@ -664,6 +687,23 @@ class FullyShardedDataParallel(nn.Module):
         self._opt = opt
         opt.fused_owner = self
         return opt
+
+    def _rs_norm_active(self) -> bool:
+        """The reduce-scatters of this backward produce each shard's final gradient exactly once, with
+        clipping on: their kernels can accumulate the global norm's sum of squares."""
+        opt = self._opt
+        return (opt is not None and self.require_sync and self.final_backward and self._shard_fresh
+                and opt.max_grad_norm is not None and opt.max_grad_norm > 0 and self._ss_partials is not None
+                and self.fuse_rs_norm)
+
+    def take_norm2(self) -> bool:
+        """True when every unit's reduce-scatter added its shard's sum of squares to the optimizer's norm^2
+        this window (the optimizer then only sums it over ranks)."""
+        n, self._norm_units = self._norm_units, 0
+        if n == len(self.units):
+            self.norm_fused_steps += 1
+            return True
+        return False
 
     def _rs_adamw_active(self) -> bool:
         opt = self._opt

@@ -238,7 +238,7 @@ def _fsdp_model(rank, world, fuse, fuse_rs=True, clip=1.0):
     fsdp = FullyShardedDataParallel(model, comm="fused", fuse_ag_gemm=fuse, fuse_rs_adamw=fuse_rs)
     opt = fsdp.make_optimizer(lr=1e-3, max_grad_norm=clip)
     src = SyntheticBatchSource(SampleSpec.for_model(cfg), 2, seed=rank, pin=False)
-    losses = []
+    losses, norms = [], []
     for step in range(3):
         for m in range(2):
             b = {k: v.to(dev) for k, v in src.batch(2 * step + m).items()}
@@ -250,13 +250,15 @@ def _fsdp_model(rank, world, fuse, fuse_rs=True, clip=1.0):
                 (out["loss"] / 2).backward()
             losses.append(float(out["loss"].detach()))
         opt.step()
+        norms.append(float(opt.grad_norm()))
         opt.zero_grad()
     torch.cuda.synchronize(dev)
     fsdp.check_health()
     views = fsdp.full_master_views()
     params = {n: views[id(p)].cpu() for n, p in model.named_parameters()} if rank == 0 else None
-    return {"losses": losses, "fused_launches": fsdp.ag_fused_launches, "params": params,
-            "streams": fsdp.comm_stream is not None, "fused_steps": fsdp.fused_steps}
+    return {"losses": losses, "fused_launches": fsdp.ag_fused_launches, "params": params, "norms": norms,
+            "streams": fsdp.comm_stream is not None, "fused_steps": fsdp.fused_steps,
+            "norm_fused_steps": fsdp.norm_fused_steps}
 
 
 def test_fsdp_ag_gemm_matches_plain_gather():
@@ -273,6 +275,20 @@ def test_fsdp_ag_gemm_matches_plain_gather():
     for n, t in b[0][1]["params"].items():
         rel = float((a[0][1]["params"][n] - t).norm() / (t.norm() + 1e-8))
         assert rel < 2e-2, (n, rel)
+
+
+def test_fsdp_clip_norm_from_reduce_scatter_matches_optimizer_pass():
+    """Clipping on: the norm^2 summed inside the reduce-scatters equals the optimizer's own pass."""
+    w = _world()
+    a = run_ranks(_fsdp_model, w, args=(True, True, 1.0), backend="nccl", env=ENV, timeout_s=240, join_s=400)
+    b = run_ranks(_fsdp_model, w, args=(True, True, 1.0), backend="nccl", env={**ENV, "NFB_FSDP_RS_NORM": "0"},
+                  timeout_s=240, join_s=400)
+    assert all(st == "ok" for st, _ in a.values()) and all(st == "ok" for st, _ in b.values()), (a, b)
+    assert a[0][1]["norm_fused_steps"] == 3 and b[0][1]["norm_fused_steps"] == 0
+    for na, nb in zip(a[0][1]["norms"], b[0][1]["norms"]):
+        assert abs(na - nb) < 1e-3 * max(1.0, nb), (na, nb)
+    for la, lb in zip(a[0][1]["losses"], b[0][1]["losses"]):
+        assert abs(la - lb) < 1e-2 * max(1.0, abs(lb)), (la, lb)
 
 
 def test_fsdp_rs_adamw_matches_unfused():
