@@ -123,6 +123,19 @@ def gemm_pair_wgrad(iters):
 
 
 @case
+def attn_bwd(iters):
+    """Native attention backward at the ViT shape, 24 images: q, k, v, o, do [24, 1024, 16, 64] bf16."""
+    from ..ops import flash_attn
+    B, S, H, D = 24, 1024, 16, 64
+    qkv = _bf(B, S, 3 * H, D)
+    q, k, v = qkv.split([H, H, H], dim=2)
+    out, lse = flash_attn.attention_fwd(q, k, v)
+    dout = _bf(B, S, H, D, seed=1)
+    for _ in range(iters):
+        flash_attn.attention_bwd(q, k, v, out, dout, lse)
+
+
+@case
 def ce_tc(iters):
     """Cross entropy on tcgen05 at BASELINE config 2: hidden [16384, 2048], W [32000, 2048]."""
     from ..ops.ce_tc import cross_entropy_tc

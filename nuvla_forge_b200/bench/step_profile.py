@@ -55,15 +55,21 @@ def main(argv=None):
     for _ in range(2):
         tr.step(batch)
     torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        e0.record()
         tr.step(batch)
+        e1.record()
         torch.cuda.synchronize()
+    elapsed_ms = e0.elapsed_time(e1)
     rows = sorted((e for e in prof.key_averages() if e.device_time_total > 0), key=lambda e: -e.device_time_total)
     total = sum(e.device_time_total for e in rows)
     cats: dict[str, float] = {}
     for e in rows:
         cats[category(e.key)] = cats.get(category(e.key), 0.0) + e.device_time_total
-    print(f"model {args.model_config}, micro-batch {args.batch_size}: total device time {total / 1e3:.1f} ms")
+    print(f"model {args.model_config}, micro-batch {args.batch_size}: total device time {total / 1e3:.1f} ms "
+          f"in {elapsed_ms:.1f} ms elapsed (kernels busy {100 * total / 1e3 / elapsed_ms:.1f}% of the step; "
+          f"below 100% = the GPU waited on the host or on dependencies)")
     for c, v in sorted(cats.items(), key=lambda kv: -kv[1]):
         print(f"  {c:10s} {v / 1e3:9.2f} ms  {100 * v / total:5.1f}%")
     for e in rows[: args.top]:

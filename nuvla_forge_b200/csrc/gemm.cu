@@ -253,15 +253,16 @@ NFB_API int nfb_gemm_swiglu_bwd(const void* dY, const void* Wd, const void* ab, 
   if (M <= 0) return 0;
   if (D <= 0 || F <= 0 || F % 128) return gemm_fail((int)cudaErrorInvalidValue, "swiglu: F must be a multiple of 128");
   if (!al16(ab) || (ldab * 2) % 16) return gemm_fail((int)cudaErrorInvalidValue, "swiglu: ab rows not 16-byte aligned");
-  CUtensorMap tdab;
+  CUtensorMap tdab, tab;
   int rc = output_map(&tdab, dab, M, 2 * F, lddab);
   if (rc) return gemm_fail(rc, "tensor map of d_ab");
+  rc = output_map(&tab, ab, M, 2 * F, ldab);        // the same 32 x 32 boxes, read by TMA loads
+  if (rc) return gemm_fail(rc, "tensor map of ab");
   SwiGluBwdEpi epi;
-  epi.ab = reinterpret_cast<const __nv_bfloat16*>(ab);
-  epi.ldab = ldab;
-  epi.chunk = 0;
+  epi.loads = 0;
+  epi.inited = 0;
   return launch<SwiGluBwdEpi, false, true>(dY, ldy, Wd, ldw, make_work(M, F, D), epi, status, (cudaStream_t)stream,
-                                           &tdab);
+                                           &tdab, &tab);
 }
 
 // Split count nfb_gemm_acc picks for this shape when given splits = 0 (for callers sizing flags).

@@ -80,16 +80,19 @@ struct alignas(8) Shared {
   uint64_t tmem_full[2];      // every CTA: an accumulator is complete
   uint64_t tmem_empty[2];     // leader: the 8 epilogue warps of the pair read an accumulator
   uint64_t mma_drain;
+  uint64_t epi_bar[4][2];     // per epilogue warp: TMA loads into its staging buffers (epilogues that read)
   uint32_t tmem_base;
   int abort;
 };
 
 constexpr size_t kSharedSlot = 1024;
 static_assert(sizeof(Shared) <= kSharedSlot, "Shared must fit its slot");
-// Epilogue staging: per epilogue warp two 32-row x 64-byte buffers (32 bf16 columns), written
-// with the 64-byte swizzle and drained by TMA stores.
+// Epilogue staging: per epilogue warp four 32-row x 64-byte buffers (32 bf16 columns each), in the
+// 64-byte swizzle of the TMA boxes; stores use two of them alternately, an epilogue that also reads
+// a tensor (SwiGLU backward) uses all four as two (gate, up) sets.
 constexpr int kEpiBufBytes = 32 * 64;
-constexpr size_t kEpiSmem = 4 * 2 * kEpiBufBytes;
+constexpr int kEpiWarpBufs = 4;
+constexpr size_t kEpiSmem = 4 * kEpiWarpBufs * kEpiBufBytes;
 constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + kSharedSlot + kEpiSmem + 1024;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
@@ -159,6 +162,15 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 // Wait until at most one of this thread's bulk groups still reads shared memory.
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Wait until none of this thread's bulk groups still reads shared memory.
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// 2-D TMA load of one box into this CTA's shared memory, completion on an mbarrier of this CTA.
+__device__ __forceinline__ void tma_load_box(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 struct Work {
@@ -201,7 +213,8 @@ struct EpiCtx {
   int lane;
   uint8_t* smem;            // this warp's two staging buffers (1024-byte aligned)
   const CUtensorMap* tmap_c; // output tensor map (bf16 [M, N], 32 x 32 boxes, 64-byte swizzle) or null
-  const CUtensorMap* tmap_d; // second output map of the same kind (epilogues with two outputs) or null
+  const CUtensorMap* tmap_d; // second map of the same kind (a second output, or an input read by TMA) or null
+  uint64_t* bar;             // this warp's two mbarriers for TMA loads into its staging buffers
 };
 
 // Epi must provide: __device__ bool warp(const EpiCtx&, const Work&, volatile int* abort, uint32_t* status)
@@ -350,7 +363,8 @@ __device__ void gemm_pair_body(const CUtensorMap* tma_a, const CUtensorMap* tma_
     const uint32_t empty_leader1 = map_to(smem_u32(&S->tmem_empty[1]), 0);
     EpiCtx c;
     c.lane = lane;
-    c.smem = reinterpret_cast<uint8_t*>(S) + kSharedSlot + (size_t)quarter * 2 * kEpiBufBytes;
+    c.smem = reinterpret_cast<uint8_t*>(S) + kSharedSlot + (size_t)quarter * kEpiWarpBufs * kEpiBufBytes;
+    c.bar = S->epi_bar[quarter];
     c.tmap_c = tma_c;
     c.tmap_d = tma_d;
     for (int it = cluster; it < w.items; it += n_clusters) {
@@ -644,48 +658,89 @@ struct SwiGluFwdEpi {
 };
 
 // SwiGLU backward fused into the down projection's input gradient: the accumulator tile is
-// d_act[m, j] for 256 hidden units j; the epilogue reads the stored pre-activations (gate, up)
-// of those units from the interleaved ab [M, 2F] and stores
+// d_act[m, j] for 256 hidden units j; the epilogue loads the stored pre-activations (gate, up) of
+// those units from the interleaved ab [M, 2F] with TMA boxes (second map) into the warp's staging
+// buffers -- the next chunk's boxes are in flight while this one is computed -- and stores
 //   d_gate = d_act * up * s * (1 + gate (1 - s)),  d_up = d_act * gate * s,  s = sigmoid(gate)
-// into d_ab (same interleaved layout) through the output map, so d_act never reaches memory.
+// in place, then TMA-stores both boxes into d_ab (same interleaved layout, first map), so d_act
+// never reaches memory and every global access is a full-line TMA transfer.
 struct SwiGluBwdEpi {
-  const __nv_bfloat16* ab;
-  int64_t ldab;
-  uint32_t chunk;
+  uint32_t loads;     // chunks whose boxes this warp requested (set = loads & 1)
+  uint32_t inited;
 
-  __device__ bool warp(const EpiCtx& c, const Work& w, volatile int*, uint32_t*) {
-    const int m = c.row0 + c.lane;
-    const bool live = m < w.M;
+  __device__ __forceinline__ void issue(const EpiCtx& c, int j, uint32_t set) {
+    // lane 0 only: the set's buffers were last read by stores of two chunks ago -> wait for them
+    bulk_wait_read0();
+    const int gcol = 256 * (j >> 7) + (j & 127);
+    uint8_t* gb = c.smem + (2 * set) * kEpiBufBytes;
+    uint8_t* ub = gb + kEpiBufBytes;
+    mbar_arrive_expect_tx(&c.bar[set], 2 * kEpiBufBytes);
+    tma_load_box(gb, c.tmap_d, &c.bar[set], gcol, c.row0);
+    tma_load_box(ub, c.tmap_d, &c.bar[set], gcol + 128, c.row0);
+  }
+
+  __device__ bool warp(const EpiCtx& c, const Work& w, volatile int* abort_flag, uint32_t* status) {
+    if (!inited) {
+      if (c.lane == 0) {
+        mbar_init(&c.bar[0], 1);
+        mbar_init(&c.bar[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      }
+      __syncwarp();
+      inited = 1;
+    }
+    const bool tile_live = c.row0 < w.M;
+    int nch = 0;                                    // live 32-column chunks of this tile
+    if (tile_live) nch = (w.N - c.n0 + 31) / 32 < TN / 32 ? (w.N - c.n0 + 31) / 32 : TN / 32;
+    if (nch > 0 && c.lane == 0) issue(c, c.n0, loads & 1u);
+    bool ok = true;
 #pragma unroll 1
     for (int cc = 0; cc < TN; cc += 32) {
       float d[32];
       tmem_ld32(c.taddr + cc, d);
-      const int j = c.n0 + cc;
-      if (c.row0 >= w.M || j >= w.N) continue;
-      const int gcol = 256 * (j >> 7) + (j & 127);
-      float g[32], u[32];
-      if (live) {
-        const __nv_bfloat16* gr = ab + (int64_t)m * ldab + gcol;
+      const int k = cc / 32;
+      if (k >= nch) continue;                       // warp-uniform
+      const uint32_t set = (loads + (uint32_t)k) & 1u;
+      if (k + 1 < nch && c.lane == 0) issue(c, c.n0 + cc + 32, set ^ 1u);
+      bool got = mbar_wait_sleep(&c.bar[set], ((loads + (uint32_t)k) >> 1) & 1u, abort_flag);
+      got = __all_sync(0xffffffffu, got);
+      if (!got) {
+        if (c.lane == 0) set_status(status, kTimeoutFlag, 220);
+        ok = false;
+        break;
+      }
+      uint8_t* gb = c.smem + (2 * set) * kEpiBufBytes;
+      uint8_t* ub = gb + kEpiBufBytes;
+      const int r = c.lane;
 #pragma unroll
-        for (int e = 0; e < 32; e += 8) {
-          load16<__nv_bfloat16>(gr + e, g + e);
-          load16<__nv_bfloat16>(gr + 128 + e, u + e);
+      for (int q = 0; q < 4; ++q) {
+        const int off = r * 64 + ((q ^ ((r >> 1) & 3)) << 4);   // 64-byte swizzle of the TMA box
+        float g[8], u[8];
+        load16<__nv_bfloat16>(reinterpret_cast<const __nv_bfloat16*>(gb + off), g);
+        load16<__nv_bfloat16>(reinterpret_cast<const __nv_bfloat16*>(ub + off), u);
+        float dg[8], du[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float sg = sigmoidf_fast(g[e]);
+          const float dd = d[8 * q + e];
+          du[e] = dd * g[e] * sg;
+          dg[e] = dd * u[e] * sg * (1.f + g[e] * (1.f - sg));
         }
-      } else {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) { g[e] = 0.f; u[e] = 0.f; }
+        store16<__nv_bfloat16>(reinterpret_cast<__nv_bfloat16*>(gb + off), dg);
+        store16<__nv_bfloat16>(reinterpret_cast<__nv_bfloat16*>(ub + off), du);
       }
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const float sg = sigmoidf_fast(g[e]);
-        const float du = d[e] * g[e] * sg;
-        d[e] = d[e] * u[e] * sg * (1.f + g[e] * (1.f - sg));
-        u[e] = du;
+      fence_async_smem();
+      __syncwarp();
+      if (c.lane == 0) {
+        const int j = c.n0 + cc;
+        const int gcol = 256 * (j >> 7) + (j & 127);
+        tma_store_2d(c.tmap_c, gb, gcol, c.row0);
+        tma_store_2d(c.tmap_c, ub, gcol + 128, c.row0);
+        bulk_commit();
       }
-      stage_store(c, chunk, d, c.tmap_c, gcol, c.row0);
-      stage_store(c, chunk, u, c.tmap_c, gcol + 128, c.row0);
     }
-    return true;
+    loads += (uint32_t)nch;
+    return ok;
   }
 
   __device__ void finish(const EpiCtx& c) {
