@@ -52,7 +52,7 @@ def _time(fn, iters, flush):
 
 
 def sustained(seconds: float, out_path: str | None) -> None:
-    """Back-to-back GEMMs for ``seconds`` per implementation, with SM clock and power sampled:
+    """Back-to-back GEMMs for ``seconds`` per implementation and role, with SM clock and power sampled:
     under the 1 kW cap the sustained rate depends on energy per FLOP, not only on burst speed."""
     import sys
     sys.path.insert(0, str(Path(__file__).resolve().parents[2]))
@@ -61,32 +61,44 @@ def sustained(seconds: float, out_path: str | None) -> None:
     from ..ops import linear as L
 
     rows = []
-    for name, M, N, K in (SHAPES[0], SHAPES[1]):
+    for name, M, N, K in (SHAPES[0], SHAPES[1], SHAPES[3]):
         g = torch.Generator(device="cuda").manual_seed(0)
         x = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
         w = torch.randn(N, K, generator=g, device="cuda").to(torch.bfloat16)
+        dy = torch.randn(M, N, generator=g, device="cuda").to(torch.bfloat16)
         y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
-        for impl, fn in (("native", lambda: L.gemm(x, w, out=y)), ("cublas", lambda: torch.mm(x, w.t(), out=y))):
-            for _ in range(5):
-                fn()
-            torch.cuda.synchronize()
-            one = _time(fn, 3, torch.empty(1, device="cuda"))
-            n = max(1, int(seconds * 1e3 / one))
-            smp = ClockSampler(visible_gpu_ids())
-            smp.start()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for _ in range(n):
-                fn()
-            e1.record()
-            torch.cuda.synchronize()
-            clk = smp.stop()
-            ms = e0.elapsed_time(e1) / n
-            row = {"shape": name, "impl": impl, "iters": n, "ms": ms, "tflops": 2.0 * M * N * K / ms / 1e9,
-                   "clocks": clk}
-            rows.append(row)
-            print(f"sustained {name:14s} {impl:6s} {row['tflops']:7.1f} TF/s  sm {clk.get('sm_mhz')} MHz "
-                  f"power {clk.get('power_w')} W  {clk.get('reasons')}", flush=True)
+        dx = torch.empty(M, K, dtype=torch.bfloat16, device="cuda")
+        dw = torch.zeros(N, K, dtype=torch.float32, device="cuda")
+        dwb = torch.empty(N, K, dtype=torch.bfloat16, device="cuda")
+        roles = [("fwd", lambda: L.gemm(x, w, out=y), lambda: torch.mm(x, w.t(), out=y)),
+                 ("dgrad", lambda: L.gemm(dy, w, b_mn=True, out=dx), lambda: torch.mm(dy, w, out=dx)),
+                 ("wgrad", lambda: L.gemm_acc(dy, x, dw, a_mn=True, b_mn=True, accumulate=True),
+                  lambda: torch.mm(dy.t(), x, out=dwb))]
+        for role, nat_fn, ref_fn in roles:
+            for impl, fn in (("native", nat_fn), ("cublas", ref_fn)):
+                for _ in range(5):
+                    fn()
+                torch.cuda.synchronize()
+                one = _time(fn, 3, torch.empty(1, device="cuda"))
+                n = max(1, int(seconds * 1e3 / one))
+                smp = ClockSampler(visible_gpu_ids())
+                smp.start()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(n):
+                    fn()
+                e1.record()
+                torch.cuda.synchronize()
+                clk = smp.stop()
+                ms = e0.elapsed_time(e1) / n
+                tf = 2.0 * M * N * K / ms / 1e9
+                row = {"shape": name, "role": role, "impl": impl, "iters": n, "ms": ms, "tflops": tf, "clocks": clk,
+                       "pj_per_flop": (clk.get("power_w") or 0) / (tf * 1e12) * 1e12 if tf else None}
+                rows.append(row)
+                print(f"sustained {name:14s} {role:6s} {impl:6s} {tf:7.1f} TF/s  sm {clk.get('sm_mhz')} MHz "
+                      f"power {clk.get('power_w')} W  {row['pj_per_flop']:.3f} pJ/FLOP", flush=True)
+        del x, w, dy, y, dx, dw, dwb
+        torch.cuda.empty_cache()
     if out_path:
         Path(out_path).write_text(json.dumps({"sustained_s": seconds, "rows": rows}, indent=1))
 

@@ -198,6 +198,12 @@ class SwiGLUMLP(nn.Module):
         if self.fused and self.interleaved and _pending_consumer is None and \
                 linear_op.swiglu_supported(x, w, self.w_down.weight):
             return linear_op.swiglu_mlp(x, w, self.w_down.weight, residual)
+        if self.interleaved and x.is_cuda and self.fused:
+            # library-GEMM path (A/B runs, unsupported shapes): one GEMM over the [gate; up] row order
+            # (a cheap weight permutation), then the packed SwiGLU kernel
+            g, u = linear_op.split_gate_up_rows(w)
+            act = swiglu_packed(linear(x, torch.cat([g, u], dim=0)))
+            return _linear(act, self.w_down.weight, residual=residual)
         ab = linear(x, w)
         if self.interleaved:
             a, b = linear_op.split_gate_up_cols(ab)
