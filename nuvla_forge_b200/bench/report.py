@@ -71,10 +71,11 @@ def section_comms(lines, reports: Path):
     for p in found:
         c = json.loads(p.read_text())
         lines += [f"### {p.name}: world {c['world_size']}, NCCL {c.get('nccl_version')}", "",
-                  "| bytes | AR fused | AR NCCL bf16 | AR NCCL fp32 | RS fused | RS NCCL | AG fused | AG NCCL |",
-                  "|---|---|---|---|---|---|---|---|"]
+                  "| bytes | AR fused | AR pipelined | AR NCCL bf16 | AR NCCL fp32 | RS fused | RS NCCL | AG fused | AG NCCL |",
+                  "|---|---|---|---|---|---|---|---|---|"]
         for r in c["rows"]:
-            lines.append(f"| {r['bytes']} | {fmt(r['ar_fused_busbw'], '.1f')} | {fmt(r['ar_nccl_bf16_busbw'], '.1f')} | "
+            lines.append(f"| {r['bytes']} | {fmt(r['ar_fused_busbw'], '.1f')} | "
+                         f"{fmt(r.get('ar_fused_pipelined_busbw'), '.1f')} | {fmt(r['ar_nccl_bf16_busbw'], '.1f')} | "
                          f"{fmt(r['ar_nccl_fp32_busbw'], '.1f')} | {fmt(r['rs_fused_busbw'], '.1f')} | "
                          f"{fmt(r['rs_nccl_busbw'], '.1f')} | {fmt(r['ag_fused_busbw'], '.1f')} | "
                          f"{fmt(r['ag_nccl_busbw'], '.1f')} |")
@@ -116,15 +117,43 @@ def section_ag_gemm(lines, reports: Path):
 
 
 def section_attention(lines, d):
-    lines += ["## Attention forward (tcgen05 kernel vs PyTorch SDPA / cuDNN)", ""]
+    lines += ["## Attention forward and backward (tcgen05 kernels vs PyTorch SDPA / cuDNN)", ""]
     if not d:
         lines += ["_Not run._", ""]
         return
-    lines += ["| shape | native ms | native TFLOP/s | SDPA ms | SDPA TFLOP/s |", "|---|---|---|---|---|"]
+    lines += ["| shape | fwd native ms (TFLOP/s) | fwd SDPA ms (TFLOP/s) | bwd native ms (TFLOP/s) | "
+              "bwd SDPA ms (TFLOP/s) |", "|---|---|---|---|---|"]
     for r in d["rows"]:
-        lines.append(f"| {r['shape']} | {fmt(r['native_ms'], '.3f')} | {fmt(r['native_tflops'], '.0f')} | "
-                     f"{fmt(r['sdpa_ms'], '.3f')} | {fmt(r['sdpa_tflops'], '.0f')} |")
+        lines.append(f"| {r['shape']} | {fmt(r['native_ms'], '.3f')} ({fmt(r['native_tflops'], '.0f')}) | "
+                     f"{fmt(r['sdpa_ms'], '.3f')} ({fmt(r['sdpa_tflops'], '.0f')}) | "
+                     f"{fmt(r.get('native_bwd_ms'), '.3f')} ({fmt(r.get('native_bwd_tflops'), '.0f')}) | "
+                     f"{fmt(r.get('sdpa_bwd_ms'), '.3f')} ({fmt(r.get('sdpa_bwd_tflops'), '.0f')}) |")
     lines.append("")
+
+
+def section_gemm(lines, d, sus):
+    lines += ["## Linear-layer GEMMs (CTA-pair tcgen05 kernel vs cuBLAS)", ""]
+    if not d:
+        lines += ["_Not run._", ""]
+    else:
+        pk = (d.get("measured_peaks") or {}).get("bf16_tflops")
+        lines += [f"Burst, L2 flushed between iterations; measured cuBLAS bf16 peak {fmt(pk, '.0f')} TFLOP/s.", "",
+                  "| shape (M x N x K) | role | native ms | native TFLOP/s | cuBLAS ms | cuBLAS TFLOP/s | speed-up |",
+                  "|---|---|---|---|---|---|---|"]
+        for r in d["rows"]:
+            lines.append(f"| {r['shape']} {r['M']}x{r['N']}x{r['K']} | {r['role']} | {fmt(r['native_ms'], '.3f')} | "
+                         f"{fmt(r['native_tflops'], '.0f')} | {fmt(r['cublas_ms'], '.3f')} | "
+                         f"{fmt(r['cublas_tflops'], '.0f')} | {fmt(r['speedup'], '.3f')}x |")
+        lines.append("")
+    if sus:
+        lines += [f"Sustained ({sus['sustained_s']} s back to back per case, under the 1 kW power cap):", "",
+                  "| shape | role | impl | TFLOP/s | SM MHz | W | pJ/FLOP |", "|---|---|---|---|---|---|---|"]
+        for r in sus["rows"]:
+            c = r.get("clocks") or {}
+            lines.append(f"| {r['shape']} | {r.get('role', 'fwd')} | {r['impl']} | {fmt(r['tflops'], '.0f')} | "
+                         f"{fmt(c.get('sm_mhz'), '.0f')} | {fmt(c.get('power_w'), '.0f')} | "
+                         f"{fmt(r.get('pj_per_flop'), '.3f')} |")
+        lines.append("")
 
 
 def section_planner(lines, d):
@@ -164,6 +193,7 @@ def main(argv=None):
     section_kernels(lines, _load(d, "kernels.json"))
     section_comms(lines, d)
     section_ag_gemm(lines, d)
+    section_gemm(lines, _load(d, "gemm.json"), _load(d, "gemm_sustained.json"))
     section_attention(lines, _load(d, "attention.json"))
     section_planner(lines, _load(d, "planner.json"))
     section_loader(lines, _load(d, "dataloader.json"))
