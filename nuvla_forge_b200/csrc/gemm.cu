@@ -123,6 +123,22 @@ static int operand_map(CUtensorMap* m, const void* p, int rows, int K, int64_t l
   return mn ? tc::make_tmap(m, p, K, rows, ld, BK) : tc::make_tmap(m, p, rows, K, ld, HALF);
 }
 
+// fp32 map for the accumulating epilogue: [M, N] with row stride ldc, 32 x 32 boxes, 128-byte swizzle.
+static int output_map_f32(CUtensorMap* m, const void* C, int M, int N, int64_t ldc) {
+  int rc = tc::get_encode();
+  if (rc) return rc;
+  rc = tc::bind_device_of(C);
+  if (rc) return rc;
+  cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+  cuuint64_t strides[1] = {(cuuint64_t)(ldc * 4)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = tc::g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(C), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
+}
+
 // Output map for the staged epilogue: bf16 [M, N] with row stride ldc, 32 x 32 boxes, 64-byte swizzle.
 static int output_map(CUtensorMap* m, const void* C, int M, int N, int64_t ldc) {
   int rc = tc::get_encode();
@@ -225,7 +241,11 @@ NFB_API int nfb_gemm_acc(const void* A, const void* B, float* C, int M, int N, i
   epi.vec_ok = al16(C) && (ldc * 4) % 16 == 0;
   epi.flags = flags;
   epi.epoch = epoch & 0xFFFFFFu;
-  return dispatch(A, lda, B, ldb, w, epi, a_mn, b_mn, status, (cudaStream_t)stream);
+  epi.chunk = 0;
+  epi.use_tma = 0;
+  CUtensorMap tcm;
+  if (epi.vec_ok && N % 4 == 0 && output_map_f32(&tcm, C, M, N, ldc) == 0) epi.use_tma = 1;
+  return dispatch(A, lda, B, ldb, w, epi, a_mn, b_mn, status, (cudaStream_t)stream, epi.use_tma ? &tcm : nullptr);
 }
 
 // act [M, F] = silu(gate) * up with (gate | up) = X W^T, W [2F, K] interleaved in 128-row blocks

@@ -159,6 +159,11 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
                ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(x), "r"(y) : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// 2-D TMA reduction: global box (x, y) += shared-memory box (element-wise f32 add in L2).
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(x), "r"(y) : "memory");
+}
 // Wait until at most one of this thread's bulk groups still reads shared memory.
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
@@ -547,13 +552,20 @@ struct LinearEpi {
 // fp32 C = acc (overwrite) or C += acc (accumulate), with ordered split-K: split 0 writes (or
 // adds to the caller's C), split j > 0 waits for split j-1 of the same rows and adds.
 // flags: one 32-bit word per (tile, warp slot); a value (epoch << 8) | j means "splits < j done".
+// With an fp32 tensor map (tmap_c: 32 x 32 boxes, 128-byte swizzle) each 32-column chunk is staged
+// in shared memory and written by one TMA store, or added into C by one TMA reduction (the L2
+// performs the read-add-write on full lines); a split releases its flag only after its
+// reductions have completed, so the additions into C happen in split order (deterministic).
+// Without a map (unaligned C) every thread reads and writes its own row.
 struct AccumF32Epi {
   float* C;
   int64_t ldc;
   int accumulate;
   int vec_ok;
+  int use_tma;
   uint32_t* flags;
   uint32_t epoch;
+  uint32_t chunk;
 
   __device__ bool warp(const EpiCtx& c, const Work& w, volatile int* abort_flag, uint32_t* status) {
     const int m = c.row0 + c.lane;
@@ -570,6 +582,7 @@ struct AccumF32Epi {
           if ((++spins & 63u) == 0 && (*abort_flag || globaltimer_ns() - t0 > kWaitNs)) { ok = false; break; }
         }
         if (!ok) set_status(status, kTimeoutFlag, 210);
+        asm volatile("fence.proxy.async.global;" ::: "memory");   // the previous split's adds precede ours
       }
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       __syncwarp();
@@ -580,6 +593,28 @@ struct AccumF32Epi {
       float v[32];
       tmem_ld32(c.taddr + cc, v);
       const int n = c.n0 + cc;
+      if (use_tma) {
+        if (!ok || c.row0 >= w.M || n >= w.N) continue;           // warp-uniform
+        uint8_t* buf = c.smem + (chunk & 1u) * 2 * kEpiBufBytes;   // 32 rows x 128 bytes
+        if (chunk >= 2) {
+          if (c.lane == 0) bulk_wait_read1();
+          __syncwarp();
+        }
+        const int r = c.lane;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          *reinterpret_cast<float4*>(buf + r * 128 + ((q ^ (r & 7)) << 4)) =
+              make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        fence_async_smem();
+        __syncwarp();
+        if (c.lane == 0) {
+          if (add) tma_reduce_add_2d(c.tmap_c, buf, n, c.row0);
+          else tma_store_2d(c.tmap_c, buf, n, c.row0);
+          bulk_commit();
+        }
+        ++chunk;
+        continue;
+      }
       if (!ok || !live || n >= w.N) continue;
       float* dst = C + (int64_t)m * ldc + n;
       if (vec_ok && n + 32 <= w.N) {
@@ -601,6 +636,10 @@ struct AccumF32Epi {
     if (ok && c.split + 1 < c.splits) {
       __syncwarp();
       if (c.lane == 0) {
+        if (use_tma) {
+          bulk_wait_all();                                        // our adds are performed in C
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+        }
         __threadfence();
         asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"((epoch << 8) | (uint32_t)(c.split + 1))
                      : "memory");
@@ -609,7 +648,10 @@ struct AccumF32Epi {
     return ok;
   }
 
-  __device__ void finish(const EpiCtx&) {}
+  __device__ void finish(const EpiCtx& c) {
+    if (use_tma && c.lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
 };
 
 // SwiGLU fused into the gate/up projection. The weight's rows are interleaved in 128-row blocks
