@@ -60,6 +60,7 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default="reports/comms.json")
     ap.add_argument("--max-mb", type=float, default=1024.0)
+    ap.add_argument("--min-mb", type=float, default=0.0, help="skip sizes below this")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--ctas", type=int, default=0, help="CTAs for the fused kernels (0 = by size)")
     ap.add_argument("--chunk", type=int, default=2048, help="pipelined all-reduce: vectors per slice per step")
@@ -71,7 +72,8 @@ def main(argv=None):
     sizes = []
     b = 1024
     while b <= args.max_mb * 2**20:
-        sizes.append(b)
+        if b >= args.min_mb * 2**20:
+            sizes.append(b)
         b *= 4
     maxn = sizes[-1] // 2
     small_cap = 1 << 20   # one-shot all-reduce up to 2 MB of bf16
