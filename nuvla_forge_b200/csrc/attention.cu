@@ -1,30 +1,30 @@
 // Flash attention forward on the 5th-generation tensor cores (sm_100a).
 //
 //   O[b, q, h, :] = softmax(scale * Q[b, q, h, :] . K[b, :, g(h), :]^T) V[b, :, g(h), :]
-//   g(h) = h / (Hq / Hkv)  (grouped-query attention), optional causal mask (kv <= q)
+//   g(h) = h / (Hq / Hkv)  (grouped-query attention), optional causal mask (kv <= q + Sk - Sq)
 //
 // Q, K, V and O are in the projection-native [B, S, H, D] layout (any token and
 // batch strides, rows of D contiguous), D = 64 or 128, bf16; the kernel also
 // writes the row log-sum-exp (natural log) [B, H, Sq] for the backward pass.
 //
-// One CTA per (128-query tile, head, batch); 6 warps with fixed roles:
-//   warp 0      TMA producer: the Q tile once, then K and V tiles of 128 keys
-//               into a two-stage ring (4-D tensor maps over [B, S, H, D]).
-//   warp 1      MMA issuer (one elected lane): S_j = Q K_j^T into one of two
-//               128-column TMEM buffers, then O += P_{j-1} V_{j-1} into a
-//               D-column TMEM accumulator (P from shared memory, K-major; V
-//               read MN-major straight from its TMA tile), so the tensor core
-//               computes S_j while the softmax warps work on S_{j-1}.
-//   warps 2-9   softmax: query row r (TMEM lane r) belongs to two threads, one
-//               in warps 2-5 (key columns 0-63 of each tile, O columns
-//               [0, D/2)) and one in warps 6-9 (the other halves). They read
-//               their scores with tcgen05.ld, exchange the tile maximum through
-//               shared memory, keep the running max / sums in registers (online
-//               softmax in base 2, SFU exp2), rescale their part of the O row in
-//               TMEM (tcgen05.ld/st) only when the max grows by more than 2^8,
-//               and write their bf16 probabilities -- one 64-key block each --
-//               into the 128-byte-swizzled P tile. At the end they normalise
-//               their O columns and store them with the log-sum-exp.
+// One CTA owns two 128-query tiles that read the same K/V: two heads of one
+// GQA group at the same queries when the group size is even, else two
+// consecutive query tiles of one head. 10 warps with fixed roles:
+//   warp 0      TMA producer: both Q tiles once, then K and V tiles of 128 keys
+//               into a ring (4-D tensor maps over [B, S, H, D]).
+//   warp 1      MMA issuer (one elected lane), per tile t and key tile j:
+//               S_t = Q_t K_j^T into a 128-column TMEM buffer, then
+//               O_t += P_t V_j with P_t read from TMEM (the softmax warps
+//               overwrite S_t with the bf16 probabilities) and V_j MN-major
+//               from its TMA tile. The two tiles are issued staggered, so the
+//               tensor core runs one tile's MMAs while the other tile's
+//               softmax warps work.
+//   warps 2-5   softmax of tile 0, warps 6-9 softmax of tile 1: one thread per
+//               query row (TMEM lane), the whole 128-key row of S in registers,
+//               so the row maximum needs no exchange. Online softmax in base 2
+//               (SFU exp2); O_t is rescaled in TMEM only when the row maximum
+//               grows by more than 2^8. At the end each thread normalises its O
+//               row and stores it with the log-sum-exp.
 // Every mbarrier wait is bounded by %globaltimer and reports a status; no
 // cluster, no multicast. Parity: the reference calls
 // F.scaled_dot_product_attention (nuvla_forge/model/dit.py:92).
@@ -36,14 +36,15 @@ namespace attn {
 
 using namespace nfb::tc;
 
-constexpr int BQ = 128;          // queries per CTA (TMEM lanes)
+constexpr int BQ = 128;          // queries per tile (TMEM lanes)
 constexpr int BKV = 128;         // keys per tile
-constexpr int kThreadsA = 320;        // producer, MMA, 8 softmax warps
-constexpr uint32_t kTmemColsA = 512;   // S0 | S1 | O
+constexpr int kThreadsA = 320;   // producer, MMA, 2 x 4 softmax warps
+constexpr uint32_t kTmemColsA = 512;   // S0 | S1 | O0 | O1
 
 struct AttnArgs {
   int B, Sq, Sk, Hq, Hkv, D;
   int causal;
+  int pair_heads;               // 1: the CTA's tiles are heads 2p, 2p+1 at one query tile
   float scale_log2;             // softmax scale * log2(e)
   __nv_bfloat16* o;
   int64_t so_b, so_s, so_h;     // element strides of O
@@ -53,12 +54,11 @@ struct AttnArgs {
 
 struct alignas(8) AttnShared {
   uint64_t q_full;
-  uint64_t kv_full[2];
-  uint64_t kv_empty[2];
+  uint64_t kv_full[4];
+  uint64_t kv_empty[4];
   uint64_t s_full[2];
-  uint64_t p_full;
-  uint64_t pv_done;
-  uint64_t o_full;
+  uint64_t p_full[2];
+  uint64_t pv_done[2];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -73,39 +73,40 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+// 32 consecutive 32-bit TMEM columns of this thread's lane (no wait: the caller issues
+// tcgen05.wait::st before it signals the MMA issuer).
+__device__ __forceinline__ void tmem_st32_nowait(uint32_t taddr, const uint32_t* v) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
       "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n\t"
-      "tcgen05.wait::st.sync.aligned;"
-      ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
-        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
-        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
-        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
-        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
-        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
-        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
-        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
-        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
-        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+      ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+        "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
+        "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
 }
 
-// Named barrier over the 64 threads of one row pair that also ANDs a flag across them, so both
-// warps of a pair always take the same branch (a warp that left alone would strand its partner).
-__device__ __forceinline__ bool pair_all(int id, bool v) {
-  int r;
+__device__ __forceinline__ void tmem_st16_nowait(uint32_t taddr, const uint32_t* v) {
   asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.b32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, %2, 64, p;\n\t"
-      "selp.b32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"((int)v), "r"(id)
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
       : "memory");
-  return r != 0;
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// D (TMEM) (+)= A (TMEM, 128 lanes x 16 bf16 packed two per column) x B (shared memory descriptor).
+__device__ __forceinline__ void umma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
 }
 
 // 2^x with the SFU's approximate base-2 exponential (flushes denormal results to zero).
@@ -120,22 +121,21 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Shared memory: [Q: D/64 x 16 KB][K: 2 stages x D/64 x 16 KB][V: 2 stages x 2 x D/64 x 8 KB][P: 2 x 16 KB][AttnShared]
+// Shared memory: [Q: 2 tiles x D/64 x 16 KB][K/V ring: kStages x (K: D/64 x 16 KB, V: 2 x D/64 x 8 KB)][AttnShared]
 template <int D>
 struct Layout {
   static constexpr int kDB = D / 64;                        // 64-column blocks of the head dim
-  static constexpr int kQBytes = BQ * D * 2;
+  static constexpr int kStages = D == 64 ? 4 : 2;
+  static constexpr int kQBytes = BQ * D * 2;                // one query tile
   static constexpr int kKBytes = BKV * D * 2;
   static constexpr int kVBytes = BKV * D * 2;
-  static constexpr int kPBytes = BQ * BKV * 2;
+  static constexpr int kStageBytes = kKBytes + kVBytes;
   static constexpr int kQ = 0;
-  static constexpr int kK = kQ + kQBytes;
-  static constexpr int kV = kK + 2 * kKBytes;
-  static constexpr int kP = kV + 2 * kVBytes;
-  static constexpr int kS = kP + kPBytes;
-  // + AttnShared slot + alignment; at least 116 KB so that one CTA (and its 512 TMEM columns) owns an SM
-  static constexpr size_t kRaw = (size_t)kS + 128 + 2048 + 1024;   // AttnShared, [2][2][128] fp32 exchange, alignment
-  static constexpr size_t kBytes = kRaw > 116 * 1024 ? kRaw : 116 * 1024;
+  static constexpr int kKV = kQ + 2 * kQBytes;
+  static constexpr int kS = kKV + kStages * kStageBytes;
+  static constexpr size_t kBytes = (size_t)kS + 256 + 1024;   // AttnShared, alignment
+  static_assert(kBytes <= 227 * 1024, "shared memory");
+  static_assert(kBytes > 114 * 1024, "one CTA (and its 512 TMEM columns) per SM");
 };
 
 template <int D>
@@ -143,31 +143,42 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                     const __grid_constant__ CUtensorMap tv, AttnArgs a) {
   using L = Layout<D>;
+  constexpr int NS = L::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   AttnShared* S = reinterpret_cast<AttnShared*>(smem + L::kS);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile int* abort_flag = &S->abort;
-  const int q0 = blockIdx.x * BQ, h = blockIdx.y, b = blockIdx.z;
-  const int hk = h / (a.Hq / a.Hkv);
-  // key tiles this query tile needs
-  int kv_end = a.Sk;
-  if (a.causal) {
-    const int lim = q0 + BQ + (a.Sk - a.Sq);   // keys kv <= q + (Sk - Sq)
-    kv_end = lim < kv_end ? lim : kv_end;
-  }
-  const int n_kv = kv_end > 0 ? (kv_end + BKV - 1) / BKV : 0;
+  // heavier (later) query tiles first when causal
+  const int qt = a.causal ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
+  const int b = blockIdx.z;
+  // tile t (0 or 1): head h_of(t), first query q0_of(t), key tiles n_of(t)
+  auto h_of = [&](int t) { return a.pair_heads ? 2 * (int)blockIdx.y + t : (int)blockIdx.y; };
+  auto q0_of = [&](int t) { return a.pair_heads ? qt * BQ : (2 * qt + t) * BQ; };
+  auto count_kv = [&](int t) {
+    int kv_end = a.Sk;
+    if (a.causal) {
+      const int lim = q0_of(t) + BQ + (a.Sk - a.Sq);   // keys kv <= q + (Sk - Sq)
+      kv_end = lim < kv_end ? lim : kv_end;
+    }
+    return (q0_of(t) < a.Sq && kv_end > 0) ? (kv_end + BKV - 1) / BKV : 0;
+  };
+  const int n0 = count_kv(0), n1 = count_kv(1);
+  auto n_of = [&](int t) { return t ? n1 : n0; };
+  const int hk = h_of(0) / (a.Hq / a.Hkv);
+  const int n_max = n0 > n1 ? n0 : n1;
 
   if (threadIdx.x == 0) {
     mbar_init(&S->q_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < NS; ++s) {
       mbar_init(&S->kv_full[s], 1);
       mbar_init(&S->kv_empty[s], 1);
-      mbar_init(&S->s_full[s], 1);
     }
-    mbar_init(&S->p_full, 256);
-    mbar_init(&S->pv_done, 1);
-    mbar_init(&S->o_full, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&S->s_full[t], 1);
+      mbar_init(&S->p_full[t], BQ);
+      mbar_init(&S->pv_done[t], 1);
+    }
     mbar_init(&S->drain, 1);
     S->abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -185,20 +196,23 @@ __global__ void __launch_bounds__(kThreadsA, 1)
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
-    if (lane == 0 && n_kv > 0) {
+    if (lane == 0 && n_max > 0) {
       prefetch_tmap(&tq);
       prefetch_tmap(&tk);
       prefetch_tmap(&tv);
-      mbar_arrive_expect_tx(&S->q_full, L::kQBytes);
-      for (int db = 0; db < L::kDB; ++db) tma_load_4d(smem + L::kQ + db * 16384, &tq, &S->q_full, db * 64, h, q0, b);
+      mbar_arrive_expect_tx(&S->q_full, (uint32_t)((n0 > 0) + (n1 > 0)) * L::kQBytes);
+      for (int t = 0; t < 2; ++t)
+        if (n_of(t) > 0)
+          for (int db = 0; db < L::kDB; ++db)
+            tma_load_4d(smem + L::kQ + t * L::kQBytes + db * 16384, &tq, &S->q_full, db * 64, h_of(t), q0_of(t), b);
       int issued = 0;
       bool ok = true;
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int st = j & 1;
-        if (j >= 2 && !mbar_wait(&S->kv_empty[st], ((j >> 1) - 1) & 1, abort_flag)) { ok = false; break; }
-        mbar_arrive_expect_tx(&S->kv_full[st], L::kKBytes + L::kVBytes);
-        uint8_t* ks = smem + L::kK + st * L::kKBytes;
-        uint8_t* vs = smem + L::kV + st * L::kVBytes;
+      for (int j = 0; j < n_max; ++j) {
+        const int st = j % NS;
+        if (j >= NS && !mbar_wait(&S->kv_empty[st], ((j / NS) - 1) & 1, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(&S->kv_full[st], L::kStageBytes);
+        uint8_t* ks = smem + L::kKV + st * L::kStageBytes;
+        uint8_t* vs = ks + L::kKBytes;
         const int kv0 = j * BKV;
         for (int db = 0; db < L::kDB; ++db) tma_load_4d(ks + db * 16384, &tk, &S->kv_full[st], db * 64, hk, kv0, b);
         for (int kb = 0; kb < 2; ++kb)
@@ -210,61 +224,71 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         set_status(a.status, kTimeoutFlag, 120);
         S->abort = 1;
       }
-      // the Q load and the last two K/V loads must land before the CTA exits (bounded)
+      // the Q loads and the K/V loads still in flight must land before the CTA exits (bounded)
       const uint64_t t0 = globaltimer_ns();
       while (!mbar_try_wait(&S->q_full, 0u) && globaltimer_ns() - t0 < kWaitNs) {}
-      for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j) {
+      for (int j = issued > NS ? issued - NS : 0; j < issued; ++j) {
         const uint64_t t1 = globaltimer_ns();
-        while (!mbar_try_wait(&S->kv_full[j & 1], (j >> 1) & 1) && globaltimer_ns() - t1 < kWaitNs) {}
+        while (!mbar_try_wait(&S->kv_full[j % NS], (j / NS) & 1) && globaltimer_ns() - t1 < kWaitNs) {}
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0 && n_kv > 0) {
+    if (lane == 0 && n_max > 0) {
       const uint32_t id_s = idesc_bf16(BQ, BKV, false, false);
       const uint32_t id_o = idesc_bf16(BQ, D, false, true);
-      const uint32_t sq = smem_u32(smem + L::kQ);
-      const uint32_t sp = smem_u32(smem + L::kP);
-      const uint32_t t_o = tmem_base + 256;
       bool ok = mbar_wait(&S->q_full, 0u, abort_flag);
-      auto issue_pv = [&](int jj) {
-        const uint32_t sv = smem_u32(smem + L::kV + (jj & 1) * L::kVBytes);
-#pragma unroll
-        for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_bf16(t_o, sw128_desc(sp + kb * 16384 + kk * 32),
-                      sw128_mn_desc(sv + kb * L::kDB * 8192 + kk * 16 * 128), id_o,
-                      (jj > 0 || kb > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&S->pv_done);
-        umma_commit(&S->kv_empty[jj & 1]);
-      };
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&S->kv_full[st], (j >> 1) & 1, abort_flag)) { ok = false; break; }
+      int kv_ready = -1;
+      auto ensure_kv = [&](int j) -> bool {
+        if (kv_ready >= j) return true;
+        if (!mbar_wait(&S->kv_full[j % NS], (j / NS) & 1, abort_flag)) return false;
         tmem_fence_after();
-        const uint32_t sk = smem_u32(smem + L::kK + st * L::kKBytes);
-        const uint32_t t_s = tmem_base + (uint32_t)(st * BKV);
+        kv_ready = j;
+        return true;
+      };
+      // S_t = Q_t K_j^T
+      auto issue_s = [&](int t, int j) {
+        const uint32_t sq = smem_u32(smem + L::kQ + t * L::kQBytes);
+        const uint32_t sk = smem_u32(smem + L::kKV + (j % NS) * L::kStageBytes);
+        const uint32_t t_s = tmem_base + (uint32_t)(t * BKV);
 #pragma unroll
         for (int db = 0; db < L::kDB; ++db)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             umma_bf16(t_s, sw128_desc(sq + db * 16384 + kk * 32), sw128_desc(sk + db * 16384 + kk * 32), id_s,
                       (db > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&S->s_full[st]);
-        if (j >= 1) {
-          if (!mbar_wait(&S->p_full, (j - 1) & 1, abort_flag)) { ok = false; break; }
+        umma_commit(&S->s_full[t]);
+      };
+      // O_t (+)= P_t V_j, P_t = bf16 pairs in the first 64 columns of S_t
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t sv = smem_u32(smem + L::kKV + (j % NS) * L::kStageBytes + L::kKBytes);
+        const uint32_t t_p = tmem_base + (uint32_t)(t * BKV);
+        const uint32_t t_o = tmem_base + 256u + (uint32_t)(t * D);
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk)
+          umma_bf16_ts(t_o, t_p + (uint32_t)(kk * 8),
+                       sw128_mn_desc(sv + (kk >> 2) * L::kDB * 8192 + (kk & 3) * 16 * 128), id_o,
+                       (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&S->pv_done[t]);
+      };
+      if (ok) ok = ensure_kv(0);
+      if (ok)
+        for (int t = 0; t < 2; ++t)
+          if (n_of(t) > 0) issue_s(t, 0);
+      for (int j = 0; j < n_max && ok; ++j) {
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (j >= n_of(t)) continue;
+          if (!mbar_wait(&S->p_full[t], j & 1, abort_flag)) { ok = false; break; }
           tmem_fence_after();
-          issue_pv(j - 1);
+          issue_pv(t, j);
+          if (j + 1 < n_of(t)) {
+            // S_t(j+1) overwrites P_t(j): wait until P_t(j) V_j has completed
+            if (!ensure_kv(j + 1) || !mbar_wait(&S->pv_done[t], j & 1, abort_flag)) { ok = false; break; }
+            tmem_fence_after();
+            issue_s(t, j + 1);
+          }
         }
-      }
-      if (ok) {
-        ok = mbar_wait(&S->p_full, (n_kv - 1) & 1, abort_flag);
-        if (ok) {
-          tmem_fence_after();
-          issue_pv(n_kv - 1);
-          umma_commit(&S->o_full);
-        }
+        if (ok) umma_commit(&S->kv_empty[j % NS]);   // every MMA reading stage j has been issued
       }
       if (!ok) {
         set_status(a.status, kTimeoutFlag, 121);
@@ -276,117 +300,94 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     }
   } else {
     // ---------------- softmax + epilogue (warps 2..9) ----------------
-    // Two warps share each TMEM lane quarter: warps 2-5 take key columns 0-63 of
-    // every tile (and O columns [0, D/2)), warps 6-9 key columns 64-127 (and O
-    // columns [D/2, D)). The two threads of a row exchange their tile maxima
-    // through shared memory behind a 64-thread named barrier.
-    const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int t = (warp - 2) >> 2;
+    const int quarter = warp & 3;                // TMEM lane quarter this warp may access
     const int r = quarter * 32 + lane;           // query row in the tile = TMEM lane
-    const int q = q0 + r;
+    const int h = h_of(t);
+    const int q = q0_of(t) + r;
+    const int n = n_of(t);
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const int bar_id = 1 + quarter;
-    float* xmax = reinterpret_cast<float*>(smem + L::kS + 128);   // [2][128] partial maxima, then [2][128] sums
-    uint8_t* prow = smem + L::kP + half * 16384 + (r >> 3) * 1024 + (r & 7) * 128;
+    const uint32_t t_s = tmem_base + lane_off + (uint32_t)(t * BKV);
+    const uint32_t t_o = tmem_base + lane_off + 256u + (uint32_t)(t * D);
     const int lim = a.causal ? q + (a.Sk - a.Sq) : a.Sk - 1;
     const int last = lim < a.Sk - 1 ? lim : a.Sk - 1;      // last key this row may see
-    constexpr int HC = BKV / 2;                            // key columns per thread
-    float m = -INFINITY, l = 0.f;                          // running max (log2 units), this half's sum
+    float m = -INFINITY, l = 0.f;                          // running reference max (log2 units), row sum
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      const int st = j & 1;
-      // (this barrier also orders the previous tile's reads of the exchange buffer before its reuse)
-      if (!pair_all(bar_id, mbar_wait(&S->s_full[st], (j >> 1) & 1, abort_flag))) { ok = false; break; }
+    for (int j = 0; j < n; ++j) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&S->s_full[t], j & 1, abort_flag))) { ok = false; break; }
       tmem_fence_after();
-      float s[HC];
+      float s[BKV];
 #pragma unroll
-      for (int c = 0; c < HC; c += 32)
-        tmem_ld32(tmem_base + lane_off + (uint32_t)(st * BKV + half * HC + c), s + c);
-      const int kv0 = j * BKV + half * HC;
-      if (kv0 + HC - 1 > last) {
+      for (int c = 0; c < BKV; c += 32) tmem_ld32(t_s + (uint32_t)c, s + c);
+      const int kv0 = j * BKV;
+      if (kv0 + BKV - 1 > last) {
 #pragma unroll
-        for (int c = 0; c < HC; ++c) s[c] = (kv0 + c <= last) ? s[c] : -INFINITY;
+        for (int c = 0; c < BKV; ++c) s[c] = (kv0 + c <= last) ? s[c] : -INFINITY;
       }
       float mt = s[0];
 #pragma unroll
-      for (int c = 1; c < HC; ++c) mt = fmaxf(mt, s[c]);
-      xmax[half * 128 + r] = mt;
-      asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
-      mt = fmaxf(mt, xmax[(half ^ 1) * 128 + r]) * a.scale_log2;
-      // lazy rescaling: keep the old reference max unless the new one exceeds it by more than 8 (2^8
-      // headroom in fp32), so O is rescaled only on large jumps
-      float m_ref = m, alpha = 1.f;
+      for (int c = 1; c < BKV; ++c) mt = fmaxf(mt, s[c]);
+      mt *= a.scale_log2;
+      // lazy rescaling: keep the reference max unless the new one exceeds it by more than 8 (2^8
+      // headroom in fp32 and bf16), so O is rescaled only on large jumps
+      float alpha = 1.f;
       if (mt > m + 8.f) {
-        m_ref = mt;
         alpha = m == -INFINITY ? 0.f : ex2_approx(m - mt);
+        m = mt;
       }
-      const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
+      const float m_use = m == -INFINITY ? 0.f : m;
       float sum = 0.f;
 #pragma unroll
-      for (int c = 0; c < HC; ++c) {
-        s[c] = ex2_approx(fmaf(s[c], a.scale_log2, -m_use));
-        sum += s[c];
+      for (int c0 = 0; c0 < BKV; c0 += 32) {
+        uint32_t p[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          const float e0 = ex2_approx(fmaf(s[c0 + c], a.scale_log2, -m_use));
+          const float e1 = ex2_approx(fmaf(s[c0 + c + 1], a.scale_log2, -m_use));
+          sum += e0 + e1;
+          p[c >> 1] = pack_bf16(e0, e1);
+        }
+        tmem_st16_nowait(t_s + (uint32_t)(c0 >> 1), p);   // 32 probabilities = 16 packed columns
       }
       l = l * alpha + sum;
-      m = m_ref;
-      if (j >= 1) {
-        // O may be rescaled (and P overwritten) only after the previous P V finished
-        if (!pair_all(bar_id, mbar_wait(&S->pv_done, (j - 1) & 1, abort_flag))) { ok = false; break; }
-        tmem_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+      // O_t is idle here: P_t(j-1) V_{j-1} completed before S_t(j) was issued
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-          for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 32) {
-            float o[32];
-            tmem_ld32(tmem_base + lane_off + 256u + (uint32_t)c, o);
+        for (int c = 0; c < D; c += 32) {
+          float o[32];
+          tmem_ld32(t_o + (uint32_t)c, o);
+          uint32_t ou[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(tmem_base + lane_off + 256u + (uint32_t)c, o);
-          }
+          for (int i = 0; i < 32; ++i) ou[i] = __float_as_uint(o[i] * alpha);
+          tmem_st32_nowait(t_o + (uint32_t)c, ou);
         }
       }
-      // this half's 64 bf16 probabilities = one 64-key block of the 128-byte-swizzled K-major P tile
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const float* p = s + c * 8;
-        uint4 v;
-        v.x = pack_bf16(p[0], p[1]);
-        v.y = pack_bf16(p[2], p[3]);
-        v.z = pack_bf16(p[4], p[5]);
-        v.w = pack_bf16(p[6], p[7]);
-        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = v;
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tmem_wait_st();
       tmem_fence_before();
-      mbar_arrive(&S->p_full);
+      mbar_arrive(&S->p_full[t]);
     }
-    // the row's total sum: this half's plus the partner's
-    float* xsum = xmax + 256;
-    xsum[half * 128 + r] = l;
-    asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
-    const float l_row = l + xsum[(half ^ 1) * 128 + r];
     if (!ok) {
       if (lane == 0) {
         set_status(a.status, kTimeoutFlag, 122);
         S->abort = 1;
       }
-    } else if (n_kv == 0) {
+    } else if (q0_of(t) < a.Sq && n == 0) {
       // no key is visible to any row of this tile (causal with Sq > Sk): zero rows
       if (q < a.Sq) {
         __nv_bfloat16* orow = a.o + (int64_t)b * a.so_b + (int64_t)q * a.so_s + (int64_t)h * a.so_h;
-        for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 8)
-          *reinterpret_cast<uint4*>(orow + c) = make_uint4(0u, 0u, 0u, 0u);
-        if (a.lse && half == 0) a.lse[((int64_t)b * a.Hq + h) * a.Sq + q] = -INFINITY;
+        for (int c = 0; c < D; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0u, 0u, 0u, 0u);
+        if (a.lse) a.lse[((int64_t)b * a.Hq + h) * a.Sq + q] = -INFINITY;
       }
-    } else {
-      const bool w = mbar_wait(&S->o_full, 0u, abort_flag);
+    } else if (n > 0) {
+      const bool w = mbar_wait(&S->pv_done[t], (n - 1) & 1, abort_flag);
       if (__all_sync(0xffffffffu, w)) {
         tmem_fence_after();
-        const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
+        const float inv = l > 0.f ? 1.f / l : 0.f;
         __nv_bfloat16* orow = a.o + (int64_t)b * a.so_b + (int64_t)q * a.so_s + (int64_t)h * a.so_h;
 #pragma unroll 1
-        for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 32) {
+        for (int c = 0; c < D; c += 32) {
           float o[32];
-          tmem_ld32(tmem_base + lane_off + 256u + (uint32_t)c, o);
+          tmem_ld32(t_o + (uint32_t)c, o);
           if (q < a.Sq) {
 #pragma unroll
             for (int i = 0; i < 32; i += 8) {
@@ -399,9 +400,8 @@ __global__ void __launch_bounds__(kThreadsA, 1)
             }
           }
         }
-        if (q < a.Sq && a.lse && half == 0)
-          a.lse[((int64_t)b * a.Hq + h) * a.Sq + q] =
-              l_row > 0.f ? m * 0.69314718055994531f + logf(l_row) : -INFINITY;
+        if (q < a.Sq && a.lse)
+          a.lse[((int64_t)b * a.Hq + h) * a.Sq + q] = l > 0.f ? m * 0.69314718055994531f + logf(l) : -INFINITY;
       } else if (lane == 0) {
         set_status(a.status, kTimeoutFlag, 123);
         S->abort = 1;
@@ -444,7 +444,8 @@ static int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtens
   const size_t smem = Layout<D>::kBytes;
   cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return (int)e;
-  dim3 grid((a.Sq + BQ - 1) / BQ, a.Hq, a.B);
+  dim3 grid(a.pair_heads ? (a.Sq + BQ - 1) / BQ : (a.Sq + 2 * BQ - 1) / (2 * BQ), a.pair_heads ? a.Hq / 2 : a.Hq,
+            a.B);
   attn_fwd_kernel<D><<<grid, kThreadsA, smem, st>>>(tq, tk, tv, a);
   return (int)cudaGetLastError();
 }
@@ -472,6 +473,7 @@ NFB_API int nfb_attn_fwd(const void* q, const void* k, const void* v, void* o, f
   if (rc) return rc;
   AttnArgs a;
   a.B = B; a.Sq = Sq; a.Sk = Sk; a.Hq = Hq; a.Hkv = Hkv; a.D = D; a.causal = causal;
+  a.pair_heads = (Hq / Hkv) % 2 == 0 ? 1 : 0;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.o = reinterpret_cast<__nv_bfloat16*>(o);
   a.so_b = so_b; a.so_s = so_s; a.so_h = so_h;

@@ -13,19 +13,21 @@
 //   attn_bwd_pre   Delta and lse * log2(e) per query row, padded to whole 128-query tiles
 //                  (padding: lse = +inf, so padded queries get P = 0), and dQ accumulator = 0.
 //   attn_bwd_kernel one CTA per (128-key tile, kv head, batch). K and V stay in shared memory;
-//                  the CTA walks every query tile of every query head of its group:
+//                  the CTA walks every query tile i of every query head of its group:
 //                    S^T  = K Q_i^T   (M 128 keys, N 128 queries, K = D) -> TMEM
 //                    dP^T = V dO_i^T  (same)                              -> TMEM
 //                    8 compute warps (two threads per key row, 64 queries each) turn S^T into
-//                    P^T and dP^T into dS^T (bf16, 128-byte-swizzled K-major tiles in smem)
-//                    dV  += P^T dO_i  (A = P^T K-major, B = dO_i read MN-major from its K-major
-//                                      TMA tile: the same smem serves both GEMMs)
-//                    dK  += dS^T Q_i  (same pattern)
+//                    P^T (bf16, written back over S^T in TMEM) and dP^T into dS^T (bf16,
+//                    128-byte-swizzled K-major tile in shared memory)
+//                    dV  += P^T dO_i  (A = P^T from TMEM, B = dO_i read MN-major from its TMA tile)
+//                    dK  += dS^T Q_i  (A = dS^T, B = Q_i read MN-major)
 //                    dQ_i = dS K      (A = the dS^T tile read MN-major, B = K read MN-major)
-//                    the compute warps add dQ_i into the fp32 accumulator (red.global.add).
+//                  The compute warps are software-pipelined: step i's dK / dQ MMAs run while they
+//                  compute P of step i+1; then each warp copies its 32 x 32 fp32 blocks of dQ_i
+//                  from TMEM into its own slice of the (consumed) dS^T tile and adds them to the
+//                  fp32 dQ accumulator with TMA reduce-adds (whole lines, performed in L2).
 //                  dK and dV stay in TMEM for the whole walk (GQA heads accumulate there) and
-//                  are written once at the end. The next tile's S^T is computed while the
-//                  compute warps drain dQ_i (with D = 64 dQ has its own TMEM columns).
+//                  are written once at the end.
 //   attn_bwd_post  dQ accumulator (fp32) -> bf16 dQ.
 // Every wait is bounded by %globaltimer and reports through the status word (no hang, no trap);
 // no cluster, no multicast. Parity: the reference differentiates F.scaled_dot_product_attention
@@ -49,7 +51,6 @@ struct BwdArgs {
   float scale_log2;            // scale * log2(e)
   const float* lse2;           // [B, Hq, Sq_pad] lse * log2(e)
   const float* delta;          // [B, Hq, Sq_pad]
-  float* dq_acc;               // [B, Sq, Hq, D] fp32
   __nv_bfloat16* dk;           // [B, Sk, Hkv, D]
   __nv_bfloat16* dv;
   int64_t sdk_b, sdk_s, sdk_h, sdv_b, sdv_s, sdv_h;
@@ -58,38 +59,42 @@ struct BwdArgs {
 
 struct alignas(8) BwdShared {
   uint64_t kv_full;
-  uint64_t qdo_full[2];
-  uint64_t qdo_empty[2];
+  uint64_t qdo_full[3];
+  uint64_t qdo_empty[3];
   uint64_t s_full;
   uint64_t dp_full;
-  uint64_t p_ready;            // 256 arrivals: P^T in smem, S^T read
+  uint64_t p_ready;            // 256 arrivals: P^T written over S^T in TMEM
+  uint64_t dv_done;            // dV MMA of the step complete (P^T consumed)
   uint64_t ds_ready;           // 256 arrivals: dS^T in smem, dP^T read
   uint64_t dq_full;
   uint64_t dq_free;            // 256 arrivals: dQ read from TMEM
-  uint64_t pds_free;           // the MMAs reading P^T / dS^T of the last tile are done
   uint64_t acc_full;           // dK, dV complete
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
 };
 
-// smem: [K: D/64 x 16 KB][V][Q: stages][dO: stages][P^T 32 KB][dS^T 32 KB][lse2, delta: stages x 1 KB][BwdShared]
+// smem: [K: D/64 x 16 KB][V][Q: stages][dO: stages][dS^T 32 KB][lse2, delta: stages x 1 KB][BwdShared]
 template <int D>
 struct LayoutB {
-  static constexpr int kStages = D == 64 ? 2 : 1;
+  static constexpr int kStages = D == 64 ? 3 : 2;
   static constexpr int kTile = T * D * 2;            // one [128 x D] bf16 tile
   static constexpr int kK = 0;
   static constexpr int kV = kK + kTile;
   static constexpr int kQ = kV + kTile;
   static constexpr int kDO = kQ + kStages * kTile;
-  static constexpr int kP = kDO + kStages * kTile;
-  static constexpr int kDS = kP + T * T * 2;
+  static constexpr int kDS = kDO + kStages * kTile;
   static constexpr int kRow = kDS + T * T * 2;       // per stage: 128 lse2 + 128 delta floats
   static constexpr int kS = kRow + kStages * 1024;
-  static constexpr size_t kBytes = (size_t)kS + 256 + 1024;
-  // TMEM columns
+  static constexpr size_t kNeed = (size_t)kS + 256;   // + BwdShared
+  // dynamic shared memory requested: the layout plus alignment slack, capped at the 227 KB limit
+  // (the kernel checks at run time that the aligned layout fits what it was given)
+  static constexpr size_t kLimit = 227 * 1024;
+  static constexpr size_t kBytes = kNeed + 1024 < kLimit ? kNeed + 1024 : kLimit;
+  static_assert(kNeed <= kLimit, "shared memory");
+  // TMEM columns: S^T (P^T bf16 over it: queries 0-63 at +0, 64-127 at +64), dP^T, dV, dK, dQ
   static constexpr uint32_t cS = 0, cDP = 128, cDV = 256, cDK = 256 + D;
-  static constexpr uint32_t cDQ = D == 64 ? 256 + 2 * D : 0;   // D = 128: dQ reuses the S^T columns
+  static constexpr uint32_t cDQ = D == 64 ? 256 + 2 * D : cDP;   // D = 128: dQ over the consumed dP^T
 };
 
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
@@ -100,6 +105,19 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
         "r"(smem_u32(bar))
       : "memory");
 }
+
+// Element-wise add of a shared-memory box into the tensor (performed by L2), bulk-group completion.
+__device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2,
+                                                  int c3) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];"
+      ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // 1-D bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16).
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -119,6 +137,26 @@ __device__ __forceinline__ uint64_t mn_desc(uint32_t saddr, uint32_t lbo_bytes) 
   return d;
 }
 
+// D (TMEM) (+)= A (TMEM, 128 lanes x 16 bf16 packed two per column) x B (shared memory descriptor).
+__device__ __forceinline__ void umma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st16_nowait(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -128,10 +166,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
-}
-
-__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }
 
 // The 8 compute warps (256 threads) as one named barrier group.
@@ -158,11 +192,18 @@ __device__ __forceinline__ int first_qtile(const BwdArgs& a, int k0) {
 template <int D>
 __global__ void __launch_bounds__(kThreadsB, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                    const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo, BwdArgs a) {
+                    const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
+                    const __grid_constant__ CUtensorMap tdq, BwdArgs a) {
   using L = LayoutB<D>;
   constexpr int kDB = D / 64;
+  constexpr int NS = L::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // the aligned layout must fit the allocation (the request is capped at the per-block limit)
+  if ((size_t)(smem - smem_raw) + L::kNeed > L::kBytes) {
+    if (threadIdx.x == 0) set_status(a.status, kTimeoutFlag, 143);
+    return;
+  }
   BwdShared* S = reinterpret_cast<BwdShared*>(smem + L::kS);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile int* abort_flag = &S->abort;
@@ -175,17 +216,17 @@ __global__ void __launch_bounds__(kThreadsB, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&S->kv_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < NS; ++s) {
       mbar_init(&S->qdo_full[s], 1);
       mbar_init(&S->qdo_empty[s], 1);
     }
     mbar_init(&S->s_full, 1);
     mbar_init(&S->dp_full, 1);
     mbar_init(&S->p_ready, 256);
+    mbar_init(&S->dv_done, 1);
     mbar_init(&S->ds_ready, 256);
     mbar_init(&S->dq_full, 1);
     mbar_init(&S->dq_free, 256);
-    mbar_init(&S->pds_free, 1);
     mbar_init(&S->acc_full, 1);
     mbar_init(&S->drain, 1);
     S->abort = 0;
@@ -217,8 +258,8 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       bool ok = true;
       int issued = 0;
       for (int t = 0; t < n_tiles && ok; ++t) {
-        const int st = t % L::kStages;
-        const int use = t / L::kStages;            // how often this stage was filled before
+        const int st = t % NS;
+        const int use = t / NS;                    // how often this stage was filled before
         if (use >= 1 && !mbar_wait_sleep(&S->qdo_empty[st], (use - 1) & 1, abort_flag)) { ok = false; break; }
         const int h = hk * G + t / per_head;
         const int q0 = (i0 + t % per_head) * T;
@@ -239,9 +280,9 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       // drain (bounded): K/V and the latest Q/dO loads
       const uint64_t t0 = globaltimer_ns();
       while (!mbar_try_wait(&S->kv_full, 0u) && globaltimer_ns() - t0 < kWaitNs) {}
-      for (int t = issued > L::kStages ? issued - L::kStages : 0; t < issued; ++t) {
+      for (int t = issued > NS ? issued - NS : 0; t < issued; ++t) {
         const uint64_t t1 = globaltimer_ns();
-        while (!mbar_try_wait(&S->qdo_full[t % L::kStages], (t / L::kStages) & 1) && globaltimer_ns() - t1 < kWaitNs) {}
+        while (!mbar_try_wait(&S->qdo_full[t % NS], (t / NS) & 1) && globaltimer_ns() - t1 < kWaitNs) {}
       }
     }
   } else if (warp == 1) {
@@ -251,17 +292,9 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       const uint32_t id_kv = idesc_bf16(T, D, false, true);     // dV, dK: A K-major, B MN-major
       const uint32_t id_q = idesc_bf16(T, D, true, true);       // dQ: A (dS^T) and B (K) MN-major
       const uint32_t sk = smem_u32(smem + L::kK), sv = smem_u32(smem + L::kV);
-      const uint32_t sp = smem_u32(smem + L::kP), sds = smem_u32(smem + L::kDS);
-      bool ok = mbar_wait_sleep(&S->kv_full, 0u, abort_flag);
-      for (int t = 0; t < n_tiles && ok; ++t) {
-        const int st = t % L::kStages;
-        const uint32_t sq = smem_u32(smem + L::kQ + st * L::kTile);
-        const uint32_t sdo = smem_u32(smem + L::kDO + st * L::kTile);
-        if (!mbar_wait_sleep(&S->qdo_full[st], (t / L::kStages) & 1, abort_flag)) { ok = false; break; }
-        // S^T columns free: the compute warps read S^T of t-1 (and, D = 128, drained dQ of t-1 there)
-        if (t >= 1 && !mbar_wait_sleep(&S->p_ready, (t - 1) & 1, abort_flag)) { ok = false; break; }
-        if (D == 128 && t >= 1 && !mbar_wait_sleep(&S->dq_free, (t - 1) & 1, abort_flag)) { ok = false; break; }
-        tmem_fence_after();
+      const uint32_t sds = smem_u32(smem + L::kDS);
+      auto issue_s = [&](int t) {        // S^T = K Q_t^T
+        const uint32_t sq = smem_u32(smem + L::kQ + (t % NS) * L::kTile);
 #pragma unroll
         for (int db = 0; db < kDB; ++db)
 #pragma unroll
@@ -269,8 +302,9 @@ __global__ void __launch_bounds__(kThreadsB, 1)
             umma_bf16(tmem + L::cS, sw128_desc(sk + db * 16384 + kk * 32), sw128_desc(sq + db * 16384 + kk * 32),
                       id_s, (db > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&S->s_full);
-        if (t >= 1 && !mbar_wait_sleep(&S->ds_ready, (t - 1) & 1, abort_flag)) { ok = false; break; }
-        tmem_fence_after();
+      };
+      auto issue_dp = [&](int t) {       // dP^T = V dO_t^T
+        const uint32_t sdo = smem_u32(smem + L::kDO + (t % NS) * L::kTile);
 #pragma unroll
         for (int db = 0; db < kDB; ++db)
 #pragma unroll
@@ -278,16 +312,33 @@ __global__ void __launch_bounds__(kThreadsB, 1)
             umma_bf16(tmem + L::cDP, sw128_desc(sv + db * 16384 + kk * 32), sw128_desc(sdo + db * 16384 + kk * 32),
                       id_s, (db > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&S->dp_full);
-        // dV += P^T dO_i
+      };
+      bool ok = mbar_wait_sleep(&S->kv_full, 0u, abort_flag) && mbar_wait_sleep(&S->qdo_full[0], 0u, abort_flag);
+      if (ok) {
+        tmem_fence_after();
+        issue_s(0);
+        issue_dp(0);
+      }
+      for (int t = 0; t < n_tiles && ok; ++t) {
+        const int st = t % NS;
+        const uint32_t sq = smem_u32(smem + L::kQ + st * L::kTile);
+        const uint32_t sdo = smem_u32(smem + L::kDO + st * L::kTile);
+        // dV += P^T dO_t, P^T from TMEM (queries 0-63 at cS, 64-127 at cS + 64)
         if (!mbar_wait_sleep(&S->p_ready, t & 1, abort_flag)) { ok = false; break; }
         tmem_fence_after();
 #pragma unroll
-        for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_bf16(tmem + L::cDV, sw128_desc(sp + kb * 16384 + kk * 32),
-                      mn_desc(sdo + (kb * 64 + kk * 16) * 128, 16384), id_kv, (t > 0 || kb > 0 || kk > 0) ? 1u : 0u);
-        // dK += dS^T Q_i
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16_ts(tmem + L::cDV, tmem + L::cS + (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8),
+                       mn_desc(sdo + kk * 16 * 128, 16384), id_kv, (t > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&S->dv_done);
+        if (t + 1 < n_tiles) {
+          // S^T of the next step overwrites P^T: wait until the dV MMA has read it
+          if (!mbar_wait_sleep(&S->qdo_full[(t + 1) % NS], ((t + 1) / NS) & 1, abort_flag) ||
+              !mbar_wait_sleep(&S->dv_done, t & 1, abort_flag)) { ok = false; break; }
+          tmem_fence_after();
+          issue_s(t + 1);
+        }
+        // dK += dS^T Q_t
         if (!mbar_wait_sleep(&S->ds_ready, t & 1, abort_flag)) { ok = false; break; }
         tmem_fence_after();
 #pragma unroll
@@ -296,7 +347,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
           for (int kk = 0; kk < 4; ++kk)
             umma_bf16(tmem + L::cDK, sw128_desc(sds + kb * 16384 + kk * 32),
                       mn_desc(sq + (kb * 64 + kk * 16) * 128, 16384), id_kv, (t > 0 || kb > 0 || kk > 0) ? 1u : 0u);
-        // dQ_i = dS K (D = 64: its own columns, free once the compute warps drained dQ of t-1)
+        // dQ_t = dS K (D = 64: own columns, free once the compute warps drained dQ of t-1)
         if (D == 64 && t >= 1 && !mbar_wait_sleep(&S->dq_free, (t - 1) & 1, abort_flag)) { ok = false; break; }
         tmem_fence_after();
 #pragma unroll
@@ -304,8 +355,13 @@ __global__ void __launch_bounds__(kThreadsB, 1)
           umma_bf16(tmem + L::cDQ, mn_desc(sds + kk * 16 * 128, 16384), mn_desc(sk + kk * 16 * 128, 16384), id_q,
                     kk > 0 ? 1u : 0u);
         umma_commit(&S->dq_full);
-        umma_commit(&S->pds_free);
         umma_commit(&S->qdo_empty[st]);
+        if (t + 1 < n_tiles) {
+          // D = 128: dQ_t occupies the dP^T columns until the compute warps have drained it
+          if (D == 128 && !mbar_wait_sleep(&S->dq_free, t & 1, abort_flag)) { ok = false; break; }
+          tmem_fence_after();
+          issue_dp(t + 1);
+        }
       }
       if (ok) umma_commit(&S->acc_full);
       if (!ok) {
@@ -318,67 +374,110 @@ __global__ void __launch_bounds__(kThreadsB, 1)
     }
   } else {
     // ---------------- compute warps 2..9 ----------------
-    // Key row r = TMEM lane (quarter * 32 + lane); half 0 takes query columns 0-63 of each tile,
-    // half 1 columns 64-127 (and dQ / dK / dV columns [half * D/2, +D/2)).
+    // Key row r = TMEM lane (quarter * 32 + lane); half 0 takes queries 0-63 of each tile, half 1
+    // queries 64-127 (and dQ / dK / dV columns [half * D/2, +D/2)).
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int key = k0 + r;
     constexpr int HC = 64;
-    // P^T / dS^T row r, this half's 64 queries = one 128-byte row of block `half`
-    const uint32_t row_off = (uint32_t)(half * 16384 + (r >> 3) * 1024 + (r & 7) * 128);
+    // this warp's rows of the dS^T tile (block `half`, rows quarter*32..+31): 4 KB, also the
+    // staging box of its dQ blocks once the MMAs have consumed dS^T
+    uint8_t* slice = smem + L::kDS + half * 16384 + quarter * 4096;
+    uint8_t* drow = slice + lane * 128;
     bool ok = true;
+    int prev_h = 0, prev_q0 = 0;
+    // dQ of the previous step: TMEM -> this warp's slice -> TMA reduce-add into the accumulator
+    auto drain_dq = [&](int tt) -> bool {
+      const bool w = mbar_wait_sleep(&S->dq_full, tt & 1, abort_flag);
+      if (!compute_all(w)) return false;
+      tmem_fence_after();
+#pragma unroll
+      for (int bx = 0; bx < D / 64; ++bx) {
+        const int col = half * (D / 2) + bx * 32;
+        float g[32];
+        tmem_ld32(tmem + lane_off + L::cDQ + (uint32_t)col, g);
+        if (bx > 0) {
+          if (lane == 0) bulk_wait_read0();      // the previous box has been read out of the slice
+          __syncwarp();
+        }
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<float4*>(drow + ((c ^ (lane & 7)) << 4)) =
+              make_float4(g[4 * c], g[4 * c + 1], g[4 * c + 2], g[4 * c + 3]);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_4d(&tdq, slice, col, prev_h, prev_q0 + quarter * 32, b);
+          bulk_commit();
+        }
+      }
+      tmem_fence_before();
+      mbar_arrive(&S->dq_free);
+      return true;
+    };
     for (int t = 0; t < n_tiles; ++t) {
-      const int st = t % L::kStages;
+      const int st = t % NS;
       const int h = hk * G + t / per_head;
       const int q0 = (i0 + t % per_head) * T;
       const float* lse2 = reinterpret_cast<const float*>(smem + L::kRow + st * 1024) + half * HC;
       const float* dlt = reinterpret_cast<const float*>(smem + L::kRow + st * 1024 + 512) + half * HC;
-      bool w = mbar_wait_sleep(&S->qdo_full[st], (t / L::kStages) & 1, abort_flag);
+      // ---- P^T of step t ----
+      bool w = mbar_wait_sleep(&S->qdo_full[st], (t / NS) & 1, abort_flag);
       w = w && mbar_wait_sleep(&S->s_full, t & 1, abort_flag);
       if (!compute_all(w)) { ok = false; break; }
       tmem_fence_after();
-      // P^T row: p[c] for queries q0 + half*64 + c
       float p[HC];
 #pragma unroll
       for (int c = 0; c < HC; c += 32) tmem_ld32(tmem + lane_off + L::cS + (uint32_t)(half * HC + c), p + c);
       const int qb = q0 + half * HC;
       const int lim = key - (a.Sk - a.Sq);        // causal: queries q >= lim see this key
+      const bool full = key < a.Sk && (!a.causal || qb >= lim);
 #pragma unroll
-      for (int c = 0; c < HC; ++c) {
-        const bool vis = key < a.Sk && (!a.causal || qb + c >= lim);
-        p[c] = vis ? ex2_approx(fmaf(p[c], a.scale_log2, -lse2[c])) : 0.f;
+      for (int c = 0; c < HC; c += 4) {
+        const float4 l4 = *reinterpret_cast<const float4*>(lse2 + c);
+        p[c] = ex2_approx(fmaf(p[c], a.scale_log2, -l4.x));
+        p[c + 1] = ex2_approx(fmaf(p[c + 1], a.scale_log2, -l4.y));
+        p[c + 2] = ex2_approx(fmaf(p[c + 2], a.scale_log2, -l4.z));
+        p[c + 3] = ex2_approx(fmaf(p[c + 3], a.scale_log2, -l4.w));
       }
-      // the previous tile's MMAs must be done with the P^T / dS^T buffers
-      if (t >= 1) {
-        w = mbar_wait_sleep(&S->pds_free, (t - 1) & 1, abort_flag);
-        if (!compute_all(w)) { ok = false; break; }
-      }
-      uint8_t* prow = smem + L::kP + row_off;
+      if (!full) {
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint4 v;
-        v.x = pack_bf16(p[8 * c + 0], p[8 * c + 1]);
-        v.y = pack_bf16(p[8 * c + 2], p[8 * c + 3]);
-        v.z = pack_bf16(p[8 * c + 4], p[8 * c + 5]);
-        v.w = pack_bf16(p[8 * c + 6], p[8 * c + 7]);
-        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = v;
+        for (int c = 0; c < HC; ++c) p[c] = (key < a.Sk && (!a.causal || qb + c >= lim)) ? p[c] : 0.f;
       }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+#pragma unroll
+      for (int c0 = 0; c0 < HC; c0 += 32) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) pk[c] = pack_bf16(p[c0 + 2 * c], p[c0 + 2 * c + 1]);
+        tmem_st16_nowait(tmem + lane_off + L::cS + (uint32_t)(half * HC + (c0 >> 1)), pk);
+      }
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tmem_fence_before();
       mbar_arrive(&S->p_ready);
-      // dS^T = scale * P^T . (dP^T - Delta)
+      // ---- dQ of step t-1 (its MMAs ran while P of step t was computed) ----
+      if (t >= 1 && !drain_dq(t - 1)) { ok = false; break; }
+      // ---- dS^T = scale * P^T . (dP^T - Delta) of step t ----
       w = mbar_wait_sleep(&S->dp_full, t & 1, abort_flag);
       if (!compute_all(w)) { ok = false; break; }
       tmem_fence_after();
-      uint8_t* drow = smem + L::kDS + row_off;
+      if (t >= 1) {
+        if (lane == 0) bulk_wait_read0();        // the slice's dQ boxes have been read
+        __syncwarp();
+      }
 #pragma unroll
       for (int c = 0; c < HC; c += 32) {
         float dp[32];
         tmem_ld32(tmem + lane_off + L::cDP + (uint32_t)(half * HC + c), dp);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) dp[j] = a.scale * p[c + j] * (dp[j] - dlt[c + j]);
+        for (int j = 0; j < 32; j += 4) {
+          const float4 d4 = *reinterpret_cast<const float4*>(dlt + c + j);
+          dp[j] = a.scale * p[c + j] * (dp[j] - d4.x);
+          dp[j + 1] = a.scale * p[c + j + 1] * (dp[j + 1] - d4.y);
+          dp[j + 2] = a.scale * p[c + j + 2] * (dp[j + 2] - d4.z);
+          dp[j + 3] = a.scale * p[c + j + 3] * (dp[j + 3] - d4.w);
+        }
 #pragma unroll
         for (int g8 = 0; g8 < 4; ++g8) {
           const int cc = (c >> 3) + g8;
@@ -393,24 +492,12 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tmem_fence_before();
       mbar_arrive(&S->ds_ready);
-      // dQ_i rows (TMEM lane = query q0 + r): add this half's D/2 columns into the accumulator
-      w = mbar_wait_sleep(&S->dq_full, t & 1, abort_flag);
-      if (!compute_all(w)) { ok = false; break; }
-      tmem_fence_after();
-      const int q = q0 + r;
-      float* dst = a.dq_acc + (((int64_t)b * a.Sq + q) * a.Hq + h) * D + half * (D / 2);
-#pragma unroll
-      for (int c = 0; c < D / 2; c += 32) {
-        float g[32];
-        tmem_ld32(tmem + lane_off + L::cDQ + (uint32_t)(half * (D / 2) + c), g);
-        if (q < a.Sq) {
-#pragma unroll
-          for (int j = 0; j < 32; j += 4) red_add_v4(dst + c + j, g[j], g[j + 1], g[j + 2], g[j + 3]);
-        }
-      }
-      tmem_fence_before();
-      mbar_arrive(&S->dq_free);
+      prev_h = h;
+      prev_q0 = q0;
     }
+    if (ok && n_tiles > 0 && !drain_dq(n_tiles - 1)) ok = false;
+    if (lane == 0) bulk_wait_all();              // every dQ reduce-add performed before the CTA exits
+    __syncwarp();
     // dK, dV rows (TMEM lane = key): this half's D/2 columns, written once
     if (ok && n_tiles > 0) {
       bool w = mbar_wait_sleep(&S->acc_full, 0u, abort_flag);
@@ -534,14 +621,31 @@ static int make_tmap_bshd(CUtensorMap* m, const void* base, int Bn, int Sn, int 
   return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
 }
 
+// 4-D fp32 tensor map over the dQ accumulator [B, Sq, Hq, D] with 32 x 32 boxes (128-byte rows,
+// 128-byte swizzle), the target of the TMA reduce-adds.
+static int make_tmap_dq(CUtensorMap* m, const float* base, int Bn, int Sn, int Hn, int Dn) {
+  int rc = get_encode();
+  if (rc) return rc;
+  rc = bind_device_of(base);
+  if (rc) return rc;
+  cuuint64_t dims[4] = {(cuuint64_t)Dn, (cuuint64_t)Hn, (cuuint64_t)Sn, (cuuint64_t)Bn};
+  cuuint64_t strides[3] = {(cuuint64_t)Dn * 4, (cuuint64_t)Hn * Dn * 4, (cuuint64_t)Sn * Hn * Dn * 4};
+  cuuint32_t box[4] = {32, 1, 32, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
+}
+
 template <int D>
 static int launch_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tdo,
-                      const BwdArgs& a, cudaStream_t st) {
+                      const CUtensorMap& tdq, const BwdArgs& a, cudaStream_t st) {
   const size_t smem = LayoutB<D>::kBytes;
   cudaError_t e = cudaFuncSetAttribute(attn_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return (int)e;
   dim3 grid((a.Sk + T - 1) / T, a.Hkv, a.B);
-  attn_bwd_kernel<D><<<grid, kThreadsB, smem, st>>>(tq, tk, tv, tdo, a);
+  attn_bwd_kernel<D><<<grid, kThreadsB, smem, st>>>(tq, tk, tv, tdo, tdq, a);
   return (int)cudaGetLastError();
 }
 
@@ -600,17 +704,20 @@ NFB_API int nfb_attn_bwd(const void* q, const void* k, const void* v, const void
   if (rc) return rc;
   rc = make_tmap_bshd(&tdo, dout, B, Sq, Hq, D, sdo_[0], sdo_[1], sdo_[2]);
   if (rc) return rc;
+  CUtensorMap tdq;
+  rc = make_tmap_dq(&tdq, acc, B, Sq, Hq, D);
+  if (rc) return rc;
   BwdArgs a;
   a.B = B; a.Sq = Sq; a.Sk = Sk; a.Hq = Hq; a.Hkv = Hkv; a.D = D; a.Sq_pad = sq_pad; a.causal = causal;
   a.scale = scale;
   a.scale_log2 = scale * 1.4426950408889634f;
-  a.lse2 = lse2; a.delta = delta; a.dq_acc = acc;
+  a.lse2 = lse2; a.delta = delta;
   a.dk = reinterpret_cast<__nv_bfloat16*>(dk);
   a.dv = reinterpret_cast<__nv_bfloat16*>(dv);
   a.sdk_b = sdk_[0]; a.sdk_s = sdk_[1]; a.sdk_h = sdk_[2];
   a.sdv_b = sdv_[0]; a.sdv_s = sdv_[1]; a.sdv_h = sdv_[2];
   a.status = status;
-  rc = D == 64 ? launch_bwd<64>(tq, tk, tv, tdo, a, st) : launch_bwd<128>(tq, tk, tv, tdo, a, st);
+  rc = D == 64 ? launch_bwd<64>(tq, tk, tv, tdo, tdq, a, st) : launch_bwd<128>(tq, tk, tv, tdo, tdq, a, st);
   if (rc) return rc;
   const int64_t n8 = (int64_t)B * Sq * Hq * D / 8;
   const unsigned grid = (unsigned)(n8 < 148 * 64 ? (n8 + 255) / 256 : 148 * 16);

@@ -33,6 +33,8 @@ CASES = [  # B, Sq, Sk, Hq, Hkv, D, causal
     (2, 96, 1176, 6, 6, 64, False),
     (2, 16, 3392, 4, 4, 128, False),
     (1, 256, 200, 2, 1, 64, False),
+    (1, 700, 700, 3, 3, 64, True),      # consecutive query tiles per CTA, unequal causal extents
+    (2, 384, 384, 2, 2, 128, True),
 ]
 
 
