@@ -67,6 +67,8 @@ _SIGS: dict[str, tuple] = {
     "nfb_tc_gemm_ex": (I, [P, P, P, I, I, I, L, L, L, I, I, I, I, P, P]),
     "nfb_attn_fwd": (I, [P, P, P, P, P, I, I, I, I, I, I, L, L, L, L, L, L, L, L, L, L, L, L, I, F, P, P]),
     "nfb_attn_bwd_scratch_bytes": (L, [I, I, I, I]),
+    "nfb_attn_fwd_trace": (None, [P]),
+    "nfb_attn_bwd_trace": (None, [P]),
     "nfb_attn_bwd": (I, [P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, P, I, F, P, P]),
     "nfb_ce_tc_tiles": (I, [I]),
     "nfb_ce_tc_stats": (I, [P, L, P, L, P, I, I, I, P, P, P, P, P]),

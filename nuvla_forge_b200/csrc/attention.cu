@@ -14,11 +14,13 @@
 //               into a ring (4-D tensor maps over [B, S, H, D]).
 //   warp 1      MMA issuer (one elected lane), per tile t and key tile j:
 //               S_t = Q_t K_j^T into a 128-column TMEM buffer, then
-//               O_t += P_t V_j with P_t read from TMEM (the softmax warps
-//               overwrite S_t with the bf16 probabilities) and V_j MN-major
-//               from its TMA tile. The two tiles are issued staggered, so the
-//               tensor core runs one tile's MMAs while the other tile's
-//               softmax warps work.
+//               O_t += P_t V_j with P_t (bf16) read from TMEM and V_j MN-major
+//               from its TMA tile. It polls the barriers of both tiles and
+//               issues whichever MMA is ready, so one tile's MMAs run while
+//               the other tile's softmax warps work. With D = 64 P_t has its
+//               own TMEM columns and the softmax releases S_t right after
+//               loading it, so S_t of the next key tile is computed while the
+//               softmax exponentiates; with D = 128 P_t is written over S_t.
 //   warps 2-5   softmax of tile 0, warps 6-9 softmax of tile 1: one thread per
 //               query row (TMEM lane), the whole 128-key row of S in registers,
 //               so the row maximum needs no exchange. Online softmax in base 2
@@ -50,6 +52,7 @@ struct AttnArgs {
   int64_t so_b, so_s, so_h;     // element strides of O
   float* lse;                   // [B, Hq, Sq] (nullable)
   uint32_t* status;
+  unsigned long long* trace;    // per-phase cycle counters (traced instantiation only)
 };
 
 struct alignas(8) AttnShared {
@@ -57,6 +60,7 @@ struct alignas(8) AttnShared {
   uint64_t kv_full[4];
   uint64_t kv_empty[4];
   uint64_t s_full[2];
+  uint64_t s_free[2];          // 128 arrivals: the softmax has loaded S_t (separate-P layout)
   uint64_t p_full[2];
   uint64_t pv_done[2];
   uint64_t drain;
@@ -109,6 +113,31 @@ __device__ __forceinline__ void umma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, u
       : "memory");
 }
 
+// Non-blocking probe of an mbarrier phase (the MMA issuer polls several barriers in turn).
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// 64 consecutive 32-bit TMEM columns of this thread's lane; the caller waits (tmem_wait_ld).
+__device__ __forceinline__ void tmem_ld64_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 // 2^x with the SFU's approximate base-2 exponential (flushes denormal results to zero).
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
@@ -136,14 +165,23 @@ struct Layout {
   static constexpr size_t kBytes = (size_t)kS + 256 + 1024;   // AttnShared, alignment
   static_assert(kBytes <= 227 * 1024, "shared memory");
   static_assert(kBytes > 114 * 1024, "one CTA (and its 512 TMEM columns) per SM");
+  // TMEM columns. D = 64: S_t | P_t (bf16 pairs) | O_t each tile, so the softmax frees S_t as soon as
+  // it has loaded it and S_t of the next key tile is computed while it exponentiates. D = 128 (no room
+  // for separate P): P_t is written over S_t, and the next S_t waits until P_t V has completed.
+  static constexpr bool kSepP = D == 64;
+  static constexpr uint32_t cS = 0;                          // + t * 128
+  static constexpr uint32_t cP = kSepP ? 256 : 0;            // + t * (kSepP ? 64 : 128)
+  static constexpr uint32_t cPStride = kSepP ? 64 : 128;
+  static constexpr uint32_t cO = kSepP ? 384 : 256;          // + t * D
 };
 
-template <int D>
+template <int D, bool kTrace>
 __global__ void __launch_bounds__(kThreadsA, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                     const __grid_constant__ CUtensorMap tv, AttnArgs a) {
   using L = Layout<D>;
   constexpr int NS = L::kStages;
+  constexpr bool kSepP = L::kSepP;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   AttnShared* S = reinterpret_cast<AttnShared*>(smem + L::kS);
@@ -176,6 +214,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&S->s_full[t], 1);
+      mbar_init(&S->s_free[t], BQ);
       mbar_init(&S->p_full[t], BQ);
       mbar_init(&S->pv_done[t], 1);
     }
@@ -207,9 +246,12 @@ __global__ void __launch_bounds__(kThreadsA, 1)
             tma_load_4d(smem + L::kQ + t * L::kQBytes + db * 16384, &tq, &S->q_full, db * 64, h_of(t), q0_of(t), b);
       int issued = 0;
       bool ok = true;
+      PhaseClock<kTrace> pc;
+      pc.start();
       for (int j = 0; j < n_max; ++j) {
         const int st = j % NS;
         if (j >= NS && !mbar_wait(&S->kv_empty[st], ((j / NS) - 1) & 1, abort_flag)) { ok = false; break; }
+        pc.mark(0);
         mbar_arrive_expect_tx(&S->kv_full[st], L::kStageBytes);
         uint8_t* ks = smem + L::kKV + st * L::kStageBytes;
         uint8_t* vs = ks + L::kKBytes;
@@ -219,7 +261,9 @@ __global__ void __launch_bounds__(kThreadsA, 1)
           for (int db = 0; db < L::kDB; ++db)
             tma_load_4d(vs + (kb * L::kDB + db) * 8192, &tv, &S->kv_full[st], db * 64, hk, kv0 + kb * 64, b);
         ++issued;
+        pc.mark(1);
       }
+      pc.flush(a.trace, 16);
       if (!ok) {
         set_status(a.status, kTimeoutFlag, 120);
         S->abort = 1;
@@ -233,63 +277,151 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+    // ---------------- MMA issuer: polls both tiles, issues whichever MMA is ready ----------------
     if (lane == 0 && n_max > 0) {
-      const uint32_t id_s = idesc_bf16(BQ, BKV, false, false);
-      const uint32_t id_o = idesc_bf16(BQ, D, false, true);
+      constexpr uint32_t id_s = idesc_bf16(BQ, BKV, false, false);
+      constexpr uint32_t id_o = idesc_bf16(BQ, D, false, true);
+      // shared-memory descriptors computed once; a tile offset is added to the start-address field
+      const uint64_t dq0 = sw128_desc(smem_u32(smem + L::kQ));
+      const uint64_t dk0 = sw128_desc(smem_u32(smem + L::kKV));
+      const uint64_t dv0 = sw128_mn_desc(smem_u32(smem + L::kKV + L::kKBytes));
+      PhaseClock<kTrace> pc;
+      pc.start();
       bool ok = mbar_wait(&S->q_full, 0u, abort_flag);
-      int kv_ready = -1;
-      auto ensure_kv = [&](int j) -> bool {
-        if (kv_ready >= j) return true;
-        if (!mbar_wait(&S->kv_full[j % NS], (j / NS) & 1, abort_flag)) return false;
-        tmem_fence_after();
-        kv_ready = j;
-        return true;
-      };
-      // S_t = Q_t K_j^T
-      auto issue_s = [&](int t, int j) {
-        const uint32_t sq = smem_u32(smem + L::kQ + t * L::kQBytes);
-        const uint32_t sk = smem_u32(smem + L::kKV + (j % NS) * L::kStageBytes);
-        const uint32_t t_s = tmem_base + (uint32_t)(t * BKV);
-#pragma unroll
-        for (int db = 0; db < L::kDB; ++db)
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_bf16(t_s, sw128_desc(sq + db * 16384 + kk * 32), sw128_desc(sk + db * 16384 + kk * 32), id_s,
-                      (db > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&S->s_full[t]);
-      };
-      // O_t (+)= P_t V_j, P_t = bf16 pairs in the first 64 columns of S_t
-      auto issue_pv = [&](int t, int j) {
-        const uint32_t sv = smem_u32(smem + L::kKV + (j % NS) * L::kStageBytes + L::kKBytes);
-        const uint32_t t_p = tmem_base + (uint32_t)(t * BKV);
-        const uint32_t t_o = tmem_base + 256u + (uint32_t)(t * D);
-#pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk)
-          umma_bf16_ts(t_o, t_p + (uint32_t)(kk * 8),
-                       sw128_mn_desc(sv + (kk >> 2) * L::kDB * 8192 + (kk & 3) * 16 * 128), id_o,
-                       (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&S->pv_done[t]);
-      };
-      if (ok) ok = ensure_kv(0);
-      if (ok)
-        for (int t = 0; t < 2; ++t)
-          if (n_of(t) > 0) issue_s(t, 0);
-      for (int j = 0; j < n_max && ok; ++j) {
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (j >= n_of(t)) continue;
-          if (!mbar_wait(&S->p_full[t], j & 1, abort_flag)) { ok = false; break; }
-          tmem_fence_after();
-          issue_pv(t, j);
-          if (j + 1 < n_of(t)) {
-            // S_t(j+1) overwrites P_t(j): wait until P_t(j) V_j has completed
-            if (!ensure_kv(j + 1) || !mbar_wait(&S->pv_done[t], j & 1, abort_flag)) { ok = false; break; }
+      pc.mark(1);
+      int js[2] = {0, 0}, jp[2] = {0, 0};     // next S / next PV per tile
+      int kv_ready = -1, released = 0;
+      uint32_t idle = 0;
+      uint64_t t_idle = 0;
+      auto try_tile = [&](const int t) -> bool {
+        bool progress = false;
+        const int n = t ? n1 : n0;
+        if (js[t] < n) {
+          const int j = js[t];
+          bool ready = true;
+          if (kv_ready < j) {
+            if (mbar_test(&S->kv_full[j % NS], (j / NS) & 1)) kv_ready = j;
+            else ready = false;
+          }
+          // S_t's columns are free once the softmax has loaded S_t(j-1) (separate P) or once
+          // P_t(j-1) V has completed (P written over S)
+          if (ready && j > 0)
+            ready = kSepP ? mbar_test(&S->s_free[t], (j - 1) & 1) : mbar_test(&S->pv_done[t], (j - 1) & 1);
+          if (ready) {
             tmem_fence_after();
-            issue_s(t, j + 1);
+            const uint64_t da = dq0 + (uint64_t)((t * L::kQBytes) >> 4);
+            const uint64_t db_ = dk0 + (uint64_t)(((j % NS) * L::kStageBytes) >> 4);
+            const uint32_t t_s = tmem_base + L::cS + (uint32_t)(t * BKV);
+#pragma unroll
+            for (int db = 0; db < L::kDB; ++db)
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                umma_bf16(t_s, da + (uint64_t)((db * 16384 + kk * 32) >> 4),
+                          db_ + (uint64_t)((db * 16384 + kk * 32) >> 4), id_s, (db > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(&S->s_full[t]);
+            ++js[t];
+            progress = true;
           }
         }
-        if (ok) umma_commit(&S->kv_empty[j % NS]);   // every MMA reading stage j has been issued
+        if (jp[t] < js[t] && mbar_test(&S->p_full[t], jp[t] & 1)) {
+          const int j = jp[t];
+          tmem_fence_after();
+          const uint64_t dv = dv0 + (uint64_t)(((j % NS) * L::kStageBytes) >> 4);
+          const uint32_t t_p = tmem_base + L::cP + (uint32_t)(t * L::cPStride);
+          const uint32_t t_o = tmem_base + L::cO + (uint32_t)(t * D);
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk)
+            umma_bf16_ts(t_o, t_p + (uint32_t)(kk * 8),
+                         dv + (uint64_t)(((kk >> 2) * L::kDB * 8192 + (kk & 3) * 16 * 128) >> 4), id_o,
+                         (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&S->pv_done[t]);
+          ++jp[t];
+          progress = true;
+          // a K/V stage is free once every tile that reads it has issued its P V
+          while (released < n_max && (jp[0] > released || n0 <= released) && (jp[1] > released || n1 <= released)) {
+            umma_commit(&S->kv_empty[released % NS]);
+            ++released;
+          }
+        }
+        return progress;
+      };
+      if (!kSepP) {
+        // P over S: S_t(j+1) can only follow P_t(j) V, so issue in a fixed staggered order, each
+        // S_t(j+1) right behind its tile's P V (a greedy poll would let the other tile's P V in between)
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (n_of(t) == 0) continue;
+          if (!mbar_wait(&S->kv_full[0], 0u, abort_flag)) { ok = false; break; }
+          kv_ready = 0;
+          tmem_fence_after();
+          const uint64_t da = dq0 + (uint64_t)((t * L::kQBytes) >> 4);
+          const uint32_t t_s = tmem_base + L::cS + (uint32_t)(t * BKV);
+#pragma unroll
+          for (int db = 0; db < L::kDB; ++db)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16(t_s, da + (uint64_t)((db * 16384 + kk * 32) >> 4), dk0 + (uint64_t)((db * 16384 + kk * 32) >> 4),
+                        id_s, (db > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&S->s_full[t]);
+          js[t] = 1;
+        }
+        for (int j = 0; j < n_max && ok; ++j) {
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (j >= n_of(t)) continue;
+            if (!mbar_wait(&S->p_full[t], j & 1, abort_flag)) { ok = false; break; }
+            pc.mark(0);
+            tmem_fence_after();
+            const uint64_t dv = dv0 + (uint64_t)(((j % NS) * L::kStageBytes) >> 4);
+            const uint32_t t_p = tmem_base + L::cP + (uint32_t)(t * L::cPStride);
+            const uint32_t t_o = tmem_base + L::cO + (uint32_t)(t * D);
+#pragma unroll
+            for (int kk = 0; kk < BKV / 16; ++kk)
+              umma_bf16_ts(t_o, t_p + (uint32_t)(kk * 8),
+                           dv + (uint64_t)(((kk >> 2) * L::kDB * 8192 + (kk & 3) * 16 * 128) >> 4), id_o,
+                           (j > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(&S->pv_done[t]);
+            pc.mark(3);
+            if (j + 1 < n_of(t)) {
+              if (kv_ready < j + 1) {
+                if (!mbar_wait(&S->kv_full[(j + 1) % NS], ((j + 1) / NS) & 1, abort_flag)) { ok = false; break; }
+                kv_ready = j + 1;
+              }
+              if (!mbar_wait(&S->pv_done[t], j & 1, abort_flag)) { ok = false; break; }
+              pc.mark(2);
+              tmem_fence_after();
+              const uint64_t da = dq0 + (uint64_t)((t * L::kQBytes) >> 4);
+              const uint64_t db_ = dk0 + (uint64_t)((((j + 1) % NS) * L::kStageBytes) >> 4);
+              const uint32_t t_s = tmem_base + L::cS + (uint32_t)(t * BKV);
+#pragma unroll
+              for (int db = 0; db < L::kDB; ++db)
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                  umma_bf16(t_s, da + (uint64_t)((db * 16384 + kk * 32) >> 4),
+                            db_ + (uint64_t)((db * 16384 + kk * 32) >> 4), id_s, (db > 0 || kk > 0) ? 1u : 0u);
+              umma_commit(&S->s_full[t]);
+              pc.mark(3);
+            }
+          }
+          if (ok) umma_commit(&S->kv_empty[j % NS]);   // every MMA reading stage j has been issued
+        }
+        jp[0] = n0;
+        jp[1] = n1;
       }
+      while (ok && (jp[0] < n0 || jp[1] < n1)) {
+        const bool p0 = try_tile(0);
+        const bool p1 = try_tile(1);
+        if (p0 || p1) {
+          pc.mark(3);
+          idle = 0;
+        } else if ((++idle & 255u) == 0) {
+          // bounded: give up after kWaitNs without progress, or when another role aborted
+          pc.mark(0);
+          const uint64_t now = globaltimer_ns();
+          if (idle == 256u) t_idle = now;
+          else if (now - t_idle > kWaitNs) ok = false;
+          if (*abort_flag) ok = false;
+        }
+      }
+      pc.flush(a.trace, 8);
       if (!ok) {
         set_status(a.status, kTimeoutFlag, 121);
         S->abort = 1;
@@ -307,26 +439,43 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     const int q = q0_of(t) + r;
     const int n = n_of(t);
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const uint32_t t_s = tmem_base + lane_off + (uint32_t)(t * BKV);
-    const uint32_t t_o = tmem_base + lane_off + 256u + (uint32_t)(t * D);
+    const uint32_t t_s = tmem_base + lane_off + L::cS + (uint32_t)(t * BKV);
+    const uint32_t t_p = tmem_base + lane_off + L::cP + (uint32_t)(t * L::cPStride);
+    const uint32_t t_o = tmem_base + lane_off + L::cO + (uint32_t)(t * D);
     const int lim = a.causal ? q + (a.Sk - a.Sq) : a.Sk - 1;
     const int last = lim < a.Sk - 1 ? lim : a.Sk - 1;      // last key this row may see
     float m = -INFINITY, l = 0.f;                          // running reference max (log2 units), row sum
     bool ok = true;
+    PhaseClock<kTrace> pc;
+    pc.start();
     for (int j = 0; j < n; ++j) {
       if (!__all_sync(0xffffffffu, mbar_wait(&S->s_full[t], j & 1, abort_flag))) { ok = false; break; }
+      pc.mark(0);
       tmem_fence_after();
       float s[BKV];
-#pragma unroll
-      for (int c = 0; c < BKV; c += 32) tmem_ld32(t_s + (uint32_t)c, s + c);
+      {
+        uint32_t* su = reinterpret_cast<uint32_t*>(s);
+        tmem_ld64_nowait(t_s, su);
+        tmem_ld64_nowait(t_s + 64u, su + 64);
+        tmem_wait_ld();
+      }
+      if (kSepP) {
+        tmem_fence_before();
+        mbar_arrive(&S->s_free[t]);              // the MMA issuer may compute the next S_t now
+      }
+      pc.mark(1);
       const int kv0 = j * BKV;
       if (kv0 + BKV - 1 > last) {
 #pragma unroll
         for (int c = 0; c < BKV; ++c) s[c] = (kv0 + c <= last) ? s[c] : -INFINITY;
       }
-      float mt = s[0];
+      // row maximum with 8 independent chains (a single chain is 127 dependent instructions)
+      float mx[8];
 #pragma unroll
-      for (int c = 1; c < BKV; ++c) mt = fmaxf(mt, s[c]);
+      for (int i = 0; i < 8; ++i) mx[i] = s[i];
+#pragma unroll
+      for (int c = 8; c < BKV; ++c) mx[c & 7] = fmaxf(mx[c & 7], s[c]);
+      float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       mt *= a.scale_log2;
       // lazy rescaling: keep the reference max unless the new one exceeds it by more than 8 (2^8
       // headroom in fp32 and bf16), so O is rescaled only on large jumps
@@ -336,21 +485,32 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         m = mt;
       }
       const float m_use = m == -INFINITY ? 0.f : m;
-      float sum = 0.f;
+      // P_t(j-1) V and O_t: the previous P V must have completed before P_t and O_t are written
+      // (with P over S it completed before S_t(j) was issued)
+      if (kSepP && j > 0) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&S->pv_done[t], (j - 1) & 1, abort_flag))) { ok = false; break; }
+        tmem_fence_after();
+      }
+      pc.mark(2);
+      float sm[4] = {0.f, 0.f, 0.f, 0.f};                  // row sum in 4 independent chains
 #pragma unroll
       for (int c0 = 0; c0 < BKV; c0 += 32) {
         uint32_t p[16];
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
-          const float e0 = ex2_approx(fmaf(s[c0 + c], a.scale_log2, -m_use));
-          const float e1 = ex2_approx(fmaf(s[c0 + c + 1], a.scale_log2, -m_use));
-          sum += e0 + e1;
+          // one pair in four on the FMA pipe, the rest on the SFU (the SFU alone bounds this loop)
+          const bool poly = ((c >> 1) & 3) == 3;
+          const float x0 = fmaf(s[c0 + c], a.scale_log2, -m_use), x1 = fmaf(s[c0 + c + 1], a.scale_log2, -m_use);
+          const float e0 = poly ? ex2_poly(x0) : ex2_approx(x0);
+          const float e1 = poly ? ex2_poly(x1) : ex2_approx(x1);
+          sm[(c >> 1) & 3] += e0 + e1;
           p[c >> 1] = pack_bf16(e0, e1);
         }
-        tmem_st16_nowait(t_s + (uint32_t)(c0 >> 1), p);   // 32 probabilities = 16 packed columns
+        tmem_st16_nowait(t_p + (uint32_t)(c0 >> 1), p);   // 32 probabilities = 16 packed columns
       }
+      const float sum = (sm[0] + sm[1]) + (sm[2] + sm[3]);
+      pc.mark(3);
       l = l * alpha + sum;
-      // O_t is idle here: P_t(j-1) V_{j-1} completed before S_t(j) was issued
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
         for (int c = 0; c < D; c += 32) {
@@ -365,6 +525,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       tmem_wait_st();
       tmem_fence_before();
       mbar_arrive(&S->p_full[t]);
+      pc.mark(4);
     }
     if (!ok) {
       if (lane == 0) {
@@ -380,6 +541,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       }
     } else if (n > 0) {
       const bool w = mbar_wait(&S->pv_done[t], (n - 1) & 1, abort_flag);
+      pc.mark(5);
       if (__all_sync(0xffffffffu, w)) {
         tmem_fence_after();
         const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -402,11 +564,13 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         }
         if (q < a.Sq && a.lse)
           a.lse[((int64_t)b * a.Hq + h) * a.Sq + q] = l > 0.f ? m * 0.69314718055994531f + logf(l) : -INFINITY;
+        pc.mark(6);
       } else if (lane == 0) {
         set_status(a.status, kTimeoutFlag, 123);
         S->abort = 1;
       }
     }
+    pc.flush(a.trace, 0);
   }
 
   tmem_fence_before();
@@ -438,15 +602,20 @@ static int make_tmap_bshd(CUtensorMap* m, const void* base, int Bn, int Sn, int 
   return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
 }
 
+// Per-phase cycle counters: when set (nfb_attn_fwd_trace), launches run the traced instantiation.
+static unsigned long long* g_trace = nullptr;
+
 template <int D>
-static int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const AttnArgs& a,
+static int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, AttnArgs a,
                       cudaStream_t st) {
   const size_t smem = Layout<D>::kBytes;
-  cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  a.trace = g_trace;
+  auto kern = g_trace ? attn_fwd_kernel<D, true> : attn_fwd_kernel<D, false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return (int)e;
   dim3 grid(a.pair_heads ? (a.Sq + BQ - 1) / BQ : (a.Sq + 2 * BQ - 1) / (2 * BQ), a.pair_heads ? a.Hq / 2 : a.Hq,
             a.B);
-  attn_fwd_kernel<D><<<grid, kThreadsA, smem, st>>>(tq, tk, tv, a);
+  kern<<<grid, kThreadsA, smem, st>>>(tq, tk, tv, a);
   return (int)cudaGetLastError();
 }
 
@@ -482,3 +651,9 @@ NFB_API int nfb_attn_fwd(const void* q, const void* k, const void* v, void* o, f
   cudaStream_t st = (cudaStream_t)stream;
   return D == 64 ? launch_fwd<64>(tq, tk, tv, a, st) : launch_fwd<128>(tq, tk, tv, a, st);
 }
+
+// Profiling aid: counters [64] of uint64 that the next forward launches add their per-phase SM cycles
+// to (softmax warps 0-6: wait S, TMEM load, max, exp + P store, rescale + signal, epilogue wait,
+// epilogue store; MMA issuer 8-11: wait P, wait K/V, wait PV done, issue; producer 16-17: wait
+// slot, issue); nullptr switches it off.
+NFB_API void nfb_attn_fwd_trace(void* counters) { g_trace = reinterpret_cast<unsigned long long*>(counters); }

@@ -55,6 +55,7 @@ struct BwdArgs {
   __nv_bfloat16* dv;
   int64_t sdk_b, sdk_s, sdk_h, sdv_b, sdv_s, sdv_h;
   uint32_t* status;
+  unsigned long long* trace;   // per-phase cycle counters (traced instantiation only)
 };
 
 struct alignas(8) BwdShared {
@@ -85,7 +86,11 @@ struct LayoutB {
   static constexpr int kDO = kQ + kStages * kTile;
   static constexpr int kDS = kDO + kStages * kTile;
   static constexpr int kRow = kDS + T * T * 2;       // per stage: 128 lse2 + 128 delta floats
-  static constexpr int kS = kRow + kStages * 1024;
+  // D = 64: a separate dQ staging area (8 warps x 4 KB), so the next dS^T write need not wait for
+  // the TMA to have read the staged dQ; D = 128 stages dQ in the warp's own (consumed) dS^T rows
+  static constexpr bool kSepStage = D == 64;
+  static constexpr int kStage = kRow + kStages * 1024;
+  static constexpr int kS = kStage + (kSepStage ? 8 * 4096 : 0);
   static constexpr size_t kNeed = (size_t)kS + 256;   // + BwdShared
   // dynamic shared memory requested: the layout plus alignment slack, capped at the 227 KB limit
   // (the kernel checks at run time that the aligned layout fits what it was given)
@@ -189,7 +194,7 @@ __device__ __forceinline__ int first_qtile(const BwdArgs& a, int k0) {
   return q_first <= 0 ? 0 : q_first / T;
 }
 
-template <int D>
+template <int D, bool kTrace>
 __global__ void __launch_bounds__(kThreadsB, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                     const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
@@ -260,7 +265,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       for (int t = 0; t < n_tiles && ok; ++t) {
         const int st = t % NS;
         const int use = t / NS;                    // how often this stage was filled before
-        if (use >= 1 && !mbar_wait_sleep(&S->qdo_empty[st], (use - 1) & 1, abort_flag)) { ok = false; break; }
+        if (use >= 1 && !mbar_wait(&S->qdo_empty[st], (use - 1) & 1, abort_flag)) { ok = false; break; }
         const int h = hk * G + t / per_head;
         const int q0 = (i0 + t % per_head) * T;
         mbar_arrive_expect_tx(&S->qdo_full[st], 2 * L::kTile + 1024);
@@ -288,81 +293,101 @@ __global__ void __launch_bounds__(kThreadsB, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0 && n_tiles > 0) {
-      const uint32_t id_s = idesc_bf16(T, T, false, false);     // S^T, dP^T
-      const uint32_t id_kv = idesc_bf16(T, D, false, true);     // dV, dK: A K-major, B MN-major
-      const uint32_t id_q = idesc_bf16(T, D, true, true);       // dQ: A (dS^T) and B (K) MN-major
-      const uint32_t sk = smem_u32(smem + L::kK), sv = smem_u32(smem + L::kV);
-      const uint32_t sds = smem_u32(smem + L::kDS);
+      constexpr uint32_t id_s = idesc_bf16(T, T, false, false);     // S^T, dP^T
+      constexpr uint32_t id_kv = idesc_bf16(T, D, false, true);     // dV, dK: A K-major, B MN-major
+      constexpr uint32_t id_q = idesc_bf16(T, D, true, true);       // dQ: A (dS^T) and B (K) MN-major
+      // shared-memory descriptors computed once; tile offsets are added to the start-address field
+      const uint64_t dk = sw128_desc(smem_u32(smem + L::kK)), dv = sw128_desc(smem_u32(smem + L::kV));
+      const uint64_t dk_mn = mn_desc(smem_u32(smem + L::kK), 16384);
+      const uint64_t dq0 = sw128_desc(smem_u32(smem + L::kQ)), dq0_mn = mn_desc(smem_u32(smem + L::kQ), 16384);
+      const uint64_t ddo0 = sw128_desc(smem_u32(smem + L::kDO)), ddo0_mn = mn_desc(smem_u32(smem + L::kDO), 16384);
+      const uint64_t dds = sw128_desc(smem_u32(smem + L::kDS)), dds_mn = mn_desc(smem_u32(smem + L::kDS), 16384);
+      auto off = [](int bytes) { return (uint64_t)(bytes >> 4); };
       auto issue_s = [&](int t) {        // S^T = K Q_t^T
-        const uint32_t sq = smem_u32(smem + L::kQ + (t % NS) * L::kTile);
+        const uint64_t dq = dq0 + off((t % NS) * L::kTile);
 #pragma unroll
         for (int db = 0; db < kDB; ++db)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_bf16(tmem + L::cS, sw128_desc(sk + db * 16384 + kk * 32), sw128_desc(sq + db * 16384 + kk * 32),
-                      id_s, (db > 0 || kk > 0) ? 1u : 0u);
+            umma_bf16(tmem + L::cS, dk + off(db * 16384 + kk * 32), dq + off(db * 16384 + kk * 32), id_s,
+                      (db > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&S->s_full);
       };
       auto issue_dp = [&](int t) {       // dP^T = V dO_t^T
-        const uint32_t sdo = smem_u32(smem + L::kDO + (t % NS) * L::kTile);
+        const uint64_t ddo = ddo0 + off((t % NS) * L::kTile);
 #pragma unroll
         for (int db = 0; db < kDB; ++db)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_bf16(tmem + L::cDP, sw128_desc(sv + db * 16384 + kk * 32), sw128_desc(sdo + db * 16384 + kk * 32),
-                      id_s, (db > 0 || kk > 0) ? 1u : 0u);
+            umma_bf16(tmem + L::cDP, dv + off(db * 16384 + kk * 32), ddo + off(db * 16384 + kk * 32), id_s,
+                      (db > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&S->dp_full);
       };
-      bool ok = mbar_wait_sleep(&S->kv_full, 0u, abort_flag) && mbar_wait_sleep(&S->qdo_full[0], 0u, abort_flag);
+      PhaseClock<kTrace> pc;
+      pc.start();
+      bool ok = mbar_wait(&S->kv_full, 0u, abort_flag) && mbar_wait(&S->qdo_full[0], 0u, abort_flag);
+      pc.mark(1);
       if (ok) {
         tmem_fence_after();
         issue_s(0);
         issue_dp(0);
       }
+      pc.mark(4);
       for (int t = 0; t < n_tiles && ok; ++t) {
         const int st = t % NS;
-        const uint32_t sq = smem_u32(smem + L::kQ + st * L::kTile);
-        const uint32_t sdo = smem_u32(smem + L::kDO + st * L::kTile);
+        const uint64_t dq_mn = dq0_mn + off(st * L::kTile);
+        const uint64_t ddo_mn = ddo0_mn + off(st * L::kTile);
         // dV += P^T dO_t, P^T from TMEM (queries 0-63 at cS, 64-127 at cS + 64)
-        if (!mbar_wait_sleep(&S->p_ready, t & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&S->p_ready, t & 1, abort_flag)) { ok = false; break; }
+        pc.mark(0);
         tmem_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           umma_bf16_ts(tmem + L::cDV, tmem + L::cS + (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8),
-                       mn_desc(sdo + kk * 16 * 128, 16384), id_kv, (t > 0 || kk > 0) ? 1u : 0u);
+                       ddo_mn + off(kk * 16 * 128), id_kv, (t > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&S->dv_done);
+        pc.mark(4);
         if (t + 1 < n_tiles) {
           // S^T of the next step overwrites P^T: wait until the dV MMA has read it
-          if (!mbar_wait_sleep(&S->qdo_full[(t + 1) % NS], ((t + 1) / NS) & 1, abort_flag) ||
-              !mbar_wait_sleep(&S->dv_done, t & 1, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&S->qdo_full[(t + 1) % NS], ((t + 1) / NS) & 1, abort_flag)) { ok = false; break; }
+          pc.mark(1);
+          if (!mbar_wait(&S->dv_done, t & 1, abort_flag)) { ok = false; break; }
+          pc.mark(2);
           tmem_fence_after();
           issue_s(t + 1);
+          pc.mark(4);
         }
         // dK += dS^T Q_t
-        if (!mbar_wait_sleep(&S->ds_ready, t & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&S->ds_ready, t & 1, abort_flag)) { ok = false; break; }
+        pc.mark(3);
         tmem_fence_after();
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_bf16(tmem + L::cDK, sw128_desc(sds + kb * 16384 + kk * 32),
-                      mn_desc(sq + (kb * 64 + kk * 16) * 128, 16384), id_kv, (t > 0 || kb > 0 || kk > 0) ? 1u : 0u);
+            umma_bf16(tmem + L::cDK, dds + off(kb * 16384 + kk * 32), dq_mn + off((kb * 64 + kk * 16) * 128), id_kv,
+                      (t > 0 || kb > 0 || kk > 0) ? 1u : 0u);
         // dQ_t = dS K (D = 64: own columns, free once the compute warps drained dQ of t-1)
-        if (D == 64 && t >= 1 && !mbar_wait_sleep(&S->dq_free, (t - 1) & 1, abort_flag)) { ok = false; break; }
+        pc.mark(4);
+        if (D == 64 && t >= 1 && !mbar_wait(&S->dq_free, (t - 1) & 1, abort_flag)) { ok = false; break; }
+        pc.mark(5);
         tmem_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_bf16(tmem + L::cDQ, mn_desc(sds + kk * 16 * 128, 16384), mn_desc(sk + kk * 16 * 128, 16384), id_q,
-                    kk > 0 ? 1u : 0u);
+          umma_bf16(tmem + L::cDQ, dds_mn + off(kk * 16 * 128), dk_mn + off(kk * 16 * 128), id_q, kk > 0 ? 1u : 0u);
         umma_commit(&S->dq_full);
         umma_commit(&S->qdo_empty[st]);
+        pc.mark(4);
         if (t + 1 < n_tiles) {
           // D = 128: dQ_t occupies the dP^T columns until the compute warps have drained it
-          if (D == 128 && !mbar_wait_sleep(&S->dq_free, t & 1, abort_flag)) { ok = false; break; }
+          if (D == 128 && !mbar_wait(&S->dq_free, t & 1, abort_flag)) { ok = false; break; }
+          pc.mark(5);
           tmem_fence_after();
           issue_dp(t + 1);
+          pc.mark(4);
         }
       }
+      pc.flush(a.trace, 8);
       if (ok) umma_commit(&S->acc_full);
       if (!ok) {
         set_status(a.status, kTimeoutFlag, 141);
@@ -386,35 +411,41 @@ __global__ void __launch_bounds__(kThreadsB, 1)
     // staging box of its dQ blocks once the MMAs have consumed dS^T
     uint8_t* slice = smem + L::kDS + half * 16384 + quarter * 4096;
     uint8_t* drow = slice + lane * 128;
+    uint8_t* stage = L::kSepStage ? smem + L::kStage + (warp - 2) * 4096 : slice;   // dQ staging box
+    uint8_t* srow = stage + lane * 128;
     bool ok = true;
     int prev_h = 0, prev_q0 = 0;
+    PhaseClock<kTrace> pc;
+    pc.start();
     // dQ of the previous step: TMEM -> this warp's slice -> TMA reduce-add into the accumulator
     auto drain_dq = [&](int tt) -> bool {
-      const bool w = mbar_wait_sleep(&S->dq_full, tt & 1, abort_flag);
+      const bool w = mbar_wait(&S->dq_full, tt & 1, abort_flag);
       if (!compute_all(w)) return false;
+      pc.mark(2);
       tmem_fence_after();
 #pragma unroll
       for (int bx = 0; bx < D / 64; ++bx) {
         const int col = half * (D / 2) + bx * 32;
         float g[32];
         tmem_ld32(tmem + lane_off + L::cDQ + (uint32_t)col, g);
-        if (bx > 0) {
-          if (lane == 0) bulk_wait_read0();      // the previous box has been read out of the slice
+        if (bx > 0 || L::kSepStage) {
+          if (lane == 0) bulk_wait_read0();      // the previous box has been read out of the staging area
           __syncwarp();
         }
 #pragma unroll
         for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<float4*>(drow + ((c ^ (lane & 7)) << 4)) =
+          *reinterpret_cast<float4*>(srow + ((c ^ (lane & 7)) << 4)) =
               make_float4(g[4 * c], g[4 * c + 1], g[4 * c + 2], g[4 * c + 3]);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) {
-          tma_reduce_add_4d(&tdq, slice, col, prev_h, prev_q0 + quarter * 32, b);
+          tma_reduce_add_4d(&tdq, stage, col, prev_h, prev_q0 + quarter * 32, b);
           bulk_commit();
         }
       }
       tmem_fence_before();
       mbar_arrive(&S->dq_free);
+      pc.mark(3);
       return true;
     };
     for (int t = 0; t < n_tiles; ++t) {
@@ -424,9 +455,10 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       const float* lse2 = reinterpret_cast<const float*>(smem + L::kRow + st * 1024) + half * HC;
       const float* dlt = reinterpret_cast<const float*>(smem + L::kRow + st * 1024 + 512) + half * HC;
       // ---- P^T of step t ----
-      bool w = mbar_wait_sleep(&S->qdo_full[st], (t / NS) & 1, abort_flag);
-      w = w && mbar_wait_sleep(&S->s_full, t & 1, abort_flag);
+      bool w = mbar_wait(&S->qdo_full[st], (t / NS) & 1, abort_flag);
+      w = w && mbar_wait(&S->s_full, t & 1, abort_flag);
       if (!compute_all(w)) { ok = false; break; }
+      pc.mark(0);
       tmem_fence_after();
       float p[HC];
 #pragma unroll
@@ -436,11 +468,15 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       const bool full = key < a.Sk && (!a.causal || qb >= lim);
 #pragma unroll
       for (int c = 0; c < HC; c += 4) {
+        // one quad in four on the FMA pipe (ex2_poly), the rest on the SFU
         const float4 l4 = *reinterpret_cast<const float4*>(lse2 + c);
-        p[c] = ex2_approx(fmaf(p[c], a.scale_log2, -l4.x));
-        p[c + 1] = ex2_approx(fmaf(p[c + 1], a.scale_log2, -l4.y));
-        p[c + 2] = ex2_approx(fmaf(p[c + 2], a.scale_log2, -l4.z));
-        p[c + 3] = ex2_approx(fmaf(p[c + 3], a.scale_log2, -l4.w));
+        const float x0 = fmaf(p[c], a.scale_log2, -l4.x), x1 = fmaf(p[c + 1], a.scale_log2, -l4.y);
+        const float x2 = fmaf(p[c + 2], a.scale_log2, -l4.z), x3 = fmaf(p[c + 3], a.scale_log2, -l4.w);
+        if (((c >> 2) & 3) == 3) {
+          p[c] = ex2_poly(x0); p[c + 1] = ex2_poly(x1); p[c + 2] = ex2_poly(x2); p[c + 3] = ex2_poly(x3);
+        } else {
+          p[c] = ex2_approx(x0); p[c + 1] = ex2_approx(x1); p[c + 2] = ex2_approx(x2); p[c + 3] = ex2_approx(x3);
+        }
       }
       if (!full) {
 #pragma unroll
@@ -456,13 +492,15 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tmem_fence_before();
       mbar_arrive(&S->p_ready);
+      pc.mark(1);
       // ---- dQ of step t-1 (its MMAs ran while P of step t was computed) ----
       if (t >= 1 && !drain_dq(t - 1)) { ok = false; break; }
       // ---- dS^T = scale * P^T . (dP^T - Delta) of step t ----
-      w = mbar_wait_sleep(&S->dp_full, t & 1, abort_flag);
+      w = mbar_wait(&S->dp_full, t & 1, abort_flag);
       if (!compute_all(w)) { ok = false; break; }
+      pc.mark(4);
       tmem_fence_after();
-      if (t >= 1) {
+      if (t >= 1 && !L::kSepStage) {
         if (lane == 0) bulk_wait_read0();        // the slice's dQ boxes have been read
         __syncwarp();
       }
@@ -492,15 +530,17 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tmem_fence_before();
       mbar_arrive(&S->ds_ready);
+      pc.mark(5);
       prev_h = h;
       prev_q0 = q0;
     }
     if (ok && n_tiles > 0 && !drain_dq(n_tiles - 1)) ok = false;
     if (lane == 0) bulk_wait_all();              // every dQ reduce-add performed before the CTA exits
     __syncwarp();
+    pc.mark(6);
     // dK, dV rows (TMEM lane = key): this half's D/2 columns, written once
     if (ok && n_tiles > 0) {
-      bool w = mbar_wait_sleep(&S->acc_full, 0u, abort_flag);
+      bool w = mbar_wait(&S->acc_full, 0u, abort_flag);
       if (compute_all(w)) {
         tmem_fence_after();
         // tcgen05.ld is warp-collective: every lane loads, only rows of real keys are stored
@@ -534,6 +574,8 @@ __global__ void __launch_bounds__(kThreadsB, 1)
         *reinterpret_cast<uint4*>(dvr + c) = make_uint4(0u, 0u, 0u, 0u);
       }
     }
+    pc.mark(7);
+    pc.flush(a.trace, 0);
     if (!ok && lane == 0) {
       set_status(a.status, kTimeoutFlag, 142);
       S->abort = 1;
@@ -638,14 +680,19 @@ static int make_tmap_dq(CUtensorMap* m, const float* base, int Bn, int Sn, int H
   return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
 }
 
+// Per-phase cycle counters: when set (nfb_attn_bwd_trace), launches run the traced instantiation.
+static unsigned long long* g_trace = nullptr;
+
 template <int D>
 static int launch_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tdo,
-                      const CUtensorMap& tdq, const BwdArgs& a, cudaStream_t st) {
+                      const CUtensorMap& tdq, BwdArgs a, cudaStream_t st) {
   const size_t smem = LayoutB<D>::kBytes;
-  cudaError_t e = cudaFuncSetAttribute(attn_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  a.trace = g_trace;
+  auto kern = g_trace ? attn_bwd_kernel<D, true> : attn_bwd_kernel<D, false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return (int)e;
   dim3 grid((a.Sk + T - 1) / T, a.Hkv, a.B);
-  attn_bwd_kernel<D><<<grid, kThreadsB, smem, st>>>(tq, tk, tv, tdo, tdq, a);
+  kern<<<grid, kThreadsB, smem, st>>>(tq, tk, tv, tdo, tdq, a);
   return (int)cudaGetLastError();
 }
 
@@ -725,3 +772,9 @@ NFB_API int nfb_attn_bwd(const void* q, const void* k, const void* v, const void
                                                             sdq_[0], sdq_[1], sdq_[2]);
   return (int)cudaGetLastError();
 }
+
+// Profiling aid: counters [64] of uint64 that the next backward launches add their per-phase SM
+// cycles to (compute warps 0-7: wait S, P^T, wait dQ, dQ drain, wait dP, dS^T, final reduce-add
+// wait, dK/dV epilogue; MMA issuer 8-13: wait P^T, wait Q/dO, wait dV done, wait dS^T, issue, wait
+// dQ drained); nullptr switches it off.
+NFB_API void nfb_attn_bwd_trace(void* counters) { g_trace = reinterpret_cast<unsigned long long*>(counters); }

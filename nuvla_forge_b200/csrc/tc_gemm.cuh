@@ -230,6 +230,56 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 2^x on the FMA pipe (no SFU), for softmax kernels that would otherwise be bound by the SFU's
+// exp2 throughput. Range reduction x = n + f with n = round(x), found by adding 1.5 * 2^23 (the sum's
+// low mantissa bits then hold n) and f in [-1/2, 1/2]; 2^f from a degree-3 polynomial fitted to 2^f on
+// that interval (least squares on the relative error, reweighted toward equal ripple; maximum
+// relative error 7.5e-5 in fp32, far below a bf16 step); 2^n is added to the exponent field. Inputs
+// are clamped at -126 so the exponent cannot wrap: x <= -126 (and -inf) gives a value below 2^-125.
+constexpr float kExp2C0 = 0.999928057f;
+constexpr float kExp2C1 = 0.693260968f;
+constexpr float kExp2C2 = 0.242611125f;
+constexpr float kExp2C3 = 0.0551716648f;
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;                 // 1.5 * 2^23: round(x) in the low mantissa bits
+  const float f = x - (t - 12582912.f);           // in [-1/2, 1/2]
+  const float p = fmaf(fmaf(fmaf(kExp2C3, f, kExp2C2), f, kExp2C1), f, kExp2C0);
+  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
+}
+
+// Per-phase cycle accounting (a profiling aid, compiled in only when kOn): lane 0 of a warp adds the
+// SM cycles spent since its previous mark to one of 8 counters (constant slot indices keep them in
+// registers) and flushes them with one atomic add each into buf[base + slot] at the end.
+template <bool kOn>
+struct PhaseClock {
+  __device__ __forceinline__ void start() {}
+  __device__ __forceinline__ void mark(int) {}
+  __device__ __forceinline__ void flush(unsigned long long*, int) {}
+};
+template <>
+struct PhaseClock<true> {
+  long long t;
+  uint32_t acc[8];
+  __device__ __forceinline__ void start() {
+    t = clock64();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0;
+  }
+  __device__ __forceinline__ void mark(int slot) {
+    const long long n = clock64();
+    acc[slot] += (uint32_t)(n - t);
+    t = n;
+  }
+  __device__ __forceinline__ void flush(unsigned long long* buf, int base) {
+    if (buf != nullptr && (threadIdx.x & 31) == 0) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (acc[i]) atomicAdd(buf + base + i, (unsigned long long)acc[i]);
+    }
+  }
+};
+
 struct TileCoord { int m_blk, n_blk; };
 
 // Tile order: groups of `group` M-blocks; inside a group, N-major, so CTAs that
