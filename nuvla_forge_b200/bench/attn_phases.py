@@ -37,9 +37,39 @@ def _report(title, counters, phases, warps_of, ctas, steps):
             print(f"  {name:<32} {c[slot] / (warps_of[role] * ctas) / steps:10.0f} cycles/step")
 
 
+EVENTS = {10: "S0 issue", 11: "S1 issue", 12: "S0 issued", 13: "S1 issued", 20: "PV0 issue", 21: "PV1 issue",
+          22: "PV0 issued", 23: "PV1 issued", 30: "sm0 wait S", 31: "sm0 got S", 32: "sm0 max done",
+          33: "sm0 PV done", 34: "sm0 P ready", 40: "sm1 wait S", 41: "sm1 got S", 42: "sm1 max done",
+          43: "sm1 PV done", 44: "sm1 P ready"}
+
+
+def _timeline(counters, which):
+    c = counters.cpu().tolist()
+    ev = sorted(((v & 0xFFFFFFFFFFFF, v >> 48) for v in c[64:] if v))
+    n = len(ev)
+    if not ev:
+        return
+    t0 = ev[0][0]
+    print(f"{which}: timeline of the first CTA ({n} events, SM cycles)")
+    phase = ["wait S", "got S", "max done", "first-half P V done", "P ready", "first half of P stored"]
+    kinds = ["S issue", "S issued", "PV(keys 0-63) issue", "PV(keys 0-63) issued", "PV(keys 64-127) issue",
+             "PV(keys 64-127) issued"]
+    for t, code in ev:
+        if code >= 10000:
+            w, rest = divmod(code - 10000, 1000)
+            name = f"warp {w + 2} (tile {w // 4}) step {rest // 10}: {phase[rest % 10]}"
+        elif code >= 1000:
+            kind, rest = divmod(code - 1000, 100)
+            name = f"    MMA tile {rest // 50} step {rest % 50}: {kinds[kind]}"
+        else:
+            name = EVENTS.get(code, code)
+        print(f"  {t - t0:8d}  {name}")
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--shape", choices=sorted(SHAPES), default="vit")
+    ap.add_argument("--timeline", action="store_true", help="print the event timeline of the first CTA")
     args = ap.parse_args(argv)
     from .. import _native as nat
     from ..ops import flash_attn
@@ -64,7 +94,7 @@ def main(argv=None):
              {"softmax": 8, "mma": 1, "tma": 1}, pairs / nq),
             ("backward", lambda: flash_attn.attention_bwd(q, k, v, out, dout, lse, causal), bwd_ctas, BWD_PHASES,
              {"compute": 8, "mma": 1}, G * pairs / nk)):
-        counters = torch.zeros(64, dtype=torch.int64, device="cuda")
+        counters = torch.zeros(2048, dtype=torch.int64, device="cuda")
         lib = nat.lib()
         setter = lib.nfb_attn_fwd_trace if which == "forward" else lib.nfb_attn_bwd_trace
         setter(counters.data_ptr())
@@ -74,6 +104,11 @@ def main(argv=None):
         e1.record()
         torch.cuda.synchronize()
         setter(None)
+        if args.timeline:
+            _timeline(counters, which)
+        c = counters.cpu().tolist()
+        if which == "forward" and c[30]:
+            print(f"  mma issuer poll loop: {c[31] / c[30]:.0f} cycles per iteration ({c[30] / ctas:.0f} per CTA)")
         # one step: a key tile for both query tiles of a forward CTA; a (head, query tile) for a backward CTA
         _report(f"{which} {args.shape}: {e0.elapsed_time(e1):.3f} ms (traced), {ctas} CTAs, {steps:.1f} steps each",
                 counters, phases, warps, ctas, steps)

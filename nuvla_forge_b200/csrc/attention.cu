@@ -38,6 +38,12 @@ namespace attn {
 
 using namespace nfb::tc;
 
+#ifndef SEP_P_FOR_D64
+#define SEP_P_FOR_D64 0
+#endif
+#ifndef POLY_EXP_FWD
+#define POLY_EXP_FWD 0
+#endif
 constexpr int BQ = 128;          // queries per tile (TMEM lanes)
 constexpr int BKV = 128;         // keys per tile
 constexpr int kThreadsA = 320;   // producer, MMA, 2 x 4 softmax warps
@@ -57,12 +63,14 @@ struct AttnArgs {
 
 struct alignas(8) AttnShared {
   uint64_t q_full;
-  uint64_t kv_full[4];
-  uint64_t kv_empty[4];
+  uint64_t kv_full[6];
+  uint64_t kv_empty[6];
   uint64_t s_full[2];
   uint64_t s_free[2];          // 128 arrivals: the softmax has loaded S_t (separate-P layout)
-  uint64_t p_full[2];
-  uint64_t pv_done[2];
+  uint64_t p_full[2];          // P_t complete (separate-P layout: its second half, keys 64-127)
+  uint64_t pv_done[2];         // P_t V complete (separate-P layout: both halves)
+  uint64_t p_half[2];          // separate-P layout: first half of P_t (keys 0-63) stored
+  uint64_t pv_half[2];         // separate-P layout: the first half's P V complete
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -154,7 +162,7 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 template <int D>
 struct Layout {
   static constexpr int kDB = D / 64;                        // 64-column blocks of the head dim
-  static constexpr int kStages = D == 64 ? 4 : 2;
+  static constexpr int kStages = D == 64 ? 5 : 2;   // a K/V load takes several steps to land
   static constexpr int kQBytes = BQ * D * 2;                // one query tile
   static constexpr int kKBytes = BKV * D * 2;
   static constexpr int kVBytes = BKV * D * 2;
@@ -162,13 +170,15 @@ struct Layout {
   static constexpr int kQ = 0;
   static constexpr int kKV = kQ + 2 * kQBytes;
   static constexpr int kS = kKV + kStages * kStageBytes;
-  static constexpr size_t kBytes = (size_t)kS + 256 + 1024;   // AttnShared, alignment
+  static constexpr int kEv = kS + 256;                        // event buffer of the traced build (4 KB)
+  static constexpr size_t kBytes = (size_t)kEv + 8192 + 1024;   // AttnShared, events, alignment
   static_assert(kBytes <= 227 * 1024, "shared memory");
   static_assert(kBytes > 114 * 1024, "one CTA (and its 512 TMEM columns) per SM");
   // TMEM columns. D = 64: S_t | P_t (bf16 pairs) | O_t each tile, so the softmax frees S_t as soon as
   // it has loaded it and S_t of the next key tile is computed while it exponentiates. D = 128 (no room
   // for separate P): P_t is written over S_t, and the next S_t waits until P_t V has completed.
-  static constexpr bool kSepP = D == 64;
+  static constexpr bool kSepP = SEP_P_FOR_D64 && D == 64;
+  static constexpr bool kPolyExpFwd = POLY_EXP_FWD != 0;
   static constexpr uint32_t cS = 0;                          // + t * 128
   static constexpr uint32_t cP = kSepP ? 256 : 0;            // + t * (kSepP ? 64 : 128)
   static constexpr uint32_t cPStride = kSepP ? 64 : 128;
@@ -182,6 +192,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
   using L = Layout<D>;
   constexpr int NS = L::kStages;
   constexpr bool kSepP = L::kSepP;
+  constexpr bool kPolyExp = L::kPolyExpFwd;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   AttnShared* S = reinterpret_cast<AttnShared*>(smem + L::kS);
@@ -217,6 +228,8 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       mbar_init(&S->s_free[t], BQ);
       mbar_init(&S->p_full[t], BQ);
       mbar_init(&S->pv_done[t], 1);
+      mbar_init(&S->p_half[t], BQ);
+      mbar_init(&S->pv_half[t], 1);
     }
     mbar_init(&S->drain, 1);
     S->abort = 0;
@@ -250,7 +263,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       pc.start();
       for (int j = 0; j < n_max; ++j) {
         const int st = j % NS;
-        if (j >= NS && !mbar_wait(&S->kv_empty[st], ((j / NS) - 1) & 1, abort_flag)) { ok = false; break; }
+        if (j >= NS && !mbar_wait_sleep(&S->kv_empty[st], ((j / NS) - 1) & 1, abort_flag)) { ok = false; break; }
         pc.mark(0);
         mbar_arrive_expect_tx(&S->kv_full[st], L::kStageBytes);
         uint8_t* ks = smem + L::kKV + st * L::kStageBytes;
@@ -287,16 +300,59 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       const uint64_t dv0 = sw128_mn_desc(smem_u32(smem + L::kKV + L::kKBytes));
       PhaseClock<kTrace> pc;
       pc.start();
+      pc.bind_events(reinterpret_cast<uint64_t*>(smem + L::kEv), 256);
       bool ok = mbar_wait(&S->q_full, 0u, abort_flag);
       pc.mark(1);
-      int js[2] = {0, 0}, jp[2] = {0, 0};     // next S / next PV per tile
+      int js[2] = {0, 0}, jp[2] = {0, 0};     // next S / next PV (its second half) per tile
+      int ja[2] = {0, 0};                     // next first-half PV per tile (separate-P layout)
       int kv_ready = -1, released = 0;
       uint32_t idle = 0;
       uint64_t t_idle = 0;
       auto try_tile = [&](const int t) -> bool {
         bool progress = false;
         const int n = t ? n1 : n0;
-        if (js[t] < n) {
+        // P V first (the softmax waits for it before it writes the next P), in two halves of 64 keys
+        // so that the first half runs while the softmax still exponentiates the second
+        if (ja[t] < js[t] && ja[t] == jp[t] && mbar_test(&S->p_half[t], ja[t] & 1)) {
+          const int j = ja[t];
+          pc.event(a.trace, 1000 + 2 * 100 + t * 50 + j);
+          tmem_fence_after();
+          const uint64_t dv = dv0 + (uint64_t)(((j % NS) * L::kStageBytes) >> 4);
+          const uint32_t t_p = tmem_base + L::cP + (uint32_t)(t * L::cPStride);
+          const uint32_t t_o = tmem_base + L::cO + (uint32_t)(t * D);
+#pragma unroll
+          for (int kk = 0; kk < BKV / 32; ++kk)
+            umma_bf16_ts(t_o, t_p + (uint32_t)(kk * 8),
+                         dv + (uint64_t)(((kk >> 2) * L::kDB * 8192 + (kk & 3) * 16 * 128) >> 4), id_o,
+                         (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&S->pv_half[t]);
+          pc.event(a.trace, 1000 + 3 * 100 + t * 50 + j);
+          ++ja[t];
+          progress = true;
+        }
+        if (jp[t] < ja[t] && mbar_test(&S->p_full[t], jp[t] & 1)) {
+          const int j = jp[t];
+          pc.event(a.trace, 1000 + 4 * 100 + t * 50 + j);
+          tmem_fence_after();
+          const uint64_t dv = dv0 + (uint64_t)(((j % NS) * L::kStageBytes) >> 4);
+          const uint32_t t_p = tmem_base + L::cP + (uint32_t)(t * L::cPStride);
+          const uint32_t t_o = tmem_base + L::cO + (uint32_t)(t * D);
+#pragma unroll
+          for (int kk = BKV / 32; kk < BKV / 16; ++kk)
+            umma_bf16_ts(t_o, t_p + (uint32_t)(kk * 8),
+                         dv + (uint64_t)(((kk >> 2) * L::kDB * 8192 + (kk & 3) * 16 * 128) >> 4), id_o, 1u);
+          umma_commit(&S->pv_done[t]);
+          pc.event(a.trace, 1000 + 5 * 100 + t * 50 + j);
+          ++jp[t];
+          progress = true;
+          // a K/V stage is free once every tile that reads it has issued its P V
+          while (released < n_max && (jp[0] > released || n0 <= released) && (jp[1] > released || n1 <= released)) {
+            umma_commit(&S->kv_empty[released % NS]);
+            ++released;
+          }
+        }
+        // S_t at most one key tile ahead of the tile's next P V: the softmax needs P V(j) before S(j+2)
+        if (js[t] < n && js[t] <= jp[t] + 1) {
           const int j = js[t];
           bool ready = true;
           if (kv_ready < j) {
@@ -308,6 +364,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
           if (ready && j > 0)
             ready = kSepP ? mbar_test(&S->s_free[t], (j - 1) & 1) : mbar_test(&S->pv_done[t], (j - 1) & 1);
           if (ready) {
+            pc.event(a.trace, 1000 + 0 * 100 + t * 50 + j);
             tmem_fence_after();
             const uint64_t da = dq0 + (uint64_t)((t * L::kQBytes) >> 4);
             const uint64_t db_ = dk0 + (uint64_t)(((j % NS) * L::kStageBytes) >> 4);
@@ -319,28 +376,9 @@ __global__ void __launch_bounds__(kThreadsA, 1)
                 umma_bf16(t_s, da + (uint64_t)((db * 16384 + kk * 32) >> 4),
                           db_ + (uint64_t)((db * 16384 + kk * 32) >> 4), id_s, (db > 0 || kk > 0) ? 1u : 0u);
             umma_commit(&S->s_full[t]);
+            pc.event(a.trace, 1000 + 1 * 100 + t * 50 + j);
             ++js[t];
             progress = true;
-          }
-        }
-        if (jp[t] < js[t] && mbar_test(&S->p_full[t], jp[t] & 1)) {
-          const int j = jp[t];
-          tmem_fence_after();
-          const uint64_t dv = dv0 + (uint64_t)(((j % NS) * L::kStageBytes) >> 4);
-          const uint32_t t_p = tmem_base + L::cP + (uint32_t)(t * L::cPStride);
-          const uint32_t t_o = tmem_base + L::cO + (uint32_t)(t * D);
-#pragma unroll
-          for (int kk = 0; kk < BKV / 16; ++kk)
-            umma_bf16_ts(t_o, t_p + (uint32_t)(kk * 8),
-                         dv + (uint64_t)(((kk >> 2) * L::kDB * 8192 + (kk & 3) * 16 * 128) >> 4), id_o,
-                         (j > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&S->pv_done[t]);
-          ++jp[t];
-          progress = true;
-          // a K/V stage is free once every tile that reads it has issued its P V
-          while (released < n_max && (jp[0] > released || n0 <= released) && (jp[1] > released || n1 <= released)) {
-            umma_commit(&S->kv_empty[released % NS]);
-            ++released;
           }
         }
         return progress;
@@ -406,7 +444,10 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         jp[0] = n0;
         jp[1] = n1;
       }
+      uint32_t iters = 0;
+      const long long loop_t0 = clock64();
       while (ok && (jp[0] < n0 || jp[1] < n1)) {
+        if (kTrace) ++iters;
         const bool p0 = try_tile(0);
         const bool p1 = try_tile(1);
         if (p0 || p1) {
@@ -421,7 +462,11 @@ __global__ void __launch_bounds__(kThreadsA, 1)
           if (*abort_flag) ok = false;
         }
       }
-      pc.flush(a.trace, 8);
+      if (kTrace && a.trace != nullptr) {
+        atomicAdd(a.trace + 30, (unsigned long long)iters);
+        atomicAdd(a.trace + 31, (unsigned long long)(clock64() - loop_t0));
+      }
+      pc.flush(a.trace, 8, 0);
       if (!ok) {
         set_status(a.status, kTimeoutFlag, 121);
         S->abort = 1;
@@ -448,9 +493,12 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     bool ok = true;
     PhaseClock<kTrace> pc;
     pc.start();
+    pc.bind_events(reinterpret_cast<uint64_t*>(smem + L::kEv) + 256 + (warp - 2) * 96, 96);
     for (int j = 0; j < n; ++j) {
+      pc.event(a.trace, 10000 + (warp - 2) * 1000 + j * 10 + 0);
       if (!__all_sync(0xffffffffu, mbar_wait(&S->s_full[t], j & 1, abort_flag))) { ok = false; break; }
       pc.mark(0);
+      pc.event(a.trace, 10000 + (warp - 2) * 1000 + j * 10 + 1);
       tmem_fence_after();
       float s[BKV];
       {
@@ -485,33 +533,14 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         m = mt;
       }
       const float m_use = m == -INFINITY ? 0.f : m;
-      // P_t(j-1) V and O_t: the previous P V must have completed before P_t and O_t are written
-      // (with P over S it completed before S_t(j) was issued)
-      if (kSepP && j > 0) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&S->pv_done[t], (j - 1) & 1, abort_flag))) { ok = false; break; }
-        tmem_fence_after();
-      }
       pc.mark(2);
-      float sm[4] = {0.f, 0.f, 0.f, 0.f};                  // row sum in 4 independent chains
-#pragma unroll
-      for (int c0 = 0; c0 < BKV; c0 += 32) {
-        uint32_t p[16];
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          // one pair in four on the FMA pipe, the rest on the SFU (the SFU alone bounds this loop)
-          const bool poly = ((c >> 1) & 3) == 3;
-          const float x0 = fmaf(s[c0 + c], a.scale_log2, -m_use), x1 = fmaf(s[c0 + c + 1], a.scale_log2, -m_use);
-          const float e0 = poly ? ex2_poly(x0) : ex2_approx(x0);
-          const float e1 = poly ? ex2_poly(x1) : ex2_approx(x1);
-          sm[(c >> 1) & 3] += e0 + e1;
-          p[c >> 1] = pack_bf16(e0, e1);
-        }
-        tmem_st16_nowait(t_p + (uint32_t)(c0 >> 1), p);   // 32 probabilities = 16 packed columns
-      }
-      const float sum = (sm[0] + sm[1]) + (sm[2] + sm[3]);
-      pc.mark(3);
-      l = l * alpha + sum;
+      // O_t is rescaled only on a large max jump; with separate P the previous P V must have
+      // completed first (with P over S it completed before S_t(j) was issued)
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        if (kSepP) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&S->pv_done[t], (j - 1) & 1, abort_flag))) { ok = false; break; }
+          tmem_fence_after();
+        }
 #pragma unroll 1
         for (int c = 0; c < D; c += 32) {
           float o[32];
@@ -522,10 +551,56 @@ __global__ void __launch_bounds__(kThreadsA, 1)
           tmem_st32_nowait(t_o + (uint32_t)c, ou);
         }
       }
+      pc.event(a.trace, 10000 + (warp - 2) * 1000 + j * 10 + 2);
+      float sm[4] = {0.f, 0.f, 0.f, 0.f};                  // row sum in 4 independent chains
+      // exponentiate 32 keys, store them as 16 packed bf16 pairs of P_t
+      auto exp_store = [&](const int c0) {
+        uint32_t p[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          // optionally one pair in four on the FMA pipe (ex2_poly), the rest on the SFU
+          const bool poly = kPolyExp && ((c >> 1) & 3) == 3;
+          const float x0 = fmaf(s[c0 + c], a.scale_log2, -m_use), x1 = fmaf(s[c0 + c + 1], a.scale_log2, -m_use);
+          const float e0 = poly ? ex2_poly(x0) : ex2_approx(x0);
+          const float e1 = poly ? ex2_poly(x1) : ex2_approx(x1);
+          sm[(c >> 1) & 3] += e0 + e1;
+          p[c >> 1] = pack_bf16(e0, e1);
+        }
+        tmem_st16_nowait(t_p + (uint32_t)(c0 >> 1), p);
+      };
+      if (kSepP) {
+        // two halves of 64 keys: each may overwrite its half of P_t(j-1) once that half's P V has
+        // read it, and the first half's P V starts while the second half is exponentiated
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          if (j > 0) {
+            uint64_t* bar = half == 0 ? &S->pv_half[t] : &S->pv_done[t];
+            if (!__all_sync(0xffffffffu, mbar_wait(bar, (j - 1) & 1, abort_flag))) { ok = false; break; }
+            tmem_fence_after();
+          }
+          if (half == 0) pc.event(a.trace, 10000 + (warp - 2) * 1000 + j * 10 + 3);
+          exp_store(half * 64);
+          exp_store(half * 64 + 32);
+          if (half == 0) {
+            tmem_wait_st();
+            tmem_fence_before();
+            mbar_arrive(&S->p_half[t]);
+            pc.event(a.trace, 10000 + (warp - 2) * 1000 + j * 10 + 5);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int c0 = 0; c0 < BKV; c0 += 32) exp_store(c0);
+      }
+      if (!ok) break;
+      const float sum = (sm[0] + sm[1]) + (sm[2] + sm[3]);
+      pc.mark(3);
+      l = l * alpha + sum;
       tmem_wait_st();
       tmem_fence_before();
       mbar_arrive(&S->p_full[t]);
       pc.mark(4);
+      pc.event(a.trace, 10000 + (warp - 2) * 1000 + j * 10 + 4);
     }
     if (!ok) {
       if (lane == 0) {
@@ -570,7 +645,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         S->abort = 1;
       }
     }
-    pc.flush(a.trace, 0);
+    pc.flush(a.trace, 0, 256 + (warp - 2) * 96);
   }
 
   tmem_fence_before();
@@ -652,8 +727,9 @@ NFB_API int nfb_attn_fwd(const void* q, const void* k, const void* v, void* o, f
   return D == 64 ? launch_fwd<64>(tq, tk, tv, a, st) : launch_fwd<128>(tq, tk, tv, a, st);
 }
 
-// Profiling aid: counters [64] of uint64 that the next forward launches add their per-phase SM cycles
+// Profiling aid: counters [1024] of uint64; the next forward launches add their per-phase SM cycles
 // to (softmax warps 0-6: wait S, TMEM load, max, exp + P store, rescale + signal, epilogue wait,
 // epilogue store; MMA issuer 8-11: wait P, wait K/V, wait PV done, issue; producer 16-17: wait
-// slot, issue); nullptr switches it off.
+// slot, issue) and, from slot 64 on, a timeline of the first CTA's events (slot 63 counts them);
+// nullptr switches it off.
 NFB_API void nfb_attn_fwd_trace(void* counters) { g_trace = reinterpret_cast<unsigned long long*>(counters); }

@@ -773,7 +773,7 @@ NFB_API int nfb_attn_bwd(const void* q, const void* k, const void* v, const void
   return (int)cudaGetLastError();
 }
 
-// Profiling aid: counters [64] of uint64 that the next backward launches add their per-phase SM
+// Profiling aid: counters [1024] of uint64; the next backward launches add their per-phase SM
 // cycles to (compute warps 0-7: wait S, P^T, wait dQ, dQ drain, wait dP, dS^T, final reduce-add
 // wait, dK/dV epilogue; MMA issuer 8-13: wait P^T, wait Q/dO, wait dV done, wait dS^T, issue, wait
 // dQ drained); nullptr switches it off.

@@ -160,8 +160,9 @@ NFB_EXPORT int nfb_attn_fwd(const void* q, const void* k, const void* v, void* o
  * the forward's lse. strides: 24 element strides, (batch, token, head) of q, k, v, o, do, dq, dk, dv.
  * scratch: nfb_attn_bwd_scratch_bytes(B, Sq, Hq, D) bytes (16-byte aligned). Three launches. */
 NFB_EXPORT int64_t nfb_attn_bwd_scratch_bytes(int B, int Sq, int Hq, int D);
-/* Profiling aid: 64 uint64 device counters that later forward / backward launches add per-phase SM
- * cycles to (nullptr: off, the default). */
+/* Profiling aid: 1024 uint64 device counters that later forward / backward launches add per-phase SM
+ * cycles to (slots 0-31), with an event timeline of the first CTA from slot 64 (nullptr: off, the
+ * default). */
 NFB_EXPORT void nfb_attn_fwd_trace(void* counters);
 NFB_EXPORT void nfb_attn_bwd_trace(void* counters);
 NFB_EXPORT int nfb_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,

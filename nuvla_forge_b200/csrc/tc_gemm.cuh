@@ -255,12 +255,16 @@ template <bool kOn>
 struct PhaseClock {
   __device__ __forceinline__ void start() {}
   __device__ __forceinline__ void mark(int) {}
-  __device__ __forceinline__ void flush(unsigned long long*, int) {}
+  __device__ __forceinline__ void bind_events(uint64_t*, int) {}
+  __device__ __forceinline__ void event(unsigned long long*, int) {}
+  __device__ __forceinline__ void flush(unsigned long long*, int, int = 0) {}
 };
 template <>
 struct PhaseClock<true> {
   long long t;
   uint32_t acc[8];
+  uint64_t* ev = nullptr;      // shared-memory event buffer of this role (first CTA only)
+  int n_ev = 0, cap = 0;
   __device__ __forceinline__ void start() {
     t = clock64();
 #pragma unroll
@@ -271,11 +275,24 @@ struct PhaseClock<true> {
     acc[slot] += (uint32_t)(n - t);
     t = n;
   }
-  __device__ __forceinline__ void flush(unsigned long long* buf, int base) {
+  // timeline of the first CTA: lane 0 appends (code << 48 | SM clock) to a shared-memory buffer
+  __device__ __forceinline__ void bind_events(uint64_t* buf, int capacity) {
+    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
+      ev = buf;
+      cap = capacity;
+    }
+  }
+  __device__ __forceinline__ void event(unsigned long long*, int code) {
+    if (ev != nullptr && (threadIdx.x & 31) == 0 && n_ev < cap)
+      ev[n_ev++] = ((uint64_t)code << 48) | ((uint64_t)clock64() & 0xFFFFFFFFFFFFull);
+  }
+  // counters into buf[base + slot]; events (if bound) into buf[64 + ev_off + i]
+  __device__ __forceinline__ void flush(unsigned long long* buf, int base, int ev_off = 0) {
     if (buf != nullptr && (threadIdx.x & 31) == 0) {
 #pragma unroll
       for (int i = 0; i < 8; ++i)
         if (acc[i]) atomicAdd(buf + base + i, (unsigned long long)acc[i]);
+      for (int i = 0; i < n_ev; ++i) buf[64 + ev_off + i] = ev[i];
     }
   }
 };
