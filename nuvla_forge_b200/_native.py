@@ -68,6 +68,7 @@ _SIGS: dict[str, tuple] = {
     "nfb_attn_fwd": (I, [P, P, P, P, P, I, I, I, I, I, I, L, L, L, L, L, L, L, L, L, L, L, L, I, F, P, P]),
     "nfb_attn_bwd_scratch_bytes": (L, [I, I, I, I]),
     "nfb_attn_fwd_trace": (None, [P]),
+    "nfb_mma_rate": (I, [I, I, I, P, I, P]),
     "nfb_attn_bwd_trace": (None, [P]),
     "nfb_attn_bwd": (I, [P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, P, I, F, P, P]),
     "nfb_ce_tc_tiles": (I, [I]),

@@ -164,6 +164,9 @@ NFB_EXPORT int64_t nfb_attn_bwd_scratch_bytes(int B, int Sq, int Hq, int D);
  * cycles to (slots 0-31), with an event timeline of the first CTA from slot 64 (nullptr: off, the
  * default). */
 NFB_EXPORT void nfb_attn_fwd_trace(void* counters);
+/* Hardware characterisation: SM cycles of `iters` back-to-back M128 x n x K16 bf16 tcgen05.mma on
+ * every SM (mode 0: operands K-major in shared memory; 1: B MN-major; 2: A from TMEM, B MN-major). */
+NFB_EXPORT int nfb_mma_rate(int mode, int n, int iters, unsigned long long* out, int sms, void* stream);
 NFB_EXPORT void nfb_attn_bwd_trace(void* counters);
 NFB_EXPORT int nfb_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
                             const float* lse, void* dq, void* dk, void* dv, void* scratch, int B, int Sq, int Sk,
