@@ -95,6 +95,7 @@ class _Unit:
     acc32: torch.Tensor | None = None
     acc_fresh: bool = True
     pending: int = 0
+    seen: set = field(default_factory=set)   # parameters whose gradient of this backward arrived
     ready: bool = False
     launched: bool = False
     bwd_gathered: bool = False
@@ -203,6 +204,10 @@ class FullyShardedDataParallel(nn.Module):
                 s.param.register_post_accumulate_grad_hook(self._grad_hook)
                 self._unit_of[id(s.param)] = u
                 self._seg_of[id(s.param)] = s
+                if s.param.dim() == 2:
+                    # the native linear backward writes this weight's fp32 gradient straight into the
+                    # unit's accumulator (grad_target / grad_done); autograd then receives none
+                    s.param._nfb_grad_owner = self
         for u in self.units[:-1]:
             self._wrap_unit(u)
         self.module.register_forward_pre_hook(self._root_pre_forward)
@@ -512,7 +517,15 @@ class FullyShardedDataParallel(nn.Module):
 
     def _grad_hook(self, p: nn.Parameter) -> None:
         if p.grad is None:
-            return
+            return                 # its gradient went to grad_target, or it received none
+        acc = self.grad_target(p)[0]
+        acc.add_(p.grad.reshape(-1))
+        p.grad = None
+        self.grad_done(p)
+
+    # gradient owner protocol (ops/linear.py:weight_grad): fp32 buffer + overwrite flag, then done
+    def grad_target(self, p: nn.Parameter):
+        """(``p``'s segment of its unit's fp32 gradient accumulator, overwrite?) for this backward."""
         if not self._callback_queued:
             self._callback_queued = True
             self._rs_order = list(reversed(self._order)) + [self.root]
@@ -525,8 +538,15 @@ class FullyShardedDataParallel(nn.Module):
             u.acc32.zero_()      # new window: parameters without a gradient contribute zeros
         u.acc_fresh = False
         seg = self._seg_of[id(p)]
-        u.acc32[seg.start: seg.start + seg.numel].add_(p.grad.reshape(-1))
-        p.grad = None
+        return u.acc32[seg.start: seg.start + seg.numel], False
+
+    def grad_done(self, p: nn.Parameter) -> None:
+        """``p``'s gradient of this backward is in its unit's accumulator."""
+        u = self._unit_of[id(p)]
+        if id(p) in u.seen:
+            raise RuntimeError(f"parameter {self._seg_of[id(p)].name} received a second gradient in one backward; "
+                               "its unit may already be reduce-scattered")
+        u.seen.add(id(p))
         u.pending -= 1
         if u.pending == 0:
             u.ready = True
@@ -637,6 +657,7 @@ class FullyShardedDataParallel(nn.Module):
                 main.wait_stream(self.comm_stream)
         for u in self.units:
             u.pending = len(u.segs)
+            u.seen = set()
             u.ready = False
             u.launched = False
             self._reshard(u)
@@ -841,6 +862,7 @@ class _AgLinear(torch.autograd.Function):
         y = torch.empty((x2.shape[0], w.shape[0]), dtype=x.dtype, device=x.device)
         fsdp._launch_ag_gemm(u, x2, w, y)
         ctx.save_for_backward(x, w)
+        ctx.w_ref = w          # the Parameter itself: its gradient owner is an attribute
         return y.view(*x.shape[:-1], w.shape[0])
 
     @staticmethod
@@ -857,7 +879,7 @@ class _AgLinear(torch.autograd.Function):
         if ctx.needs_input_grad[0]:
             gx = (linear_op.input_grad(gy2, w) if native else gy2 @ w).view(x.shape)
         if ctx.needs_input_grad[1]:
-            gw = linear_op.weight_grad(gy2, x2, w) if native else gy2.t() @ x2
+            gw = linear_op.weight_grad(gy2, x2, ctx.w_ref) if native else gy2.t() @ x2
         return gx, gw, None, None
 
 

@@ -60,9 +60,9 @@ def _fsdp_train(rank, world, steps, accum, no_sync, clip):
     return None
 
 
-def _reference(world, steps, accum, clip):
+def _reference(world, steps, accum, clip, make=None):
     torch.manual_seed(0)
-    net = Net()
+    net = make() if make is not None else Net()
     opt = torch.optim.AdamW(net.parameters(), lr=1e-2, weight_decay=0.01)
     for step in range(steps):
         opt.zero_grad()
@@ -202,3 +202,85 @@ def test_fsdp_rs_adamw_host_path_matches_flat_step():
     assert steps_a == steps_b == 3 and fused_a == 3 and fused_b == 0
     for n, t in pb.items():
         assert torch.allclose(pa[n], t, rtol=1e-5, atol=1e-6), n
+
+
+class _OwnerLinearFn(torch.autograd.Function):
+    """The native linear's gradient contract on CPU: dW (fp32) goes to the weight's gradient owner."""
+
+    @staticmethod
+    def forward(ctx, x, w, b):
+        ctx.save_for_backward(x, w)
+        ctx.w_ref = w
+        return x @ w.t() + b
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        dy2, x2 = dy.reshape(-1, dy.shape[-1]), x.reshape(-1, x.shape[-1])
+        owner = getattr(ctx.w_ref, "_nfb_grad_owner", None)
+        gw = dy2.t().float() @ x2.float()
+        if owner is not None:
+            buf, overwrite = owner.grad_target(ctx.w_ref)
+            buf.view(w.shape).copy_(gw) if overwrite else buf.view(w.shape).add_(gw)
+            owner.grad_done(ctx.w_ref)
+            gw = None
+        return dy @ w, gw, dy2.sum(0)
+
+
+class OwnerLinear(nn.Linear):
+    def forward(self, x):
+        return _OwnerLinearFn.apply(x, self.weight, self.bias)
+
+
+class OwnerBlock(Block):
+    def __init__(self, d):
+        super().__init__(d)
+        self.a, self.b = OwnerLinear(d, 2 * d), OwnerLinear(2 * d, d)
+
+
+class OwnerNet(Net):
+    def __init__(self, twice=False):
+        super().__init__()
+        self.blocks = nn.ModuleList([OwnerBlock(16) for _ in range(3)])
+        self.twice = twice
+
+    def forward(self, x):
+        h = self.inp(x)
+        for b in self.blocks:
+            h = b(b(h)) if self.twice else b(h)
+        return self.out(h)
+
+
+def _fsdp_owner_train(rank, world, steps, accum, twice=False):
+    from nuvla_forge_b200.parallel.fsdp import FullyShardedDataParallel
+
+    torch.manual_seed(0)
+    net = OwnerNet(twice)
+    fsdp = FullyShardedDataParallel(net, unit_types=(Block,))
+    assert all(getattr(p, "_nfb_grad_owner", None) is fsdp for p in net.parameters() if p.dim() == 2)
+    opt = fsdp.make_optimizer(lr=1e-2, weight_decay=0.01, max_grad_norm=0.5)
+    for step in range(steps):
+        for m in range(accum):
+            x, y = _data(step, rank, m)
+            ctx = fsdp.no_sync() if m < accum - 1 else torch.enable_grad()
+            with ctx:
+                (((fsdp(x) - y) ** 2).mean() / accum).backward()
+        opt.step()
+        opt.zero_grad()
+    views = fsdp.full_master_views()
+    if rank == 0:
+        return {n: views[id(p)].clone() for n, p in net.named_parameters()}
+    return None
+
+
+def test_fsdp_gradient_owner_protocol_matches_single_process():
+    """Weights whose backward writes dW into FSDP's accumulator (as the native linear does) train
+    exactly like autograd gradients, with no_sync accumulation and the global clip."""
+    out = run_ranks(_fsdp_owner_train, 2, args=(3, 2))
+    _check(out, _reference(2, 3, 2, 0.5, make=OwnerNet))
+
+
+def test_fsdp_gradient_owner_rejects_a_second_gradient():
+    out = run_ranks(_fsdp_owner_train, 2, args=(1, 1, True))
+    assert all(st != "ok" for st, _ in out.values()), out
+    assert all("second gradient" in str(msg) for _, msg in out.values()), out
