@@ -94,7 +94,9 @@ def main(argv=None):
         n = nbytes // 2
         n -= n % (8 * world)
         shard = n // world
-        ctas = args.ctas or (16 if nbytes <= 1 << 20 else 64 if nbytes <= 16 << 20 else 132)
+        # measured on 2 B200s (reports/comms_n2_ctas.json): above 16 MB the fused kernels need ~256
+        # CTAs to approach the link rate (all-reduce 145 -> 435 GB/s bus bandwidth from 32 to 256)
+        ctas = args.ctas or (16 if nbytes <= 1 << 20 else 64 if nbytes <= 4 << 20 else 132 if nbytes <= 16 << 20 else 256)
         it = args.iters if nbytes < 256 << 20 else max(5, args.iters // 4)
         s = nat.stream(dev)
         # fused all-reduce: fp32 in/out, bf16 wire
