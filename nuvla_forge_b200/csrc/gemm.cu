@@ -51,19 +51,19 @@ static ClusterCache g_cc;
 static std::mutex g_cc_mu;
 
 template <class K>
-static int max_clusters(K kernel, int* out) {
+static int max_clusters(K kernel, int* out, size_t smem_bytes) {
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(g_cc_mu);
   for (int i = 0; i < g_cc.n; ++i) {
     if (g_cc.fn[i] == (const void*)kernel && g_cc.dev[i] == dev) { *out = g_cc.clusters[i]; return 0; }
   }
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes);
   if (e != cudaSuccess) return (int)e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * 74, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.dynamicSmemBytes = smem_bytes;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
@@ -155,6 +155,23 @@ static int output_map(CUtensorMap* m, const void* C, int M, int N, int64_t ldc) 
   return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
 }
 
+// Map for the SwiGLU-backward epilogue: bf16 [M, N] with row stride ldc, 32-row x 64-column boxes
+// (128-byte rows), 128-byte swizzle.
+static int output_map_wide(CUtensorMap* m, const void* C, int M, int N, int64_t ldc) {
+  int rc = tc::get_encode();
+  if (rc) return rc;
+  rc = tc::bind_device_of(C);
+  if (rc) return rc;
+  cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+  cuuint64_t strides[1] = {(cuuint64_t)(ldc * 2)};
+  cuuint32_t box[2] = {64, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = tc::g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(C), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
+}
+
 template <class Epi, bool A_MN, bool B_MN>
 static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Work w, const Epi& epi, uint32_t* status,
                   cudaStream_t st, const CUtensorMap* tc_map = nullptr, const CUtensorMap* td_map = nullptr) {
@@ -169,12 +186,12 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Work w
   if (rc) return gemm_fail(rc, "tensor map of B");
   auto kern = gemm_pair_kernel<Epi, A_MN, B_MN>;
   int clusters = 0;
-  rc = max_clusters(kern, &clusters);
+  rc = max_clusters(kern, &clusters, smem_bytes_for<Epi>());
   if (rc) return gemm_fail(rc, "cluster occupancy query");
   const int grid_clusters = w.items < clusters ? w.items : clusters;
   cudaError_t pending = cudaGetLastError();     // an error left by an earlier call of this thread
   if (pending != cudaSuccess) return gemm_fail((int)pending, "error pending before the launch");
-  kern<<<2 * grid_clusters, kThreads, kSmemBytes, st>>>(ta, tb, tcm, tdm, w, epi, status);
+  kern<<<2 * grid_clusters, kThreads, smem_bytes_for<Epi>(), st>>>(ta, tb, tcm, tdm, w, epi, status);
   rc = (int)cudaGetLastError();
   return rc ? gemm_fail(rc, "kernel launch") : 0;
 }
@@ -225,7 +242,7 @@ NFB_API int nfb_gemm_acc(const void* A, const void* B, float* C, int M, int N, i
   const int tiles = w.m_tiles * w.n_tiles;
   if (splits <= 0) {
     int clusters = 0;
-    int rc = max_clusters(gemm_pair_kernel<AccumF32Epi, true, true>, &clusters);
+    int rc = max_clusters(gemm_pair_kernel<AccumF32Epi, true, true>, &clusters, smem_bytes_for<AccumF32Epi>());
     if (rc) return rc;
     splits = choose_splits(tiles, w.k_blocks, clusters);
   }
@@ -274,12 +291,13 @@ NFB_API int nfb_gemm_swiglu_bwd(const void* dY, const void* Wd, const void* ab, 
   if (D <= 0 || F <= 0 || F % 128) return gemm_fail((int)cudaErrorInvalidValue, "swiglu: F must be a multiple of 128");
   if (!al16(ab) || (ldab * 2) % 16) return gemm_fail((int)cudaErrorInvalidValue, "swiglu: ab rows not 16-byte aligned");
   CUtensorMap tdab, tab;
-  int rc = output_map(&tdab, dab, M, 2 * F, lddab);
+  int rc = output_map_wide(&tdab, dab, M, 2 * F, lddab);
   if (rc) return gemm_fail(rc, "tensor map of d_ab");
-  rc = output_map(&tab, ab, M, 2 * F, ldab);        // the same 32 x 32 boxes, read by TMA loads
+  rc = output_map_wide(&tab, ab, M, 2 * F, ldab);   // the same 32 x 64 boxes, read by TMA loads
   if (rc) return gemm_fail(rc, "tensor map of ab");
   SwiGluBwdEpi epi;
   epi.loads = 0;
+  epi.done = 0;
   epi.inited = 0;
   return launch<SwiGluBwdEpi, false, true>(dY, ldy, Wd, ldw, make_work(M, F, D), epi, status, (cudaStream_t)stream,
                                            &tdab, &tab);
@@ -289,13 +307,13 @@ NFB_API int nfb_gemm_swiglu_bwd(const void* dY, const void* Wd, const void* ab, 
 NFB_API int nfb_gemm_acc_splits(int M, int N, int K) {
   Work w = make_work(M, N, K);
   int clusters = 0;
-  if (max_clusters(gemm_pair_kernel<AccumF32Epi, true, true>, &clusters)) return 1;
+  if (max_clusters(gemm_pair_kernel<AccumF32Epi, true, true>, &clusters, smem_bytes_for<AccumF32Epi>())) return 1;
   return choose_splits(w.m_tiles * w.n_tiles, w.k_blocks, clusters);
 }
 
 NFB_API int nfb_gemm_max_clusters() {
   int clusters = 0;
-  if (max_clusters(gemm_pair_kernel<LinearEpi, false, false>, &clusters)) return -1;
+  if (max_clusters(gemm_pair_kernel<LinearEpi, false, false>, &clusters, smem_bytes_for<LinearEpi>())) return -1;
   return clusters;
 }
 

@@ -66,7 +66,7 @@ constexpr int TM = 256;                   // tile rows (128 per CTA)
 constexpr int TN = 256;                   // tile columns (B rows: 128 per CTA)
 constexpr int HALF = 128;
 constexpr int BK = 64;
-constexpr int kStages = 6;
+constexpr int kStages = 6;                // K stages of the main loop (an epilogue may use fewer)
 constexpr int kABytes = HALF * BK * 2;    // 16 KB
 constexpr int kBBytes = HALF * BK * 2;    // 16 KB
 constexpr int kStageBytes = kABytes + kBBytes;
@@ -80,7 +80,7 @@ struct alignas(8) Shared {
   uint64_t tmem_full[2];      // every CTA: an accumulator is complete
   uint64_t tmem_empty[2];     // leader: the 8 epilogue warps of the pair read an accumulator
   uint64_t mma_drain;
-  uint64_t epi_bar[4][2];     // per epilogue warp: TMA loads into its staging buffers (epilogues that read)
+  uint64_t epi_bar[4][4];     // per epilogue warp: TMA loads into its staging buffers (epilogues that read)
   uint32_t tmem_base;
   int abort;
 };
@@ -92,9 +92,13 @@ static_assert(sizeof(Shared) <= kSharedSlot, "Shared must fit its slot");
 // a tensor (SwiGLU backward) uses all four as two (gate, up) sets.
 constexpr int kEpiBufBytes = 32 * 64;
 constexpr int kEpiWarpBufs = 4;
-constexpr size_t kEpiSmem = 4 * kEpiWarpBufs * kEpiBufBytes;
-constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + kSharedSlot + kEpiSmem + 1024;
-static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+// Dynamic shared memory of a kernel instance: each epilogue type declares its main-loop stage count
+// (kStages) and staging buffers per warp (kWarpBufs); one that streams a tensor in trades a stage for
+// a deeper staging ring.
+template <class Epi>
+__host__ __device__ constexpr size_t smem_bytes_for() {
+  return (size_t)Epi::kStages * kStageBytes + kSharedSlot + 4 * (size_t)Epi::kWarpBufs * kEpiBufBytes + 1024;
+}
 
 __device__ __forceinline__ uint32_t cta_rank() {
   uint32_t r;
@@ -230,6 +234,9 @@ __device__ void gemm_pair_body(const CUtensorMap* tma_a, const CUtensorMap* tma_
                                const CUtensorMap* tma_d, const Work& w, Epi& epi, uint32_t* status) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kStages = Epi::kStages;
+  static_assert(kStages <= g2::kStages, "stage barriers");
+  static_assert(smem_bytes_for<Epi>() <= 227 * 1024, "shared memory budget");
   Shared* S = reinterpret_cast<Shared*>(smem + (size_t)kStages * kStageBytes);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -368,11 +375,15 @@ __device__ void gemm_pair_body(const CUtensorMap* tma_a, const CUtensorMap* tma_
     const uint32_t empty_leader1 = map_to(smem_u32(&S->tmem_empty[1]), 0);
     EpiCtx c;
     c.lane = lane;
-    c.smem = reinterpret_cast<uint8_t*>(S) + kSharedSlot + (size_t)quarter * kEpiWarpBufs * kEpiBufBytes;
+    c.smem = reinterpret_cast<uint8_t*>(S) + kSharedSlot + (size_t)quarter * Epi::kWarpBufs * kEpiBufBytes;
     c.bar = S->epi_bar[quarter];
     c.tmap_c = tma_c;
     c.tmap_d = tma_d;
     for (int it = cluster; it < w.items; it += n_clusters) {
+      const Item I = item_at(w, it);
+      c.row0 = I.m_blk * TM + HALF * (int)rank + quarter * 32;
+      c.n0 = I.n_blk * TN;
+      epi.prefetch(c, w);        // loads that do not depend on the accumulator start under the main loop
       bool ok = mbar_wait_sleep(&S->tmem_full[acc], acc_phase, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) {
@@ -383,9 +394,6 @@ __device__ void gemm_pair_body(const CUtensorMap* tma_a, const CUtensorMap* tma_
         break;
       }
       tmem_fence_after();
-      const Item I = item_at(w, it);
-      c.row0 = I.m_blk * TM + HALF * (int)rank + quarter * 32;
-      c.n0 = I.n_blk * TN;
       c.split = I.split;
       c.splits = w.splits;
       c.tile = I.tile;
@@ -455,6 +463,9 @@ __device__ __forceinline__ void round_bf16(float* v, int n) {
 // TMA store (full lines, out-of-range rows and columns clipped by the TMA unit); two buffers per
 // warp alternate. Otherwise each thread stores its row directly.
 struct LinearEpi {
+  static constexpr int kStages = g2::kStages;
+  static constexpr int kWarpBufs = kEpiWarpBufs;
+  __device__ __forceinline__ void prefetch(const EpiCtx&, const Work&) {}
   void* C;
   int64_t ldc;
   const __nv_bfloat16* bias;   // [N] or null
@@ -558,6 +569,9 @@ struct LinearEpi {
 // reductions have completed, so the additions into C happen in split order (deterministic).
 // Without a map (unaligned C) every thread reads and writes its own row.
 struct AccumF32Epi {
+  static constexpr int kStages = g2::kStages;
+  static constexpr int kWarpBufs = kEpiWarpBufs;
+  __device__ __forceinline__ void prefetch(const EpiCtx&, const Work&) {}
   float* C;
   int64_t ldc;
   int accumulate;
@@ -661,6 +675,9 @@ struct AccumF32Epi {
 // the first map and act = silu(gate) * up for the tile's 128 hidden units with the second.
 // Gate and up are rounded to bf16 before act is formed, as when act is computed from stored ab.
 struct SwiGluFwdEpi {
+  static constexpr int kStages = g2::kStages;
+  static constexpr int kWarpBufs = kEpiWarpBufs;
+  __device__ __forceinline__ void prefetch(const EpiCtx&, const Work&) {}
   uint32_t chunk;
 
   __device__ bool warp(const EpiCtx& c, const Work& w, volatile int*, uint32_t*) {
@@ -707,66 +724,94 @@ struct SwiGluFwdEpi {
 // in place, then TMA-stores both boxes into d_ab (same interleaved layout, first map), so d_act
 // never reaches memory and every global access is a full-line TMA transfer.
 struct SwiGluBwdEpi {
-  uint32_t loads;     // chunks whose boxes this warp requested (set = loads & 1)
+  // The epilogue streams 4 bytes in and 4 bytes out per output element, as much DRAM traffic as the
+  // main loop's arithmetic at D = 1024, so it works on 64-column chunks whose (gate, up) boxes have
+  // 128-byte rows (whole L2 lines; 32-column boxes move half lines): two sets of 32 x 64 bf16 boxes
+  // per warp, loads one chunk ahead, the first of a tile issued before its accumulator is ready.
+  // One K stage fewer pays for the staging shared memory (measured: 0.993 -> 0.893 ms at
+  // M 98304, F 4096, D 1024; three sets with two stages fewer were slower, 0.914 ms).
+  static constexpr int kStages = g2::kStages - 1;
+  static constexpr int kWarpBufs = 8;               // 2 sets x (gate, up) x 4 KB, in 2 KB units
+  static constexpr int kSets = 2;
+  static constexpr int kAhead = 1;
+  static constexpr int kBoxBytes = 32 * 128;
+  uint32_t loads;     // lane 0: chunks whose loads this warp issued (counted over all its tiles)
+  uint32_t done;      // chunks this warp stored (counted over all its tiles)
   uint32_t inited;
 
-  __device__ __forceinline__ void issue(const EpiCtx& c, int j, uint32_t set) {
-    // lane 0 only: the set's buffers were last read by stores of two chunks ago -> wait for them
-    bulk_wait_read0();
+  // lane 0: load chunk `loads` (tile column j, a multiple of 64) into set loads % kSets once the
+  // store that last used the set (chunk loads - kSets; one store group per chunk, in order) read it
+  __device__ __forceinline__ void issue(const EpiCtx& c, int j) {
+    const int pending = (int)done + kSets - 1 - (int)loads;   // store groups that may stay unread
+    if (pending <= 0) bulk_wait_read0();
+    else if (pending == 1) bulk_wait_read1();
+    else asm volatile("cp.async.bulk.wait_group.read 2;" ::: "memory");
+    const uint32_t set = loads % kSets;
     const int gcol = 256 * (j >> 7) + (j & 127);
-    uint8_t* gb = c.smem + (2 * set) * kEpiBufBytes;
-    uint8_t* ub = gb + kEpiBufBytes;
-    mbar_arrive_expect_tx(&c.bar[set], 2 * kEpiBufBytes);
+    uint8_t* gb = c.smem + (2 * set) * kBoxBytes;
+    uint8_t* ub = gb + kBoxBytes;
+    mbar_arrive_expect_tx(&c.bar[set], 2 * kBoxBytes);
     tma_load_box(gb, c.tmap_d, &c.bar[set], gcol, c.row0);
     tma_load_box(ub, c.tmap_d, &c.bar[set], gcol + 128, c.row0);
+    ++loads;
   }
 
-  __device__ bool warp(const EpiCtx& c, const Work& w, volatile int* abort_flag, uint32_t* status) {
+  __device__ __forceinline__ static int live_chunks(const EpiCtx& c, const Work& w) {
+    if (c.row0 >= w.M) return 0;
+    const int n = (w.N - c.n0 + 63) / 64;           // N is a multiple of 128
+    return n < TN / 64 ? n : TN / 64;
+  }
+
+  __device__ void prefetch(const EpiCtx& c, const Work& w) {
     if (!inited) {
       if (c.lane == 0) {
-        mbar_init(&c.bar[0], 1);
-        mbar_init(&c.bar[1], 1);
+        for (int i = 0; i < kSets; ++i) mbar_init(&c.bar[i], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
       }
       __syncwarp();
       inited = 1;
     }
-    const bool tile_live = c.row0 < w.M;
-    int nch = 0;                                    // live 32-column chunks of this tile
-    if (tile_live) nch = (w.N - c.n0 + 31) / 32 < TN / 32 ? (w.N - c.n0 + 31) / 32 : TN / 32;
-    if (nch > 0 && c.lane == 0) issue(c, c.n0, loads & 1u);
+    const int nch = live_chunks(c, w);
+    if (c.lane == 0)
+      for (int k = 0; k < kAhead && k < nch; ++k) issue(c, c.n0 + 64 * k);
+  }
+
+  __device__ bool warp(const EpiCtx& c, const Work& w, volatile int* abort_flag, uint32_t* status) {
+    const int nch = live_chunks(c, w);               // live 64-column chunks of this tile
     bool ok = true;
 #pragma unroll 1
-    for (int cc = 0; cc < TN; cc += 32) {
-      float d[32];
-      tmem_ld32(c.taddr + cc, d);
-      const int k = cc / 32;
+    for (int cc = 0; cc < TN; cc += 64) {
+      float d[64];
+      tmem_ld32(c.taddr + cc, d);                   // warp-collective: every lane, every chunk
+      tmem_ld32(c.taddr + cc + 32, d + 32);
+      const int k = cc / 64;
       if (k >= nch) continue;                       // warp-uniform
-      const uint32_t set = (loads + (uint32_t)k) & 1u;
-      if (k + 1 < nch && c.lane == 0) issue(c, c.n0 + cc + 32, set ^ 1u);
-      bool got = mbar_wait_sleep(&c.bar[set], ((loads + (uint32_t)k) >> 1) & 1u, abort_flag);
+      if (k + kAhead < nch && c.lane == 0) issue(c, c.n0 + cc + 64 * kAhead);
+      const uint32_t g = done;                      // this chunk's number, counted over the warp's tiles
+      const uint32_t set = g % kSets;
+      bool got = mbar_wait_sleep(&c.bar[set], (g / kSets) & 1u, abort_flag);
       got = __all_sync(0xffffffffu, got);
       if (!got) {
         if (c.lane == 0) set_status(status, kTimeoutFlag, 220);
         ok = false;
         break;
       }
-      uint8_t* gb = c.smem + (2 * set) * kEpiBufBytes;
-      uint8_t* ub = gb + kEpiBufBytes;
+      uint8_t* gb = c.smem + (2 * set) * kBoxBytes;
+      uint8_t* ub = gb + kBoxBytes;
       const int r = c.lane;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int off = r * 64 + ((q ^ ((r >> 1) & 3)) << 4);   // 64-byte swizzle of the TMA box
-        float g[8], u[8];
-        load16<__nv_bfloat16>(reinterpret_cast<const __nv_bfloat16*>(gb + off), g);
+      for (int q = 0; q < 8; ++q) {
+        const int off = r * 128 + ((q ^ (r & 7)) << 4);   // 128-byte swizzle of the TMA box
+        float g8[8], u[8];
+        load16<__nv_bfloat16>(reinterpret_cast<const __nv_bfloat16*>(gb + off), g8);
         load16<__nv_bfloat16>(reinterpret_cast<const __nv_bfloat16*>(ub + off), u);
         float dg[8], du[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const float sg = sigmoidf_fast(g[e]);
+          const float sg = sigmoidf_fast(g8[e]);
           const float dd = d[8 * q + e];
-          du[e] = dd * g[e] * sg;
-          dg[e] = dd * u[e] * sg * (1.f + g[e] * (1.f - sg));
+          du[e] = dd * g8[e] * sg;
+          dg[e] = dd * u[e] * sg * (1.f + g8[e] * (1.f - sg));
         }
         store16<__nv_bfloat16>(reinterpret_cast<__nv_bfloat16*>(gb + off), dg);
         store16<__nv_bfloat16>(reinterpret_cast<__nv_bfloat16*>(ub + off), du);
@@ -780,8 +825,8 @@ struct SwiGluBwdEpi {
         tma_store_2d(c.tmap_c, ub, gcol + 128, c.row0);
         bulk_commit();
       }
+      ++done;
     }
-    loads += (uint32_t)nch;
     return ok;
   }
 
