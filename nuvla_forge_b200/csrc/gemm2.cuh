@@ -429,9 +429,10 @@ __device__ void gemm_pair_body(const CUtensorMap* tma_a, const CUtensorMap* tma_
 // staged boxes (the buffer alternates); every lane calls it.
 __device__ __forceinline__ void stage_store(const EpiCtx& c, uint32_t& chunk, const float* v,
                                             const CUtensorMap* map, int x, int y) {
-  uint8_t* buf = c.smem + (chunk & 1u) * kEpiBufBytes;
-  if (chunk >= 2) {
-    if (c.lane == 0) bulk_wait_read1();           // the store that last used this buffer has read it
+  // four staging buffers in rotation: up to three earlier stores may still be reading theirs
+  uint8_t* buf = c.smem + (chunk & 3u) * kEpiBufBytes;
+  if (chunk >= 4) {
+    if (c.lane == 0) asm volatile("cp.async.bulk.wait_group.read 3;" ::: "memory");   // this buffer's last store read it
     __syncwarp();
   }
   const int r = c.lane;
@@ -474,7 +475,7 @@ struct LinearEpi {
   int out_f32;
   int vec_ok;                  // C (and R) rows 16-byte aligned
   int use_tma;                 // bf16 output through the staged TMA store
-  uint32_t chunk;              // chunks this warp has staged so far (buffer = chunk & 1)
+  uint32_t chunk;              // chunks this warp has staged so far (buffer = chunk & 3)
 
   __device__ __forceinline__ void add_bias_res(float* v, int m, int n, int N, bool full) const {
     if (bias) {
