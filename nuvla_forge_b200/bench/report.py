@@ -71,10 +71,10 @@ def section_comms(lines, reports: Path):
     for p in found:
         c = json.loads(p.read_text())
         lines += [f"### {p.name}: world {c['world_size']}, NCCL {c.get('nccl_version')}", "",
-                  "| bytes | AR fused | AR pipelined | AR NCCL bf16 | AR NCCL fp32 | RS fused | RS NCCL | AG fused | AG NCCL |",
-                  "|---|---|---|---|---|---|---|---|---|"]
+                  "| bytes | CTAs | AR fused | AR pipelined | AR NCCL bf16 | AR NCCL fp32 | RS fused | RS NCCL | AG fused | "
+                  "AG NCCL |", "|---|---|---|---|---|---|---|---|---|---|"]
         for r in c["rows"]:
-            lines.append(f"| {r['bytes']} | {fmt(r['ar_fused_busbw'], '.1f')} | "
+            lines.append(f"| {r['bytes']} | {r.get('ctas', '—')} | {fmt(r['ar_fused_busbw'], '.1f')} | "
                          f"{fmt(r.get('ar_fused_pipelined_busbw'), '.1f')} | {fmt(r['ar_nccl_bf16_busbw'], '.1f')} | "
                          f"{fmt(r['ar_nccl_fp32_busbw'], '.1f')} | {fmt(r['rs_fused_busbw'], '.1f')} | "
                          f"{fmt(r['rs_nccl_busbw'], '.1f')} | {fmt(r['ag_fused_busbw'], '.1f')} | "
@@ -128,6 +128,18 @@ def section_attention(lines, d):
                      f"{fmt(r['sdpa_ms'], '.3f')} ({fmt(r['sdpa_tflops'], '.0f')}) | "
                      f"{fmt(r.get('native_bwd_ms'), '.3f')} ({fmt(r.get('native_bwd_tflops'), '.0f')}) | "
                      f"{fmt(r.get('sdpa_bwd_ms'), '.3f')} ({fmt(r.get('sdpa_bwd_tflops'), '.0f')}) |")
+    lines.append("")
+
+
+def section_mma_rates(lines, d):
+    lines += ["## tcgen05.mma throughput by shape and operand source (bench_mma_rates)", ""]
+    if not d:
+        lines += ["_Not run._", ""]
+        return
+    lines += ["| instruction | operands | cycles / instruction | FLOP / clk / SM | of 8192 |", "|---|---|---|---|---|"]
+    for r in d["rows"]:
+        lines.append(f"| M128 N{r['n']} K16 | {r['operands']} | {fmt(r['cycles_per_instr'], '.1f')} | "
+                     f"{fmt(r['flop_per_clk_per_sm'], '.0f')} | {fmt(100 * r['frac_of_8192'], '.0f')}% |")
     lines.append("")
 
 
@@ -195,6 +207,7 @@ def main(argv=None):
     section_ag_gemm(lines, d)
     section_gemm(lines, _load(d, "gemm.json"), _load(d, "gemm_sustained.json"))
     section_attention(lines, _load(d, "attention.json"))
+    section_mma_rates(lines, _load(d, "mma_rates.json"))
     section_planner(lines, _load(d, "planner.json"))
     section_loader(lines, _load(d, "dataloader.json"))
     Path(args.out).write_text("\n".join(lines) + "\n")

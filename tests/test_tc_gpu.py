@@ -98,3 +98,16 @@ def test_ce_dispatch_uses_tc_path():
     nat.reset_launch_count()
     chunked_cross_entropy(hid, w, tgt).backward()
     assert nat.launch_count() >= 4   # count, stats, merge, grad
+
+
+def test_mma_rate_probe_completes_and_reports_full_rate_for_n128():
+    """nfb_mma_rate: back-to-back M128 N128 K16 MMAs run at (close to) the tensor core's full rate."""
+    from nuvla_forge_b200 import _native as nat
+
+    out = torch.zeros(2, dtype=torch.int64, device="cuda")
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    nat.call("nfb_mma_rate", 0, 128, 1024, nat.ptr(out), sms, nat.stream())
+    torch.cuda.synchronize()
+    cycles, ok = (int(v) for v in out.tolist())
+    assert ok == 1
+    assert 55 < cycles / 1024 < 90, cycles / 1024     # 64 cycles per instruction at the full rate
