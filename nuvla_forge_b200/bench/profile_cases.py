@@ -53,6 +53,19 @@ def norm_bwd(iters):
 
 
 @case
+def add_rmsnorm_bwd(iters):
+    """Residual add + RMSNorm backward at the ViT shape of the 1b config (the training step's norm seam)."""
+    from ..ops import add_rmsnorm
+    x = _bf(98304, 1024).requires_grad_(True)
+    y = _bf(98304, 1024, seed=1).requires_grad_(True)
+    w = _bf(1024, seed=2).requires_grad_(True)
+    h, o = add_rmsnorm(x, y, w)
+    dh, do = _bf(98304, 1024, seed=3), _bf(98304, 1024, seed=4)
+    for _ in range(iters):
+        torch.autograd.grad([h, o], [x, y, w], [dh, do], retain_graph=True)
+
+
+@case
 def rmsnorm_bwd(iters):
     """Plain RMSNorm backward at the ViT shape of the 1b config: [98304, 1024]."""
     from ..ops import rmsnorm

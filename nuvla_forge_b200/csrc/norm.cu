@@ -416,14 +416,25 @@ __global__ void __launch_bounds__(512, (GATE == GATE_VEC || MOD) ? 1 : 2) norm_b
   __threadfence();
 
   const float* sp = a.partials + (size_t)b * a.P * 3 * N;
-  for (int64_t c = tid; c < N; c += nthreads) {
-    float A = 0.f, D = 0.f, G = 0.f;
-    for (int64_t q = 0; q < a.P; ++q) {
-      const float* pq = sp + (size_t)q * 3 * N;
-      A += __ldcg(pq + c);
-      if (MOD) D += __ldcg(pq + N + c);
-      if (GATE == GATE_VEC) G += __ldcg(pq + 2 * N + c);
+  // Sum of the sample's P partial rows, column by column, in a fixed order (four interleaved
+  // partial sums over q, combined pairwise): independent loads keep many L2 requests in flight,
+  // where one running sum made every load wait for the previous add.
+  auto fold = [&](int64_t off) -> float {
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    int64_t q = 0;
+    for (; q + 4 <= a.P; q += 4) {
+      s0 += __ldcg(sp + (size_t)q * 3 * N + off);
+      s1 += __ldcg(sp + (size_t)(q + 1) * 3 * N + off);
+      s2 += __ldcg(sp + (size_t)(q + 2) * 3 * N + off);
+      s3 += __ldcg(sp + (size_t)(q + 3) * 3 * N + off);
     }
+    for (; q < a.P; ++q) s0 += __ldcg(sp + (size_t)q * 3 * N + off);
+    return (s0 + s1) + (s2 + s3);
+  };
+  for (int64_t c = tid; c < N; c += nthreads) {
+    const float A = fold(c);
+    const float D = MOD ? fold(N + c) : 0.f;
+    const float G = GATE == GATE_VEC ? fold(2 * N + c) : 0.f;
     float w = a.w_f32 ? reinterpret_cast<const float*>(a.weight)[c]
                       : to_f32(reinterpret_cast<const T*>(a.weight)[c]);
     float s1 = 1.f;
@@ -445,8 +456,16 @@ __global__ void __launch_bounds__(512, (GATE == GATE_VEC || MOD) ? 1 : 2) norm_b
   if (s_ticket != (uint32_t)(a.B - 1)) return;
   __threadfence();
   for (int64_t c = tid; c < N; c += nthreads) {
-    float s = 0.f;
-    for (int64_t q = 0; q < a.B; ++q) s += __ldcg(a.dwb + q * N + c);
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    int64_t q = 0;
+    for (; q + 4 <= a.B; q += 4) {
+      s0 += __ldcg(a.dwb + q * N + c);
+      s1 += __ldcg(a.dwb + (q + 1) * N + c);
+      s2 += __ldcg(a.dwb + (q + 2) * N + c);
+      s3 += __ldcg(a.dwb + (q + 3) * N + c);
+    }
+    for (; q < a.B; ++q) s0 += __ldcg(a.dwb + q * N + c);
+    const float s = (s0 + s1) + (s2 + s3);
     if (a.w_f32) reinterpret_cast<float*>(a.dweight)[c] = s;
     else reinterpret_cast<T*>(a.dweight)[c] = from_f32<T>(s);
   }
