@@ -9,6 +9,7 @@
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <type_traits>
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -40,37 +41,73 @@ template <typename T> struct Vec16 {
   union { uint4 u; T v[N]; };
 };
 
+// A 16-byte vector to / from fp32, two 16-bit elements per 32-bit word at a time: a bf16 is the top
+// half of the fp32 with the same value (widening is a shift or a mask), and one packed conversion
+// rounds two floats (round to nearest even, as the scalar conversions do), halving the conversion
+// instructions of the bandwidth-bound kernels.
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4& u, float* out) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) out[k] = __uint_as_float(w[k]);
+  } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      out[2 * k] = __uint_as_float(w[k] << 16);
+      out[2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+      out[2 * k] = f.x;
+      out[2 * k + 1] = f.y;
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 pack16(const float* in) {
+  uint32_t w[4];
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) w[k] = __float_as_uint(in[k]);
+  } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn(in[2 * k], in[2 * k + 1]);
+      w[k] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const __half2 h = __floats2half2_rn(in[2 * k], in[2 * k + 1]);
+      w[k] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 template <typename T>
 __device__ __forceinline__ void load16(const T* p, float* out) {
-  Vec16<T> r;
-  r.u = *reinterpret_cast<const uint4*>(p);
-#pragma unroll
-  for (int i = 0; i < Vec16<T>::N; ++i) out[i] = to_f32(r.v[i]);
+  unpack16<T>(*reinterpret_cast<const uint4*>(p), out);
 }
 
 template <typename T>
 __device__ __forceinline__ void store16(T* p, const float* in) {
-  Vec16<T> r;
-#pragma unroll
-  for (int i = 0; i < Vec16<T>::N; ++i) r.v[i] = from_f32<T>(in[i]);
-  *reinterpret_cast<uint4*>(p) = r.u;
+  *reinterpret_cast<uint4*>(p) = pack16<T>(in);
 }
 
 // Streaming (evict-first) variants for data that is touched exactly once.
 template <typename T>
 __device__ __forceinline__ void load16_stream(const T* p, float* out) {
-  Vec16<T> r;
-  r.u = __ldcs(reinterpret_cast<const uint4*>(p));
-#pragma unroll
-  for (int i = 0; i < Vec16<T>::N; ++i) out[i] = to_f32(r.v[i]);
+  unpack16<T>(__ldcs(reinterpret_cast<const uint4*>(p)), out);
 }
 
 template <typename T>
 __device__ __forceinline__ void store16_stream(T* p, const float* in) {
-  Vec16<T> r;
-#pragma unroll
-  for (int i = 0; i < Vec16<T>::N; ++i) r.v[i] = from_f32<T>(in[i]);
-  __stcs(reinterpret_cast<uint4*>(p), r.u);
+  __stcs(reinterpret_cast<uint4*>(p), pack16<T>(in));
 }
 
 // 8 consecutive elements of T (one 16-byte vector for 2-byte types, two for fp32).

@@ -110,9 +110,8 @@ struct RawChunk {
     }
   }
   __device__ __forceinline__ void get(float* out) const {
-    const T* v = reinterpret_cast<const T*>(u);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) out[j] = to_f32(v[j]);
+    unpack16<T>(u[0], out);
+    if (sizeof(T) == 4) unpack16<T>(u[sizeof(T) == 2 ? 0 : 1], out + 4);
   }
 };
 
