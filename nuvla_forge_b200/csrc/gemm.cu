@@ -273,9 +273,9 @@ NFB_API int nfb_gemm_swiglu_fwd(const void* X, const void* W, void* ab, void* ac
   if (M <= 0) return 0;
   if (K <= 0 || F <= 0 || F % 128) return gemm_fail((int)cudaErrorInvalidValue, "swiglu: F must be a multiple of 128");
   CUtensorMap tab, tact;
-  int rc = output_map(&tab, ab, M, 2 * F, ldab);
+  int rc = output_map_wide(&tab, ab, M, 2 * F, ldab);
   if (rc) return gemm_fail(rc, "tensor map of ab");
-  rc = output_map(&tact, act, M, F, ldact);
+  rc = output_map_wide(&tact, act, M, F, ldact);
   if (rc) return gemm_fail(rc, "tensor map of act");
   SwiGluFwdEpi epi;
   epi.chunk = 0;

@@ -453,6 +453,28 @@ __device__ __forceinline__ void stage_store(const EpiCtx& c, uint32_t& chunk, co
   ++chunk;
 }
 
+// The same for a 32-row x 64-column bf16 box (128-byte rows: whole L2 lines), 128-byte swizzle, four
+// 4 KB buffers per warp in rotation (epilogues with kWarpBufs >= 8).
+__device__ __forceinline__ void stage_store_wide(const EpiCtx& c, uint32_t& chunk, const float* v,
+                                                 const CUtensorMap* map, int x, int y) {
+  uint8_t* buf = c.smem + (chunk & 3u) * (2 * kEpiBufBytes);
+  if (chunk >= 4) {
+    if (c.lane == 0) asm volatile("cp.async.bulk.wait_group.read 3;" ::: "memory");   // this buffer's last store read it
+    __syncwarp();
+  }
+  const int r = c.lane;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    *reinterpret_cast<uint4*>(buf + r * 128 + ((j ^ (r & 7)) << 4)) = pack16<__nv_bfloat16>(v + 8 * j);
+  fence_async_smem();
+  __syncwarp();
+  if (c.lane == 0) {
+    tma_store_2d(map, buf, x, y);
+    bulk_commit();
+  }
+  ++chunk;
+}
+
 __device__ __forceinline__ void round_bf16(float* v, int n) {
   for (int i = 0; i < n; ++i) v[i] = __bfloat162float(__float2bfloat16_rn(v[i]));
 }
@@ -676,8 +698,11 @@ struct AccumF32Epi {
 // the first map and act = silu(gate) * up for the tile's 128 hidden units with the second.
 // Gate and up are rounded to bf16 before act is formed, as when act is computed from stored ab.
 struct SwiGluFwdEpi {
-  static constexpr int kStages = g2::kStages;
-  static constexpr int kWarpBufs = kEpiWarpBufs;
+  // Stores gate, up (the backward's pre-activations) and silu(gate) * up for 64 hidden units at a
+  // time as 32 x 64 boxes with 128-byte rows (whole L2 lines); one K stage fewer pays for the four
+  // 4 KB staging buffers per warp.
+  static constexpr int kStages = g2::kStages - 1;
+  static constexpr int kWarpBufs = 8;
   __device__ __forceinline__ void prefetch(const EpiCtx&, const Work&) {}
   uint32_t chunk;
 
@@ -690,23 +715,19 @@ struct SwiGluFwdEpi {
     }
     const int h0 = c.n0 / 2;                       // first hidden unit of this tile
 #pragma unroll 1
-    for (int cc = 0; cc < TN / 2; cc += 32) {
-      if (c.n0 + cc >= w.N) {
-        float v[32];
-        tmem_ld32(c.taddr + cc, v);
-        tmem_ld32(c.taddr + 128 + cc, v);
-        continue;
-      }
-      float g[32], u[32];
+    for (int cc = 0; cc < TN / 2; cc += 64) {
+      float g[64], u[64];
       tmem_ld32(c.taddr + cc, g);
+      tmem_ld32(c.taddr + cc + 32, g + 32);
       tmem_ld32(c.taddr + 128 + cc, u);
-      stage_store(c, chunk, g, c.tmap_c, c.n0 + cc, c.row0);
-      stage_store(c, chunk, u, c.tmap_c, c.n0 + 128 + cc, c.row0);
-      round_bf16(g, 32);
-      round_bf16(u, 32);
+      tmem_ld32(c.taddr + 128 + cc + 32, u + 32);
+      stage_store_wide(c, chunk, g, c.tmap_c, c.n0 + cc, c.row0);
+      stage_store_wide(c, chunk, u, c.tmap_c, c.n0 + 128 + cc, c.row0);
+      round_bf16(g, 64);
+      round_bf16(u, 64);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) g[j] = g[j] * sigmoidf_fast(g[j]) * u[j];
-      stage_store(c, chunk, g, c.tmap_d, h0 + cc, c.row0);
+      for (int j = 0; j < 64; ++j) g[j] = g[j] * sigmoidf_fast(g[j]) * u[j];
+      stage_store_wide(c, chunk, g, c.tmap_d, h0 + cc, c.row0);
     }
     return true;
   }
