@@ -8,8 +8,13 @@ the kernels support (bf16, D in {64, 128}, 16-byte-aligned rows, Hkv dividing
 Hq, and for a causal mask Sq == Sk: the kernels align the mask to the bottom
 right, which only equals PyTorch's top-left ``is_causal`` for square masks).
 
-``enable()`` (or ``NFB_ATTN_NATIVE=1`` at import) routes ``ops.attention``
-through them (forward and backward).
+Routing of ``ops.attention`` (``NFB_ATTN_NATIVE`` at import, or ``enable(mode)``): ``auto``
+(default) uses the native kernels only where they measured faster than cuDNN on B200 -- a short
+query sequence attending a long context (at most 128 queries, at least 1024 keys: the DiT's
+cross-attention into the backbone states, forward + backward 0.236 vs 0.251 ms at config 3;
+reports/attention.json) -- and cuDNN SDPA elsewhere (self-attention over the ViT and backbone
+tokens, where the native kernels run at 57-69% of cuDNN's speed); ``1`` uses them wherever they
+support the shape, ``0`` never.
 """
 
 from __future__ import annotations
@@ -120,18 +125,33 @@ class _NativeAttention(torch.autograd.Function):
         return dq, dk, dv, None, None
 
 
+_MODE = "auto"
+
+
+def _faster_than_sdpa(q, k) -> bool:
+    """The measured regime where the native kernels beat cuDNN: few queries, a long context."""
+    return q.shape[1] <= 128 and k.shape[1] >= 1024
+
+
 def _native(q, k, v, causal, scale):
     if not supported(q, k, v, causal):
+        return None
+    if _MODE == "auto" and not _faster_than_sdpa(q, k):
         return None
     if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
         return _NativeAttention.apply(q, k, v, causal, scale)
     return attention_fwd(q, k, v, causal, scale)[0]
 
 
-def enable(flag: bool = True) -> None:
-    """Route ops.attention through the native forward (off by default)."""
-    register_native(_native if flag else None)
+def enable(flag: bool | str = True) -> None:
+    """Route ops.attention through the native kernels: True / "1" wherever supported, "auto" where
+    they measured faster than cuDNN, False / "0" never."""
+    global _MODE
+    mode = {True: "1", False: "0"}.get(flag, str(flag))
+    if mode not in ("0", "1", "auto"):
+        raise ValueError(f"attention routing mode {flag!r}: expected 0, 1 or auto")
+    _MODE = mode
+    register_native(_native if mode != "0" else None)
 
 
-if os.environ.get("NFB_ATTN_NATIVE", "0") == "1":
-    enable(True)
+enable(os.environ.get("NFB_ATTN_NATIVE", "auto"))

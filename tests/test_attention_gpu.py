@@ -79,6 +79,7 @@ def test_attention_native_autograd_path():
         flash_attn.enable(False)
     qb, kb, vb = b.split([4, 4, 4], dim=2)
     ob = attention(qb, kb, vb, causal=True)
+    flash_attn.enable("auto")
     go = torch.randn_like(oa)
     oa.backward(go)
     ob.backward(go)
@@ -142,5 +143,23 @@ def test_attention_native_fwd_bwd_autograd_path():
     qb, kb, vb = b.split([8, 2, 2], dim=2)
     ob = attention(qb, kb, vb, causal=True)
     ob.backward(go)
+    flash_attn.enable("auto")
     assert float((oa.float() - ob.float()).norm() / ob.float().norm()) < 1e-2
     assert float((a.grad.float() - b.grad.float()).norm() / b.grad.float().norm()) < 2e-2
+
+
+def test_auto_routing_uses_native_only_where_it_measured_faster():
+    """Default routing: few queries into a long context go native, self-attention stays on SDPA."""
+    from nuvla_forge_b200.ops import flash_attn
+
+    g = torch.Generator(device=DEV).manual_seed(3)
+    mk = lambda *s: torch.randn(*s, generator=g, device=DEV).to(torch.bfloat16)  # noqa: E731
+    flash_attn.enable("auto")
+    q, kv = mk(2, 16, 4, 64), mk(2, 3392, 8, 64)
+    k, v = kv.split([4, 4], dim=2)
+    assert flash_attn._native(q, k, v, False, None) is not None          # DiT cross-attention shape
+    qs = mk(2, 1024, 12, 64)
+    assert flash_attn._native(*qs.split([4, 4, 4], dim=2), False, None) is None   # self-attention
+    flash_attn.enable(True)
+    assert flash_attn._native(*qs.split([4, 4, 4], dim=2), False, None) is not None
+    flash_attn.enable("auto")
