@@ -14,13 +14,15 @@
 //               into a ring (4-D tensor maps over [B, S, H, D]).
 //   warp 1      MMA issuer (one elected lane), per tile t and key tile j:
 //               S_t = Q_t K_j^T into a 128-column TMEM buffer, then
-//               O_t += P_t V_j with P_t (bf16) read from TMEM and V_j MN-major
-//               from its TMA tile. It polls the barriers of both tiles and
-//               issues whichever MMA is ready, so one tile's MMAs run while
-//               the other tile's softmax warps work. With D = 64 P_t has its
-//               own TMEM columns and the softmax releases S_t right after
-//               loading it, so S_t of the next key tile is computed while the
-//               softmax exponentiates; with D = 128 P_t is written over S_t.
+//               O_t += P_t V_j with P_t (bf16) written over S_t by the softmax
+//               warps and read from TMEM, V_j MN-major from its TMA tile. The
+//               two tiles are issued staggered (P_0 V, S_0 of the next key
+//               tile, P_1 V, S_1 ...), so one tile's MMAs run while the other
+//               tile's softmax warps work. A variant built with
+//               SEP_P_FOR_D64=1 gives P its own TMEM columns at D = 64, lets
+//               the softmax release S right after loading it, splits P V in
+//               two halves and polls both tiles' barriers; it measured slower
+//               (more barriers and register spills) and is off by default.
 //   warps 2-5   softmax of tile 0, warps 6-9 softmax of tile 1: one thread per
 //               query row (TMEM lane), the whole 128-key row of S in registers,
 //               so the row maximum needs no exchange. Online softmax in base 2
@@ -38,6 +40,9 @@ namespace attn {
 
 using namespace nfb::tc;
 
+// Measured variants, off by default (see the header and the layout comment): separate P columns at
+// D = 64, and a quarter of the forward's exponentials on the FMA pipe (ex2_poly; slower here because
+// the extra registers spill).
 #ifndef SEP_P_FOR_D64
 #define SEP_P_FOR_D64 0
 #endif
@@ -174,9 +179,9 @@ struct Layout {
   static constexpr size_t kBytes = (size_t)kEv + 8192 + 1024;   // AttnShared, events, alignment
   static_assert(kBytes <= 227 * 1024, "shared memory");
   static_assert(kBytes > 114 * 1024, "one CTA (and its 512 TMEM columns) per SM");
-  // TMEM columns. D = 64: S_t | P_t (bf16 pairs) | O_t each tile, so the softmax frees S_t as soon as
-  // it has loaded it and S_t of the next key tile is computed while it exponentiates. D = 128 (no room
-  // for separate P): P_t is written over S_t, and the next S_t waits until P_t V has completed.
+  // TMEM columns: S_0 | S_1 | O_0 | O_1, with P_t written over S_t (the next S_t waits until P_t V
+  // has completed). With SEP_P_FOR_D64=1 and D = 64: S_t | P_t (bf16 pairs) | O_t per tile, so the
+  // softmax frees S_t as soon as it has loaded it.
   static constexpr bool kSepP = SEP_P_FOR_D64 && D == 64;
   static constexpr bool kPolyExpFwd = POLY_EXP_FWD != 0;
   static constexpr uint32_t cS = 0;                          // + t * 128
