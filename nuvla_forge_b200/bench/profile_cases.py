@@ -126,6 +126,24 @@ def gemm_pair_vit_qkv(iters):
 
 
 @case
+def gemm_pair_swiglu_bwd(iters):
+    """Down projection's input gradient with the SwiGLU backward in its epilogue, ViT MLP shape at 24
+    images: dY [24576, 1024], W_down [1024, 4096], ab / d_ab [24576, 8192] (interleaved gate / up)."""
+    from .. import _native as nat
+    from ..ops import linear as L
+    M, F, D = 24576, 4096, 1024
+    dy, wd = _bf(M, D), _bf(D, F, seed=1)
+    ab = _bf(M, 2 * F, seed=2)
+    dab = torch.empty_like(ab)
+    st = L.status_word(dy.device)
+    for _ in range(iters):
+        nat.call("nfb_gemm_swiglu_bwd", nat.ptr(dy), nat.ptr(wd), nat.ptr(ab), nat.ptr(dab), M, F, D, dy.stride(0),
+                 wd.stride(0), ab.stride(0), dab.stride(0), nat.ptr(st), nat.stream(dy.device))
+    torch.cuda.synchronize()
+    L.check_status()
+
+
+@case
 def gemm_pair_wgrad(iters):
     """CTA-pair GEMM weight gradient at the backbone proj shape: dW [2048, 2048] fp32 over 27136 tokens."""
     from ..ops.linear import gemm_acc
