@@ -1,12 +1,14 @@
 """Where the native attention kernels spend their cycles, phase by phase.
 
-    python -m nuvla_forge_b200.bench.attn_phases [--shape vit|backbone]
+    python -m nuvla_forge_b200.bench.attn_phases [--shape vit|backbone] [--timeline]
 
 Runs the tcgen05 forward and backward once each with their per-phase cycle counters switched on
 (``nfb_attn_fwd_trace`` / ``nfb_attn_bwd_trace``: lane 0 of every warp adds the SM cycles spent
 in each phase of its loop) and prints, per role, the average cycles per warp and per step (one
 step = one 128 x 128 tile pair). Waits show which role the others stall on; the compute phases
-show how far each is from its instruction or pipe bound. A profiling aid: the traced kernels are
+show how far each is from its instruction or pipe bound. ``--timeline`` also prints the first
+CTA's events in order (MMA batches issued per tile and step, and each softmax warp's phase
+boundaries), which shows what a waiting role waits for. A profiling aid: the traced kernels are
 separate instantiations, the untraced ones carry no counters.
 """
 
@@ -37,12 +39,6 @@ def _report(title, counters, phases, warps_of, ctas, steps):
             print(f"  {name:<32} {c[slot] / (warps_of[role] * ctas) / steps:10.0f} cycles/step")
 
 
-EVENTS = {10: "S0 issue", 11: "S1 issue", 12: "S0 issued", 13: "S1 issued", 20: "PV0 issue", 21: "PV1 issue",
-          22: "PV0 issued", 23: "PV1 issued", 30: "sm0 wait S", 31: "sm0 got S", 32: "sm0 max done",
-          33: "sm0 PV done", 34: "sm0 P ready", 40: "sm1 wait S", 41: "sm1 got S", 42: "sm1 max done",
-          43: "sm1 PV done", 44: "sm1 P ready"}
-
-
 def _timeline(counters, which):
     c = counters.cpu().tolist()
     ev = sorted(((v & 0xFFFFFFFFFFFF, v >> 48) for v in c[64:] if v))
@@ -62,7 +58,7 @@ def _timeline(counters, which):
             kind, rest = divmod(code - 1000, 100)
             name = f"    MMA tile {rest // 50} step {rest % 50}: {kinds[kind]}"
         else:
-            name = EVENTS.get(code, code)
+            name = str(code)
         print(f"  {t - t0:8d}  {name}")
 
 
