@@ -32,7 +32,7 @@ static int gemm_fail(int rc, const char* site) {
 namespace {
 
 template <class Epi, bool A_MN, bool B_MN>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<Epi>(), 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                      const __grid_constant__ CUtensorMap tc, const __grid_constant__ CUtensorMap td, Work w,
                      Epi epi, uint32_t* status) {
@@ -51,7 +51,7 @@ static ClusterCache g_cc;
 static std::mutex g_cc_mu;
 
 template <class K>
-static int max_clusters(K kernel, int* out, size_t smem_bytes) {
+static int max_clusters(K kernel, int* out, size_t smem_bytes, int threads) {
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(g_cc_mu);
@@ -62,7 +62,7 @@ static int max_clusters(K kernel, int* out, size_t smem_bytes) {
   if (e != cudaSuccess) return (int)e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * 74, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
   cfg.dynamicSmemBytes = smem_bytes;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -186,12 +186,12 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, Work w
   if (rc) return gemm_fail(rc, "tensor map of B");
   auto kern = gemm_pair_kernel<Epi, A_MN, B_MN>;
   int clusters = 0;
-  rc = max_clusters(kern, &clusters, smem_bytes_for<Epi>());
+  rc = max_clusters(kern, &clusters, smem_bytes_for<Epi>(), threads_for<Epi>());
   if (rc) return gemm_fail(rc, "cluster occupancy query");
   const int grid_clusters = w.items < clusters ? w.items : clusters;
   cudaError_t pending = cudaGetLastError();     // an error left by an earlier call of this thread
   if (pending != cudaSuccess) return gemm_fail((int)pending, "error pending before the launch");
-  kern<<<2 * grid_clusters, kThreads, smem_bytes_for<Epi>(), st>>>(ta, tb, tcm, tdm, w, epi, status);
+  kern<<<2 * grid_clusters, threads_for<Epi>(), smem_bytes_for<Epi>(), st>>>(ta, tb, tcm, tdm, w, epi, status);
   rc = (int)cudaGetLastError();
   return rc ? gemm_fail(rc, "kernel launch") : 0;
 }
@@ -242,7 +242,7 @@ NFB_API int nfb_gemm_acc(const void* A, const void* B, float* C, int M, int N, i
   const int tiles = w.m_tiles * w.n_tiles;
   if (splits <= 0) {
     int clusters = 0;
-    int rc = max_clusters(gemm_pair_kernel<AccumF32Epi, true, true>, &clusters, smem_bytes_for<AccumF32Epi>());
+    int rc = max_clusters(gemm_pair_kernel<AccumF32Epi, true, true>, &clusters, smem_bytes_for<AccumF32Epi>(), threads_for<AccumF32Epi>());
     if (rc) return rc;
     splits = choose_splits(tiles, w.k_blocks, clusters);
   }
@@ -307,13 +307,13 @@ NFB_API int nfb_gemm_swiglu_bwd(const void* dY, const void* Wd, const void* ab, 
 NFB_API int nfb_gemm_acc_splits(int M, int N, int K) {
   Work w = make_work(M, N, K);
   int clusters = 0;
-  if (max_clusters(gemm_pair_kernel<AccumF32Epi, true, true>, &clusters, smem_bytes_for<AccumF32Epi>())) return 1;
+  if (max_clusters(gemm_pair_kernel<AccumF32Epi, true, true>, &clusters, smem_bytes_for<AccumF32Epi>(), threads_for<AccumF32Epi>())) return 1;
   return choose_splits(w.m_tiles * w.n_tiles, w.k_blocks, clusters);
 }
 
 NFB_API int nfb_gemm_max_clusters() {
   int clusters = 0;
-  if (max_clusters(gemm_pair_kernel<LinearEpi, false, false>, &clusters, smem_bytes_for<LinearEpi>())) return -1;
+  if (max_clusters(gemm_pair_kernel<LinearEpi, false, false>, &clusters, smem_bytes_for<LinearEpi>(), threads_for<LinearEpi>())) return -1;
   return clusters;
 }
 

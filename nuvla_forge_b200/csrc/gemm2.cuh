@@ -80,7 +80,7 @@ struct alignas(8) Shared {
   uint64_t tmem_full[2];      // every CTA: an accumulator is complete
   uint64_t tmem_empty[2];     // leader: the 8 epilogue warps of the pair read an accumulator
   uint64_t mma_drain;
-  uint64_t epi_bar[4][4];     // per epilogue warp: TMA loads into its staging buffers (epilogues that read)
+  uint64_t epi_bar[8][4];     // per epilogue warp: TMA loads into its staging buffers (epilogues that read)
   uint32_t tmem_base;
   int abort;
 };
@@ -97,8 +97,13 @@ constexpr int kEpiWarpBufs = 4;
 // a deeper staging ring.
 template <class Epi>
 __host__ __device__ constexpr size_t smem_bytes_for() {
-  return (size_t)Epi::kStages * kStageBytes + kSharedSlot + 4 * (size_t)Epi::kWarpBufs * kEpiBufBytes + 1024;
+  return (size_t)Epi::kStages * kStageBytes + kSharedSlot + (size_t)Epi::kEpiWarps * Epi::kWarpBufs * kEpiBufBytes +
+         1024;
 }
+// Threads of a CTA: the TMA producer warp, the MMA warp and the epilogue warps (four, one per TMEM
+// lane quarter, or eight, two per quarter splitting the tile's columns).
+template <class Epi>
+__host__ __device__ constexpr int threads_for() { return 64 + 32 * Epi::kEpiWarps; }
 
 __device__ __forceinline__ uint32_t cta_rank() {
   uint32_t r;
@@ -216,6 +221,7 @@ __device__ __forceinline__ Item item_at(const Work& w, int it) {
 // columns start at n0; taddr is the TMEM address of (its first lane, the accumulator's column 0).
 struct EpiCtx {
   int row0, n0;
+  int col0, col1;      // the tile columns this warp handles (all 256 with four epilogue warps)
   int split, splits, tile;
   int slot;            // (tile's warp slot) = cta * 4 + quarter, for per-warp split-K flags
   uint32_t taddr;
@@ -253,7 +259,7 @@ __device__ void gemm_pair_body(const CUtensorMap* tma_a, const CUtensorMap* tma_
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&S->tmem_full[a], 1);
-      mbar_init(&S->tmem_empty[a], 8);   // 4 epilogue warps x 2 CTAs
+      mbar_init(&S->tmem_empty[a], 2 * Epi::kEpiWarps);   // every epilogue warp of both CTAs
     }
     mbar_init(&S->mma_drain, 1);
     S->abort = 0;
@@ -367,16 +373,21 @@ __device__ void gemm_pair_body(const CUtensorMap* tma_a, const CUtensorMap* tma_
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5, both CTAs) ----------------
-    const int quarter = warp & 3;
+    // ---------------- epilogue (warps 2.., both CTAs) ----------------
+    static_assert(Epi::kEpiWarps == 4 || Epi::kEpiWarps == 8, "epilogue warps");
+    const int ew = warp - 2;                       // epilogue warp index
+    const int quarter = warp & 3;                  // the TMEM lane quarter this warp may access
+    const int cols = TN / (Epi::kEpiWarps / 4);    // tile columns per warp
     int acc = 0;
     uint32_t acc_phase = 0;
     const uint32_t empty_leader0 = map_to(smem_u32(&S->tmem_empty[0]), 0);
     const uint32_t empty_leader1 = map_to(smem_u32(&S->tmem_empty[1]), 0);
     EpiCtx c;
     c.lane = lane;
-    c.smem = reinterpret_cast<uint8_t*>(S) + kSharedSlot + (size_t)quarter * Epi::kWarpBufs * kEpiBufBytes;
-    c.bar = S->epi_bar[quarter];
+    c.smem = reinterpret_cast<uint8_t*>(S) + kSharedSlot + (size_t)ew * Epi::kWarpBufs * kEpiBufBytes;
+    c.bar = S->epi_bar[ew];
+    c.col0 = (ew >> 2) * cols;
+    c.col1 = c.col0 + cols;
     c.tmap_c = tma_c;
     c.tmap_d = tma_d;
     for (int it = cluster; it < w.items; it += n_clusters) {
@@ -486,6 +497,7 @@ __device__ __forceinline__ void round_bf16(float* v, int n) {
 // TMA store (full lines, out-of-range rows and columns clipped by the TMA unit); two buffers per
 // warp alternate. Otherwise each thread stores its row directly.
 struct LinearEpi {
+  static constexpr int kEpiWarps = 4;
   static constexpr int kStages = g2::kStages;
   static constexpr int kWarpBufs = kEpiWarpBufs;
   __device__ __forceinline__ void prefetch(const EpiCtx&, const Work&) {}
@@ -592,6 +604,7 @@ struct LinearEpi {
 // reductions have completed, so the additions into C happen in split order (deterministic).
 // Without a map (unaligned C) every thread reads and writes its own row.
 struct AccumF32Epi {
+  static constexpr int kEpiWarps = 4;
   static constexpr int kStages = g2::kStages;
   static constexpr int kWarpBufs = kEpiWarpBufs;
   __device__ __forceinline__ void prefetch(const EpiCtx&, const Work&) {}
@@ -698,6 +711,7 @@ struct AccumF32Epi {
 // the first map and act = silu(gate) * up for the tile's 128 hidden units with the second.
 // Gate and up are rounded to bf16 before act is formed, as when act is computed from stored ab.
 struct SwiGluFwdEpi {
+  static constexpr int kEpiWarps = 4;
   // Stores gate, up (the backward's pre-activations) and silu(gate) * up for 64 hidden units at a
   // time as 32 x 64 boxes with 128-byte rows (whole L2 lines); one K stage fewer pays for the four
   // 4 KB staging buffers per warp.
@@ -747,78 +761,70 @@ struct SwiGluFwdEpi {
 // never reaches memory and every global access is a full-line TMA transfer.
 struct SwiGluBwdEpi {
   // The epilogue streams 4 bytes in and 4 bytes out per output element, as much DRAM traffic as the
-  // main loop's arithmetic at D = 1024, so it works on 64-column chunks whose (gate, up) boxes have
-  // 128-byte rows (whole L2 lines; 32-column boxes move half lines): two sets of 32 x 64 bf16 boxes
-  // per warp, loads one chunk ahead, the first of a tile issued before its accumulator is ready.
-  // One K stage fewer pays for the staging shared memory (measured: 0.993 -> 0.893 ms at
-  // M 98304, F 4096, D 1024; three sets with two stages fewer were slower, 0.914 ms).
+  // main loop's arithmetic at D = 1024, and one warp per TMEM lane quarter left its loads, SFU and
+  // shared-memory latencies exposed: eight epilogue warps (two per quarter, each half of the tile's
+  // columns) hide them for one another. Each works on 64-column chunks whose (gate, up) boxes have
+  // 128-byte rows (whole L2 lines) in one 8 KB staging set; a tile's first load is issued before its
+  // accumulator is ready. One K stage fewer pays for the staging shared memory.
+  static constexpr int kEpiWarps = 8;
   static constexpr int kStages = g2::kStages - 1;
-  static constexpr int kWarpBufs = 8;               // 2 sets x (gate, up) x 4 KB, in 2 KB units
-  static constexpr int kSets = 2;
-  static constexpr int kAhead = 1;
+  static constexpr int kWarpBufs = 4;               // one (gate, up) set of 4 KB boxes, in 2 KB units
   static constexpr int kBoxBytes = 32 * 128;
   uint32_t loads;     // lane 0: chunks whose loads this warp issued (counted over all its tiles)
   uint32_t done;      // chunks this warp stored (counted over all its tiles)
   uint32_t inited;
 
-  // lane 0: load chunk `loads` (tile column j, a multiple of 64) into set loads % kSets once the
-  // store that last used the set (chunk loads - kSets; one store group per chunk, in order) read it
+  // lane 0: load chunk `loads` (tile column j, a multiple of 64) into the staging set once the
+  // previous chunk's stores have read it
   __device__ __forceinline__ void issue(const EpiCtx& c, int j) {
-    const int pending = (int)done + kSets - 1 - (int)loads;   // store groups that may stay unread
-    if (pending <= 0) bulk_wait_read0();
-    else if (pending == 1) bulk_wait_read1();
-    else asm volatile("cp.async.bulk.wait_group.read 2;" ::: "memory");
-    const uint32_t set = loads % kSets;
+    bulk_wait_read0();
     const int gcol = 256 * (j >> 7) + (j & 127);
-    uint8_t* gb = c.smem + (2 * set) * kBoxBytes;
+    uint8_t* gb = c.smem;
     uint8_t* ub = gb + kBoxBytes;
-    mbar_arrive_expect_tx(&c.bar[set], 2 * kBoxBytes);
-    tma_load_box(gb, c.tmap_d, &c.bar[set], gcol, c.row0);
-    tma_load_box(ub, c.tmap_d, &c.bar[set], gcol + 128, c.row0);
+    mbar_arrive_expect_tx(&c.bar[0], 2 * kBoxBytes);
+    tma_load_box(gb, c.tmap_d, &c.bar[0], gcol, c.row0);
+    tma_load_box(ub, c.tmap_d, &c.bar[0], gcol + 128, c.row0);
     ++loads;
   }
 
   __device__ __forceinline__ static int live_chunks(const EpiCtx& c, const Work& w) {
-    if (c.row0 >= w.M) return 0;
-    const int n = (w.N - c.n0 + 63) / 64;           // N is a multiple of 128
-    return n < TN / 64 ? n : TN / 64;
+    if (c.row0 >= w.M || c.n0 + c.col0 >= w.N) return 0;
+    const int n = (w.N - c.n0 - c.col0 + 63) / 64;  // N is a multiple of 128
+    const int m = (c.col1 - c.col0) / 64;
+    return n < m ? n : m;
   }
 
   __device__ void prefetch(const EpiCtx& c, const Work& w) {
     if (!inited) {
       if (c.lane == 0) {
-        for (int i = 0; i < kSets; ++i) mbar_init(&c.bar[i], 1);
+        mbar_init(&c.bar[0], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
       }
       __syncwarp();
       inited = 1;
     }
-    const int nch = live_chunks(c, w);
-    if (c.lane == 0)
-      for (int k = 0; k < kAhead && k < nch; ++k) issue(c, c.n0 + 64 * k);
+    if (c.lane == 0 && live_chunks(c, w) > 0) issue(c, c.n0 + c.col0);
   }
 
   __device__ bool warp(const EpiCtx& c, const Work& w, volatile int* abort_flag, uint32_t* status) {
-    const int nch = live_chunks(c, w);               // live 64-column chunks of this tile
+    const int nch = live_chunks(c, w);               // live 64-column chunks of this warp's columns
     bool ok = true;
 #pragma unroll 1
-    for (int cc = 0; cc < TN; cc += 64) {
+    for (int cc = c.col0; cc < c.col1; cc += 64) {
       float d[64];
       tmem_ld32(c.taddr + cc, d);                   // warp-collective: every lane, every chunk
       tmem_ld32(c.taddr + cc + 32, d + 32);
-      const int k = cc / 64;
+      const int k = (cc - c.col0) / 64;
       if (k >= nch) continue;                       // warp-uniform
-      if (k + kAhead < nch && c.lane == 0) issue(c, c.n0 + cc + 64 * kAhead);
       const uint32_t g = done;                      // this chunk's number, counted over the warp's tiles
-      const uint32_t set = g % kSets;
-      bool got = mbar_wait_sleep(&c.bar[set], (g / kSets) & 1u, abort_flag);
+      bool got = mbar_wait_sleep(&c.bar[0], g & 1u, abort_flag);
       got = __all_sync(0xffffffffu, got);
       if (!got) {
         if (c.lane == 0) set_status(status, kTimeoutFlag, 220);
         ok = false;
         break;
       }
-      uint8_t* gb = c.smem + (2 * set) * kBoxBytes;
+      uint8_t* gb = c.smem;
       uint8_t* ub = gb + kBoxBytes;
       const int r = c.lane;
 #pragma unroll
@@ -848,6 +854,7 @@ struct SwiGluBwdEpi {
         bulk_commit();
       }
       ++done;
+      if (k + 1 < nch && c.lane == 0) issue(c, c.n0 + cc + 64);   // after this chunk's stores read the set
     }
     return ok;
   }
