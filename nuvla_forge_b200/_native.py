@@ -169,9 +169,14 @@ def launch_count() -> int:
     return _launches[0]
 
 
+_fns: dict[str, object] = {}
+
+
 def call(name: str, *args) -> int:
     """Call ``name`` (one kernel launch) and raise if it returns a non-zero CUDA error code."""
-    fn = getattr(lib(), name)
+    fn = _fns.get(name)
+    if fn is None:
+        fn = _fns[name] = getattr(lib(), name)
     _launches[0] += 1
     rc = fn(*args)
     if rc != 0:
@@ -191,12 +196,21 @@ def _err_name(rc: int) -> str:
         return "?"
 
 
-def ptr(t: torch.Tensor | None) -> c_void_p:
-    return c_void_p(0 if t is None else t.data_ptr())
+# Pointers and streams are passed as plain ints (None for NULL): every entry point declares
+# c_void_p argument types, so ctypes converts them without a wrapper object per argument.
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
 
 
-def stream(device: torch.device | None = None) -> c_void_p:
-    return c_void_p(torch.cuda.current_stream(device).cuda_stream)
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def stream(device: torch.device | None = None) -> int:
+    """The current CUDA stream of ``device`` (default: the current device) as a ``cudaStream_t`` value."""
+    if _raw_stream is not None and (device is None or isinstance(device, torch.device)):
+        idx = device.index if device is not None else None
+        return _raw_stream(torch.cuda.current_device() if idx is None else idx)
+    return torch.cuda.current_stream(device).cuda_stream
 
 
 def dtype_code(dt: torch.dtype) -> int:

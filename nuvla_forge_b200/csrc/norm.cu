@@ -415,35 +415,75 @@ __global__ void __launch_bounds__(512, (GATE == GATE_VEC || MOD) ? 1 : 2) norm_b
   __threadfence();
 
   const float* sp = a.partials + (size_t)b * a.P * 3 * N;
-  // Sum of the sample's P partial rows, column by column, in a fixed order (four interleaved
-  // partial sums over q, combined pairwise): independent loads keep many L2 requests in flight,
-  // where one running sum made every load wait for the previous add.
-  auto fold = [&](int64_t off) -> float {
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-    int64_t q = 0;
-    for (; q + 4 <= a.P; q += 4) {
-      s0 += __ldcg(sp + (size_t)q * 3 * N + off);
-      s1 += __ldcg(sp + (size_t)(q + 1) * 3 * N + off);
-      s2 += __ldcg(sp + (size_t)(q + 2) * 3 * N + off);
-      s3 += __ldcg(sp + (size_t)(q + 3) * 3 * N + off);
+  // Sum of the sample's P partial rows in a fixed order. A column quad (four columns, one 16-byte
+  // load per partial row) is shared by S consecutive lanes, lane s taking rows s, s + S, ... into
+  // four interleaved sums; a butterfly of shuffles then adds the S lane sums. With one sample
+  // (P = 2 x SMs rows) the single last CTA otherwise waits on P / 4 dependent L2 round trips per
+  // column.
+  const int64_t nq4 = N / 4;
+  int S = 1;
+  while (S < 8 && nq4 * S * 2 <= nthreads) S *= 2;
+  auto fold4 = [&](int64_t off, int s, bool live) -> float4 {
+    float4 acc[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (live) {
+      const float* base = sp + off;
+      const size_t rs = (size_t)3 * N;
+      int64_t q = s;
+      for (; q + 3 * S < a.P; q += 4 * S) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float4 v = __ldcg(reinterpret_cast<const float4*>(base + (size_t)(q + k * S) * rs));
+          acc[k].x += v.x; acc[k].y += v.y; acc[k].z += v.z; acc[k].w += v.w;
+        }
+      }
+      for (; q < a.P; q += S) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(base + (size_t)q * rs));
+        acc[0].x += v.x; acc[0].y += v.y; acc[0].z += v.z; acc[0].w += v.w;
+      }
     }
-    for (; q < a.P; ++q) s0 += __ldcg(sp + (size_t)q * 3 * N + off);
-    return (s0 + s1) + (s2 + s3);
+    float4 r;
+    r.x = (acc[0].x + acc[1].x) + (acc[2].x + acc[3].x);
+    r.y = (acc[0].y + acc[1].y) + (acc[2].y + acc[3].y);
+    r.z = (acc[0].z + acc[1].z) + (acc[2].z + acc[3].z);
+    r.w = (acc[0].w + acc[1].w) + (acc[2].w + acc[3].w);
+    // lanes of one quad are S consecutive lanes of one warp (S divides 32)
+    for (int o = 1; o < S; o <<= 1) {
+      r.x += __shfl_xor_sync(0xffffffffu, r.x, o);
+      r.y += __shfl_xor_sync(0xffffffffu, r.y, o);
+      r.z += __shfl_xor_sync(0xffffffffu, r.z, o);
+      r.w += __shfl_xor_sync(0xffffffffu, r.w, o);
+    }
+    return r;
   };
-  for (int64_t c = tid; c < N; c += nthreads) {
-    const float A = fold(c);
-    const float D = MOD ? fold(N + c) : 0.f;
-    const float G = GATE == GATE_VEC ? fold(2 * N + c) : 0.f;
-    float w = a.w_f32 ? reinterpret_cast<const float*>(a.weight)[c]
-                      : to_f32(reinterpret_cast<const T*>(a.weight)[c]);
-    float s1 = 1.f;
-    if (MOD) {
-      s1 = 1.f + to_f32(reinterpret_cast<const T*>(a.scale)[b * a.ss + c]);
-      reinterpret_cast<T*>(a.dscale)[b * N + c] = from_f32<T>(w * A);
-      reinterpret_cast<T*>(a.dshift)[b * N + c] = from_f32<T>(D);
+  // the loop bound is padded to whole warps (nthreads is a multiple of 32), so every lane of a
+  // warp runs the same iterations and the shuffles see the full warp
+  const int64_t items = nq4 * S, items_pad = (items + 31) / 32 * 32;
+  for (int64_t it = tid; it < items_pad; it += nthreads) {
+    const bool live = it < items;
+    const int64_t c0 = (it / S) * 4;
+    const int s = (int)(it % S);
+    const float4 A4 = fold4(c0, s, live);
+    const float4 D4 = MOD ? fold4(N + c0, s, live) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 G4 = GATE == GATE_VEC ? fold4(2 * N + c0, s, live) : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (!live || s != 0) continue;
+    const float Av[4] = {A4.x, A4.y, A4.z, A4.w}, Dv[4] = {D4.x, D4.y, D4.z, D4.w};
+    const float Gv[4] = {G4.x, G4.y, G4.z, G4.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t c = c0 + j;
+      float w = a.w_f32 ? reinterpret_cast<const float*>(a.weight)[c]
+                        : to_f32(reinterpret_cast<const T*>(a.weight)[c]);
+      float s1 = 1.f;
+      if (MOD) {
+        s1 = 1.f + to_f32(reinterpret_cast<const T*>(a.scale)[b * a.ss + c]);
+        reinterpret_cast<T*>(a.dscale)[b * N + c] = from_f32<T>(w * Av[j]);
+        reinterpret_cast<T*>(a.dshift)[b * N + c] = from_f32<T>(Dv[j]);
+      }
+      if (GATE == GATE_VEC) reinterpret_cast<T*>(a.dgate)[b * N + c] = from_f32<T>(Gv[j]);
+      a.dwb[b * N + c] = s1 * Av[j];
     }
-    if (GATE == GATE_VEC) reinterpret_cast<T*>(a.dgate)[b * N + c] = from_f32<T>(G);
-    a.dwb[b * N + c] = s1 * A;
   }
   __threadfence();
   __syncthreads();

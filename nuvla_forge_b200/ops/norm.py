@@ -61,10 +61,23 @@ def set_impl(impl: int) -> None:
     """Select the norm kernel family: 0 = warp/team (default), 1 = bulk-copy pipelined."""
     nat.lib().nfb_norm_set_impl(int(impl))
     _impl_set[0] = True
+    _bwd_ctas.clear()
 
 
 def get_impl() -> int:
     return int(nat.lib().nfb_norm_get_impl())
+
+
+_bwd_ctas: dict[tuple[int, int, int], int] = {}
+
+
+def _bwd_P(M: int, N: int, B: int) -> int:
+    """CTAs per sample of the backward (depends on the shape, the SM count and the kernel family)."""
+    key = (M, N, B)
+    P = _bwd_ctas.get(key)
+    if P is None:
+        P = _bwd_ctas[key] = int(nat.lib().nfb_norm_bwd_P(M, N, B))
+    return P
 
 
 def check_status(device: torch.device | None = None) -> None:
@@ -91,9 +104,11 @@ def _rows(t: torch.Tensor, n: int) -> torch.Tensor:
     """2-D [rows, n] view with unit column stride and a 16-byte-aligned row stride."""
     if t.dim() != 2:
         t = t.reshape(-1, n)
+    if t.is_contiguous():  # rows of n % 8 == 0 elements keep every row 16-byte aligned
+        return t if t.data_ptr() % 16 == 0 else t.clone()
     es = t.element_size()
     if t.stride(1) != 1 or (t.stride(0) * es) % 16 or t.data_ptr() % 16:
-        t = t.contiguous()
+        t = t.contiguous()  # t is not contiguous here, so this copies into a fresh (aligned) allocation
     return t
 
 
@@ -144,7 +159,7 @@ def _bwd(ctx, dh_up, dout):
     dout = _rows(dout, N)
     if dh_up is not None:
         dh_up = _rows(dh_up, N)
-    P = int(nat.lib().nfb_norm_bwd_P(M, N, B))
+    P = _bwd_P(M, N, B)
     partials = torch.empty(B * P * 3 * N, dtype=torch.float32, device=dev)
     dwb = torch.empty(B * N, dtype=torch.float32, device=dev)
     tickets = ticket_buffer(dev, B + 1)
