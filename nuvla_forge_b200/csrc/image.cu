@@ -13,7 +13,8 @@
 //   zero so the patch GEMM's K stays a multiple of 8. One CTA owns one strip
 //   of p image rows: the strip is contiguous in HWC, so it is read once with
 //   16-byte loads into shared memory and the strip's patches are written out
-//   contiguously.
+//   contiguously (p = 14 / 16 with 16-byte image rows: the tiled kernel below;
+//   other shapes: a per-element gather through a column table).
 #include "common.cuh"
 
 namespace nfb {
@@ -102,6 +103,110 @@ __global__ void __launch_bounds__(256) image_patchify_kernel(const uint8_t* __re
   }
 }
 
+constexpr int kPatchGroup = 16;
+
+// Two floats as one packed pair of 2-byte values (round to nearest even).
+template <typename TO>
+__device__ __forceinline__ uint32_t pack_pair(float a, float b) {
+  if constexpr (std::is_same<TO, __nv_bfloat16>::value) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+
+// Tiled variant for even patch sizes with 16-byte image rows (the ViT's 448 x 448, p = 14). The
+// strip is copied into shared memory with each image row padded by 16 bytes; a task is one image
+// row (ky) of one patch (px): 3p consecutive bytes, read as aligned 32-bit words and realigned with
+// funnel shifts, written as bf16 pairs into a shared-memory copy of the strip's patch rows; then the
+// CTA writes its patch rows (contiguous in the output) with 16-byte stores, 16 patches at a time. A warp's 32 tasks are
+// 8 patches x 4 image rows and patch rows sit 2 * kpad + 16 bytes apart, so for p = 14 the pair
+// stores of a warp fall in 32 different banks (the per-element gather from one unpadded strip
+// was bound by bank conflicts).
+template <typename TO, int P>
+__global__ void __launch_bounds__(256) image_patchify_tiled_kernel(const uint8_t* __restrict__ in,
+                                                                   TO* __restrict__ out, int H, int W,
+                                                                   int kpad, NormConst k) {
+  static_assert(P % 2 == 0 && sizeof(TO) == 2, "even patch size, 2-byte output");
+  constexpr int K = 3 * P * P;
+  constexpr int RUN = 3 * P;                 // bytes of one image row of one patch
+  constexpr int NWORD = (RUN + 3 + 3) / 4;   // aligned words that cover the run at any offset
+  constexpr int kGroup = kPatchGroup;        // patch rows staged at a time
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int row_bytes = W * 3;               // multiple of 16 (checked by the launcher)
+  const int rs = row_bytes + 16;             // padded image row in shared memory
+  const int os = kpad * 2 + 16;              // padded patch row in shared memory
+  uint8_t* strip = smem;
+  uint8_t* rows = smem + P * rs;
+  const int rows_of_patches = H / P, pw = W / P;
+  const int64_t img = blockIdx.x / rows_of_patches;
+  const int py = blockIdx.x % rows_of_patches;
+  const uint4* src = reinterpret_cast<const uint4*>(in + (img * H + (int64_t)py * P) * row_bytes);
+  const int cpr_in = row_bytes / 16, nin = P * cpr_in;
+  constexpr int kLd = 5;
+  for (int base = threadIdx.x; base < nin; base += kLd * blockDim.x) {
+    uint4 v[kLd];
+#pragma unroll
+    for (int u = 0; u < kLd; ++u) {
+      const int i = base + u * blockDim.x;
+      if (i < nin) v[u] = __ldcs(src + i);
+    }
+#pragma unroll
+    for (int u = 0; u < kLd; ++u) {
+      const int i = base + u * blockDim.x;
+      if (i < nin) *reinterpret_cast<uint4*>(strip + (i / cpr_in) * rs + (i % cpr_in) * 16) = v[u];
+    }
+  }
+  // zero padding columns K..kpad of every patch row
+  const int nstage = pw < kGroup ? pw : kGroup;
+  for (int i = threadIdx.x; i < nstage * (kpad - K); i += blockDim.x) {
+    const int r = i / (kpad - K), c = K + i % (kpad - K);
+    *reinterpret_cast<TO*>(rows + r * os + c * 2) = from_f32<TO>(0.f);
+  }
+  __syncthreads();
+  // the strip's patches in groups of kGroup (staging for one group only keeps more CTAs resident)
+  const int cpr_out = kpad / 8, kyb = (P + 3) / 4;
+  TO* strip_out = out + ((img * rows_of_patches + py) * (int64_t)pw) * kpad;
+  for (int g0 = 0; g0 < pw; g0 += kGroup) {
+    const int ng = pw - g0 < kGroup ? pw - g0 : kGroup;
+    const int pxb = (ng + 7) / 8;
+    for (int t = threadIdx.x; t < pxb * kyb * 32; t += blockDim.x) {
+      const int blk = t >> 5;
+      const int r = (blk % pxb) * 8 + (t & 7);          // patch row within the group
+      const int ky = (blk / pxb) * 4 + ((t >> 3) & 3);
+      if (r >= ng || ky >= P) continue;
+      const int b0 = ky * rs + (g0 + r) * RUN;
+      const uint32_t* w = reinterpret_cast<const uint32_t*>(strip) + (b0 >> 2);
+      const uint32_t sh = (uint32_t)(b0 & 3) * 8;
+      uint32_t wv[NWORD];
+#pragma unroll
+      for (int i = 0; i < NWORD; ++i) wv[i] = w[i];
+      uint32_t v[(RUN + 3) / 4];
+#pragma unroll
+      for (int i = 0; i < (RUN + 3) / 4; ++i) v[i] = __funnelshift_r(wv[i], wv[i + 1], sh);
+      uint8_t* dst = rows + r * os + ky * P * 2;
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+#pragma unroll
+        for (int kx = 0; kx < P; kx += 2) {
+          const int t0 = kx * 3 + c, t1 = (kx + 1) * 3 + c;
+          const float f0 = (float)((v[t0 >> 2] >> (8 * (t0 & 3))) & 0xFFu);
+          const float f1 = (float)((v[t1 >> 2] >> (8 * (t1 & 3))) & 0xFFu);
+          *reinterpret_cast<uint32_t*>(dst + (c * P * P + kx) * 2) =
+              pack_pair<TO>(fmaf(f0, k.scale[c], k.bias[c]), fmaf(f1, k.scale[c], k.bias[c]));
+        }
+      }
+    }
+    __syncthreads();
+    uint4* dst = reinterpret_cast<uint4*>(strip_out + (int64_t)g0 * kpad);
+    for (int i = threadIdx.x; i < ng * cpr_out; i += blockDim.x)
+      dst[i] = *reinterpret_cast<const uint4*>(rows + (i / cpr_out) * os + (i % cpr_out) * 16);
+    if (g0 + kGroup < pw) __syncthreads();  // the next group reuses the staging rows
+  }
+}
+
 static NormConst make_const(const float* mean, const float* std) {
   NormConst k;
   for (int c = 0; c < 3; ++c) {
@@ -141,6 +246,25 @@ NFB_API int nfb_image_patchify(int out_dtype, const void* in, void* out, int64_t
   NormConst k = make_const(mean, std);
   cudaStream_t st = (cudaStream_t)stream;
   const int64_t grid = n_img * (H / p);
+  const size_t tiled_smem = (size_t)p * (W * 3 + 16) + (size_t)(W / p < kPatchGroup ? W / p : kPatchGroup) * (kpad * 2 + 16);
+  const bool aligned = ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+  if ((p == 14 || p == 16) && (W * 3) % 16 == 0 && aligned && tiled_smem <= 200 * 1024 &&
+      (out_dtype == kBF16 || out_dtype == kF16)) {
+#define NFB_PATCH_TILED(TO, P)                                                                               \
+    do {                                                                                                   \
+      cudaFuncSetAttribute(image_patchify_tiled_kernel<TO, P>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                           (int)tiled_smem);                                                               \
+      image_patchify_tiled_kernel<TO, P><<<(unsigned)grid, 256, tiled_smem, st>>>(                          \
+          (const uint8_t*)in, (TO*)out, H, W, kpad, k);                                                    \
+    } while (0)
+    if (out_dtype == kBF16) {
+      if (p == 14) NFB_PATCH_TILED(__nv_bfloat16, 14); else NFB_PATCH_TILED(__nv_bfloat16, 16);
+    } else {
+      if (p == 14) NFB_PATCH_TILED(__half, 14); else NFB_PATCH_TILED(__half, 16);
+    }
+#undef NFB_PATCH_TILED
+    return (int)cudaGetLastError();
+  }
   const size_t smem = ((size_t)kpad * 4 + 15) / 16 * 16 + ((size_t)p * W * 3 + 15) / 16 * 16;
   if (smem > 200 * 1024) return (int)cudaErrorInvalidValue;
   if (out_dtype == kBF16) {

@@ -206,6 +206,11 @@ def test_image_kernels():
     assert torch.count_nonzero(out[..., 588:]) == 0
     hwc2 = torch.randint(0, 256, (3, 128, 128, 3), dtype=torch.uint8, generator=g).to(DEV)
     assert rel_err(patchify_images(hwc2, 16), patchify_ref(hwc2, 16, 768)) < TOL[torch.bfloat16]
+    # 24 patches per strip: one full staging group of 16 and a partial one
+    hwc3 = torch.randint(0, 256, (2, 28, 336, 3), dtype=torch.uint8, generator=g).to(DEV)
+    out3 = patchify_images(hwc3, 14)
+    assert rel_err(out3, patchify_ref(hwc3, 14, 592)) < TOL[torch.bfloat16]
+    assert torch.count_nonzero(out3[..., 588:]) == 0
 
 
 @pytest.mark.parametrize("m,h,v,chunk", [(256, 128, 1000, 64), (1000, 384, 32000, 1024), (96, 64, 4096, 4096)])
