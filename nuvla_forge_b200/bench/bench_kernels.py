@@ -14,6 +14,9 @@ Byte counts are the algorithmic minimum of each op:
   adaLN fwd+bwd: read x, y; write h, out; read dh, dout, h, y; write dx, dy = 10 tensors
   SwiGLU fwd+bwd: read a, b; write out; read dout, a, b; write da, db = 8 tensors
   CE fwd+bwd: FLOPs of 3 GEMMs of 2*M*H*V each (logits, dW, dh)
+  patchify: read the uint8 frames, write the bf16 patch rows (the reference normalises whole frames
+    in eager PyTorch and cuts patches inside its Conv2d; "eager" here is that normalisation plus
+    the unfold into patch rows)
 """
 
 from __future__ import annotations
@@ -48,6 +51,26 @@ def timeit(fn, iters=20, warmup=5, flush=True):
     for _ in range(iters):
         if flush:
             flush_l2()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    times.sort()
+    return times[len(times) // 2]
+
+
+def timeit_device(fn, iters=20, warmup=5):
+    """Median CUDA-event time of fn's GPU work alone (ms): L2 flushed, then a ~0.1 ms device sleep
+    queued before the start event so the host's launch overhead overlaps it."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        flush_l2()
+        torch.cuda._sleep(200_000)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         fn()
@@ -123,6 +146,19 @@ def bench_swiglu(m, n, dtype, peaks, ref):
     res["native_ms"] = timeit(run(fused_swiglu))
     if ref is not None:
         res["reference_triton_ms"] = timeit(run(ref.fused_swiglu))
+    from .. import _native as nat
+    if nat.HAS_NATIVE:
+        # the two kernels alone (no autograd between them, L2 flushed before each, device time only)
+        out, da, db = (torch.empty(m, n, device="cuda", dtype=dtype) for _ in range(3))
+        dc, s = nat.dtype_code(dtype), nat.stream()
+        res["native_fwd_kernel_ms"] = timeit_device(lambda: nat.call(
+            "nfb_swiglu_fwd", dc, nat.ptr(a), nat.ptr(b), nat.ptr(out), m, n, n, n, n, s))
+        res["native_bwd_kernel_ms"] = timeit_device(lambda: nat.call(
+            "nfb_swiglu_bwd", dc, nat.ptr(dout), nat.ptr(a), nat.ptr(b), nat.ptr(da), nat.ptr(db), m, n, n, n, n, n, n,
+            s))
+        kb = bandwidth_gb_s(8 * m * n * torch.finfo(dtype).bits // 8,
+                            res["native_fwd_kernel_ms"] + res["native_bwd_kernel_ms"])
+        res["kernels_gb_s"], res["kernels_frac_of_measured_hbm"] = kb, kb / peaks["hbm_gbs"]
     moved = 8 * m * n * torch.finfo(dtype).bits // 8
     bw = bandwidth_gb_s(moved, res["native_ms"])
     res.update(bytes=moved, achieved_gb_s=bw, frac_of_measured_hbm=bw / peaks["hbm_gbs"],
@@ -164,6 +200,22 @@ def bench_ce(m, h, v, dtype, peaks, ref):
     return res
 
 
+def bench_patchify(n, hw, p, peaks):
+    from ..ops import patchify_images
+    from ..ops.image import patch_kpad
+    from ..ops.reference import patchify_ref
+    img = torch.randint(0, 256, (n, hw, hw, 3), dtype=torch.uint8, device="cuda")
+    kpad = patch_kpad(p)
+    res = {"shape": f"{n}x{hw}x{hw}x3 p{p}"}
+    res["eager_ms"] = timeit(lambda: patchify_ref(img, p, kpad, torch.bfloat16))
+    res["native_ms"] = timeit(lambda: patchify_images(img, p))
+    moved = img.numel() + n * (hw // p) ** 2 * kpad * 2
+    bw = bandwidth_gb_s(moved, res["native_ms"])
+    res.update(bytes=moved, achieved_gb_s=bw, frac_of_measured_hbm=bw / peaks["hbm_gbs"],
+               roofline=roofline_note(bw, peaks["hbm_gbs"]), speedup_vs_eager=res["eager_ms"] / res["native_ms"])
+    return res
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default="reports/kernels.json")
@@ -176,7 +228,7 @@ def main(argv=None):
     ref = None if args.no_reference else reference_kernels()
     dt = torch.bfloat16
     report = {"device": torch.cuda.get_device_name(0), "peaks": peaks, "reference_triton": ref is not None,
-              "adaln": [], "swiglu": [], "cross_entropy": []}
+              "adaln": [], "swiglu": [], "cross_entropy": [], "patchify": []}
     adaln_shapes = [(8, 2048, 1536)] + ([] if args.quick else [(8, 32, 384), (8, 128, 384), (16, 256, 768),
                                                                 (8, 512, 1024), (4, 1024, 1536)])
     swiglu_shapes = [(16384, 4096)] + ([] if args.quick else [(8192, 1536), (16384, 1536), (32768, 3072)])
@@ -201,6 +253,10 @@ def main(argv=None):
               f" | ref-triton {r.get('reference_triton_ms', float('nan')):7.2f} ms {r.get('reference_triton_peak_mib', 0):7.0f} MiB"
               f" | native {r.get('native_ms', float('nan')):7.2f} ms {r.get('native_peak_mib', 0):7.0f} MiB"
               f" | {r.get('roofline', '')}")
+    for s in [(96, 448, 14)]:
+        r = bench_patchify(*s, peaks)
+        report["patchify"].append(r)
+        print(f"patchify {r['shape']:<18} eager {r['eager_ms']:7.3f} | native {r['native_ms']:7.3f} ms | {r['roofline']}")
     out = Path(args.out)
     out.parent.mkdir(parents=True, exist_ok=True)
     out.write_text(json.dumps(report, indent=2))

@@ -51,6 +51,23 @@ def section_kernels(lines, k):
                          f"{fmt(r.get('native_ms'), '.3f')} | {fmt(r.get('speedup_vs_reference_triton'))}x | "
                          f"{fmt(r.get('achieved_gb_s'), '.0f')} | {fmt(100 * r.get('frac_of_measured_hbm', 0), '.0f')}% |")
         lines.append("")
+        timed = [r for r in k.get(key, []) if r.get("native_fwd_kernel_ms")]
+        if timed:
+            lines += ["The two native kernels alone (L2 flushed before each; the table above times forward, "
+                      "autograd and backward back to back):", ""]
+            for r in timed:
+                lines.append(f"* `{r['shape']}`: forward {fmt(r['native_fwd_kernel_ms'], '.3f')} ms + backward "
+                             f"{fmt(r['native_bwd_kernel_ms'], '.3f')} ms = {fmt(r.get('kernels_gb_s'), '.0f')} GB/s, "
+                             f"{fmt(100 * r.get('kernels_frac_of_measured_hbm', 0), '.0f')}% of measured HBM")
+            lines.append("")
+    if k.get("patchify"):
+        lines += ["### Patchify (uint8 HWC frames -> normalised bf16 patch rows)", "",
+                  "| shape | eager ms | native ms | vs eager | achieved GB/s | of measured HBM |", "|---|---|---|---|---|---|"]
+        for r in k["patchify"]:
+            lines.append(f"| `{r['shape']}` | {fmt(r.get('eager_ms'), '.3f')} | {fmt(r.get('native_ms'), '.3f')} | "
+                         f"{fmt(r.get('speedup_vs_eager'))}x | {fmt(r.get('achieved_gb_s'), '.0f')} | "
+                         f"{fmt(100 * r.get('frac_of_measured_hbm', 0), '.0f')}% |")
+        lines.append("")
     lines += ["### Cross entropy (fwd+bwd; peak memory: lower is better)", "",
               "| shape | naive ms / MiB | reference Triton ms / MiB | native ms / MiB | vs Triton | TFLOP/s (3 GEMMs) |",
               "|---|---|---|---|---|---|"]
