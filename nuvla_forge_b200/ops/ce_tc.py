@@ -4,9 +4,10 @@ The [M, V] logits live only in tensor memory: pass 1 turns each 128x256 logit
 tile into per-row online-softmax partials, a merge kernel produces the
 log-sum-exp and the per-row losses, and pass 2 recomputes the tile and writes
 ``(softmax - onehot) / count`` in bf16 for one row chunk at a time, which the
-two gradient GEMMs consume on the same tcgen05 core (d_hidden = dl @ W with W
-read MN-major; d_W += dl^T @ h with both operands MN-major, accumulated in
-fp32; ``NFB_CE_TC_GRAD_GEMM=0`` hands them to cuBLAS instead). Like the reference
+two gradient GEMMs consume on the CTA-pair tcgen05 core of the linear layers
+(d_hidden = dl @ W with W read MN-major; d_W += dl^T @ h with both operands
+MN-major, accumulated in fp32; ``NFB_CE_TC_GRAD_GEMM=0`` hands them to cuBLAS
+instead). Like the reference
 (nuvla_forge/kernels/chunked_ce.py:120-182) the gradients are produced during
 forward and backward only scales them; unlike it, no fp32 logit tile exists and
 nothing synchronises the host.
@@ -19,6 +20,7 @@ import os
 import torch
 
 from .. import _native as nat
+from . import linear as _linear
 from .chunked_ce import count_valid, register_tc
 
 _status: dict[int, torch.Tensor] = {}
@@ -89,8 +91,9 @@ class _CrossEntropyTC(torch.autograd.Function):
         nat.call("nfb_ce_tc_merge", nat.ptr(pmax), nat.ptr(psum), nat.ptr(tlogit), nat.ptr(tg), nat.ptr(count), M, V,
                  ignore_index, nat.ptr(lse), nat.ptr(loss_rows), s)
         d_hidden = torch.empty((M, H), dtype=hidden.dtype, device=dev)
-        d_weight = torch.zeros((V, H), dtype=torch.float32, device=dev)
         native_grad = _native_grad_gemms(V, H, hidden.dtype) and h.stride(1) == 1
+        # the first chunk's d_W GEMM overwrites, so the native path needs no zero fill
+        d_weight = (torch.empty if native_grad else torch.zeros)((V, H), dtype=torch.float32, device=dev)
         for r0 in range(0, M, chunk_rows):
             r1 = min(r0 + chunk_rows, M)
             hc = h[r0:r1]
@@ -99,9 +102,11 @@ class _CrossEntropyTC(torch.autograd.Function):
                      nat.ptr(lse[r0:r1]), nat.ptr(count), ignore_index, r1 - r0, V, H, nat.ptr(dl), dl.stride(0),
                      nat.ptr(st), s)
             if native_grad:
-                # d_hidden[chunk] = dl @ W (W read as an MN-major B); d_W += dl^T @ h (both MN-major)
-                tc_gemm(dl, w, b_mn=True, out=d_hidden[r0:r1])
-                tc_gemm(dl, hc, a_mn=True, b_mn=True, out=d_weight, accumulate=True)
+                # on the CTA-pair core of the linear layers: d_hidden[chunk] = dl @ W (W read as an
+                # MN-major B, the input-gradient shape); d_W (+)= dl^T @ h (both MN-major, fp32, the
+                # weight-gradient shape, added by TMA reductions)
+                _linear.gemm(dl, w, b_mn=True, out=d_hidden[r0:r1])
+                _linear.gemm_acc(dl, hc, d_weight, a_mn=True, b_mn=True, accumulate=r0 > 0)
             else:
                 d_hidden[r0:r1] = torch.mm(dl, w).to(hidden.dtype)
                 d_weight += torch.mm(dl.t(), hc, out_dtype=torch.float32)
