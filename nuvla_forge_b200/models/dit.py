@@ -25,7 +25,7 @@ import torch.nn.functional as F
 from torch import nn
 
 from ..ops import fused_adaln_residual_rmsnorm
-from .layers import Attention, RMSNorm, SwiGLUMLP, TimestepEmbedder, linear, modulate
+from .layers import Attention, RMSNorm, SwiGLUMLP, TimestepEmbedder, checkpointed, linear, modulate
 
 
 class DiTBlock(nn.Module):
@@ -44,6 +44,7 @@ class DiTBlock(nn.Module):
         # adaLN-Zero: every block starts as the identity on the residual stream.
         nn.init.zeros_(self.cond[1].weight)
         nn.init.zeros_(self.cond[1].bias)
+        self.grad_checkpoint = False  # recompute the block in backward (models/layers.checkpointed)
 
     def _cond(self, c):
         lin = self.cond[1]
@@ -52,6 +53,9 @@ class DiTBlock(nn.Module):
     def forward_chain(self, x, c, context, pending=None):
         """Fused path. ``pending`` = (y, gate): the previous block's gated branch
         output not yet added to x. Returns (x, (mlp_out, gate2))."""
+        return checkpointed(self, self._chain, x, c, context, pending)
+
+    def _chain(self, x, c, context, pending):
         b, t, _ = x.shape
         shift1, scale1, gate1, shift2, scale2, gate2 = self._cond(c).chunk(6, dim=-1)
         if pending is None:
@@ -70,6 +74,9 @@ class DiTBlock(nn.Module):
         if self.fused:
             x, (m, g) = self.forward_chain(x, c, context)
             return x + g.unsqueeze(1) * m
+        return checkpointed(self, self._forward_unfused, x, c, context)
+
+    def _forward_unfused(self, x, c, context):
         shift1, scale1, gate1, shift2, scale2, gate2 = self._cond(c).chunk(6, dim=-1)
         x = x + gate1.unsqueeze(1) * self.attn(modulate(self.norm1(x), shift1, scale1))
         x = x + self.cross(self.norm_cross(x), context)

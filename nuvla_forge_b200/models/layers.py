@@ -25,6 +25,7 @@ from __future__ import annotations
 import math
 
 import torch
+import torch.utils.checkpoint
 import torch.nn.functional as F
 from torch import nn
 
@@ -215,11 +216,21 @@ class SwiGLUMLP(nn.Module):
         return _linear(act, self.w_down.weight, residual=residual)
 
 
+def checkpointed(block: nn.Module, fn, *args):
+    """``fn(*args)``, recomputed in backward when ``block.grad_checkpoint`` is set and autograd is
+    recording: only the block's inputs stay alive between forward and backward
+    (torch.utils.checkpoint, non-reentrant, RNG state preserved)."""
+    if getattr(block, "grad_checkpoint", False) and torch.is_grad_enabled():
+        return torch.utils.checkpoint.checkpoint(fn, *args, use_reentrant=False)
+    return fn(*args)
+
+
 class TransformerBlock(nn.Module):
     """Pre-norm block: x + attn(norm1(x)), then + mlp(norm2(x)).
 
     Parity: nuvla_forge/model/nuvla.py:47-59 (RMSNorm, fused-qkv attention,
-    SwiGLU with hidden 4*dim by default).
+    SwiGLU with hidden 4*dim by default). ``grad_checkpoint = True`` recomputes the
+    block in backward, on the fused (``forward_chain``) and the unfused path alike.
     """
 
     def __init__(self, dim: int, heads: int, fused: bool = True, kv_heads: int | None = None,
@@ -229,8 +240,12 @@ class TransformerBlock(nn.Module):
         self.attn = Attention(dim, heads, kv_heads=kv_heads, causal=causal, fused=fused)
         self.norm2 = RMSNorm(dim, fused=fused)
         self.mlp = SwiGLUMLP(dim, ffn or dim * 4, fused=fused)
+        self.grad_checkpoint = False
 
     def forward(self, x):
+        return checkpointed(self, self._forward, x)
+
+    def _forward(self, x):
         x = self.attn(self.norm1(x), residual=x)
         return self.mlp(self.norm2(x), residual=x)
 
@@ -240,6 +255,9 @@ class TransformerBlock(nn.Module):
         ``pending`` is the previous block's MLP output not yet added to ``x``.
         Returns (x, this block's MLP output, not yet added).
         """
+        return checkpointed(self, self._chain, x, pending)
+
+    def _chain(self, x, pending):
         ref = not self.norm1.fused
         if pending is None:
             h = self.norm1(x)

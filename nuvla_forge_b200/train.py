@@ -58,7 +58,7 @@ class Trainer:
     def __init__(self, cfg: NuVLAConfig, info: DistInfo | None = None, *, lr: float = 3e-4,
                  weight_decay: float = 0.01, max_grad_norm: float = 1.0, bucket_mb: float = 25.0,
                  comm: str = "auto", fsdp: bool = False, grad_accum: int = 1, no_sync_accum: bool = True,
-                 bf16: bool = True, grad_checkpoint: bool = False, seed: int = 1234, compile: bool = False,
+                 bf16: bool = True, grad_checkpoint: bool | str = False, seed: int = 1234, compile: bool = False,
                  fused_gather: bool | None = None, heartbeat_s: float = 0.5, peer_timeout_s: float = 30.0):
         self.info = info or setup_distributed()
         self.cfg = cfg
@@ -68,8 +68,11 @@ class Trainer:
         torch.manual_seed(seed)  # same init on every rank; DDP also broadcasts rank 0's weights
         model = NuVLA(cfg).to(self.device)
         torch.manual_seed(seed + self.info.rank)
-        if grad_checkpoint:
-            _checkpoint_encoder(model)
+        ckpt = set_grad_checkpointing(model, grad_checkpoint)
+        if ckpt and fsdp:
+            # the recompute replays a block's forward inside backward without the module call that
+            # gathers an FSDP unit's weights, so the two are not combined
+            raise ValueError("activation checkpointing is not supported together with --fsdp")
         if compile:
             model = torch.compile(model)
         param_dtype = torch.bfloat16 if (bf16 and self.device.type == "cuda") else torch.float32
@@ -164,17 +167,34 @@ class Trainer:
         return sum(p.numel() for p in self.module.parameters())
 
 
-def _checkpoint_encoder(model: NuVLA) -> None:
-    """Recompute vision blocks in backward (parity: nuvla_forge/train.py:139-152)."""
-    from torch.utils.checkpoint import checkpoint
+CHECKPOINT_STACKS = ("encoder", "fusion", "text", "dit")
 
-    for blk in model.encoder.blocks:
-        inner = blk.forward
 
-        def fwd(*a, _inner=inner, **kw):
-            return checkpoint(_inner, *a, use_reentrant=False, **kw)
+def set_grad_checkpointing(model: NuVLA, parts) -> list[str]:
+    """Recompute the blocks of the chosen stacks in backward instead of keeping their activations.
 
-        blk.forward = fwd
+    ``parts``: False / None / "none" (off); True (the vision encoder's blocks, as the reference's
+    ``--grad-checkpoint``, nuvla_forge/train.py:139-152); "all"; or stack names from
+    ``CHECKPOINT_STACKS`` as a comma-separated string or a sequence. Works on the fused block chain
+    the native path runs (``forward_chain``) and on the unfused blocks. Returns the stacks enabled.
+    """
+    if parts is None or parts is False or parts == "none" or parts == "":
+        chosen: list[str] = []
+    elif parts is True:
+        chosen = ["encoder"]
+    elif parts == "all":
+        chosen = list(CHECKPOINT_STACKS)
+    else:
+        chosen = [p.strip() for p in parts.split(",")] if isinstance(parts, str) else list(parts)
+    unknown = [p for p in chosen if p not in CHECKPOINT_STACKS]
+    if unknown:
+        raise ValueError(f"unknown checkpoint stack(s) {unknown}; choose from {CHECKPOINT_STACKS} or 'all'")
+    stacks = {"encoder": model.encoder.blocks, "fusion": model.fusion, "text": model.text_blocks,
+              "dit": model.dit.blocks}
+    for name, blocks in stacks.items():
+        for blk in blocks:
+            blk.grad_checkpoint = name in chosen
+    return chosen
 
 
 # ----------------------------------------------------------------------
@@ -196,7 +216,11 @@ def build_args(argv=None):
     p.add_argument("--fast-loader", action="store_true")
     p.add_argument("--cuda-prefetch", action="store_true")
     p.add_argument("--bf16", action="store_true")
-    p.add_argument("--grad-checkpoint", action="store_true")
+    p.add_argument("--grad-checkpoint", action="store_true",
+                   help="recompute the vision encoder's blocks in backward (as the reference)")
+    p.add_argument("--grad-checkpoint-blocks", default=None,
+                   help="recompute these block stacks in backward: comma-separated from "
+                        "encoder,fusion,text,dit, or 'all' (overrides --grad-checkpoint)")
     p.add_argument("--ddp-bucket-mb", type=float, default=25.0)
     p.add_argument("--no-sync-accum", action="store_true")
     p.add_argument("--fsdp", action="store_true")
@@ -311,7 +335,8 @@ def main(argv=None):
         flash_attn.enable(True)
     trainer = Trainer(cfg, info, lr=args.lr, max_grad_norm=args.max_grad_norm, bucket_mb=args.ddp_bucket_mb,
                       comm=args.comm, fsdp=args.fsdp, grad_accum=args.grad_accum,
-                      no_sync_accum=args.no_sync_accum, bf16=args.bf16, grad_checkpoint=args.grad_checkpoint,
+                      no_sync_accum=args.no_sync_accum, bf16=args.bf16,
+                      grad_checkpoint=args.grad_checkpoint_blocks or args.grad_checkpoint,
                       seed=args.seed, compile=args.compile, fused_gather=False if args.no_fused_gather else None,
                       peer_timeout_s=args.peer_timeout)
     start_step = 0
