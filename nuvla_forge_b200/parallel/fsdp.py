@@ -491,7 +491,10 @@ class FullyShardedDataParallel(nn.Module):
             setattr(mod, meth, wrapped)
 
     def _pre_forward(self, u: _Unit) -> None:
-        self._gather(u, lazy=self.fuse_ag_gemm)
+        # A unit recomputed in backward (activation checkpointing) is gathered in full: the
+        # recompute has to replay the forward's ops, and the GEMM-fused gather exists only in the
+        # forward (in backward the unit is gathered before its recompute).
+        self._gather(u, lazy=self.fuse_ag_gemm and not getattr(u.module, "grad_checkpoint", False))
         if u not in self._order:
             self._order.append(u)
         u.bwd_gathered = False

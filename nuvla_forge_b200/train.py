@@ -68,11 +68,7 @@ class Trainer:
         torch.manual_seed(seed)  # same init on every rank; DDP also broadcasts rank 0's weights
         model = NuVLA(cfg).to(self.device)
         torch.manual_seed(seed + self.info.rank)
-        ckpt = set_grad_checkpointing(model, grad_checkpoint)
-        if ckpt and fsdp:
-            # the recompute replays a block's forward inside backward without the module call that
-            # gathers an FSDP unit's weights, so the two are not combined
-            raise ValueError("activation checkpointing is not supported together with --fsdp")
+        set_grad_checkpointing(model, grad_checkpoint)
         if compile:
             model = torch.compile(model)
         param_dtype = torch.bfloat16 if (bf16 and self.device.type == "cuda") else torch.float32

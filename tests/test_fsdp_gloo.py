@@ -284,3 +284,92 @@ def test_fsdp_gradient_owner_rejects_a_second_gradient():
     out = run_ranks(_fsdp_owner_train, 2, args=(1, 1, True))
     assert all(st != "ok" for st, _ in out.values()), out
     assert all("second gradient" in str(msg) for _, msg in out.values()), out
+
+
+class CkptBlock(Block):
+    """Block recomputed in backward through models.layers.checkpointed, as the model's blocks are."""
+
+    def __init__(self, d):
+        super().__init__(d)
+        self.grad_checkpoint = True
+        self.recomputed = 0
+
+    def forward(self, x):
+        from nuvla_forge_b200.models.layers import checkpointed
+
+        return checkpointed(self, self._body, x)
+
+    def _body(self, x):
+        if torch.is_grad_enabled() and not torch.is_inference_mode_enabled():
+            self.recomputed += 1
+        return x + self.b(torch.tanh(self.a(x)))
+
+
+class CkptNet(Net):
+    def __init__(self):
+        super().__init__()
+        torch.manual_seed(0)  # same parameters as Net() under the same seed
+        fresh = Net()
+        self.blocks = nn.ModuleList([CkptBlock(16) for _ in range(3)])
+        self.load_state_dict(fresh.state_dict())
+
+
+def _fsdp_ckpt_train(rank, world, steps, accum):
+    from nuvla_forge_b200.parallel.fsdp import FullyShardedDataParallel
+
+    torch.manual_seed(0)
+    net = CkptNet()
+    fsdp = FullyShardedDataParallel(net, unit_types=(CkptBlock,))
+    opt = fsdp.make_optimizer(lr=1e-2, weight_decay=0.01, max_grad_norm=0.5)
+    for step in range(steps):
+        for m in range(accum):
+            x, y = _data(step, rank, m)
+            ctx = fsdp.no_sync() if m < accum - 1 else torch.enable_grad()
+            with ctx:
+                (((fsdp(x) - y) ** 2).mean() / accum).backward()
+        opt.step()
+        opt.zero_grad()
+    # each block ran its body twice per micro-step: forward, then the recompute in backward
+    assert all(b.recomputed == 2 * steps * accum for b in net.blocks), [b.recomputed for b in net.blocks]
+    views = fsdp.full_master_views()
+    if rank == 0:
+        return {n: views[id(p)].clone() for n, p in net.named_parameters()}
+    return None
+
+
+def test_fsdp_with_activation_checkpointing_matches_single_process():
+    """Units recomputed in backward: FSDP's output hook gathers the unit before the recompute reads
+    its weights, so training matches the single-process reference."""
+    out = run_ranks(_fsdp_ckpt_train, 2, args=(3, 2))
+    _check(out, _reference(2, 3, 2, 0.5))
+
+
+def _fsdp_lazy_flags(rank, world):
+    from nuvla_forge_b200.parallel.fsdp import FullyShardedDataParallel
+
+    torch.manual_seed(0)
+    net = Net()
+    net.blocks[1].grad_checkpoint = True
+    fsdp = FullyShardedDataParallel(net, unit_types=(Block,))
+    fsdp.fuse_ag_gemm = True      # as on GPUs; record the gather mode instead of gathering lazily
+    seen = []
+    real = fsdp._gather
+
+    def gather(u, lazy=False):
+        seen.append((u.name, lazy))
+        return real(u, lazy=False)
+
+    fsdp._gather = gather
+    x, y = _data(0, rank, 0)
+    with torch.no_grad():
+        fsdp(x)
+    return seen
+
+
+def test_fsdp_checkpointed_unit_skips_the_fused_gather():
+    """With the GEMM-fused gather on, only a checkpointed unit is gathered in full in forward."""
+    out = run_ranks(_fsdp_lazy_flags, 2)
+    assert all(st == "ok" for st, _ in out.values()), out
+    modes = dict(out[0][1])
+    blocks = sorted(n for n in modes if "blocks" in n)
+    assert [modes[n] for n in blocks] == [True, False, True], modes
