@@ -187,13 +187,14 @@ def call(name: str, *args) -> int:
     return rc
 
 
+_ERR_NAMES = {1: "cudaErrorInvalidValue", 2: "cudaErrorMemoryAllocation", 98: "cudaErrorInvalidDeviceFunction",
+              209: "cudaErrorNoKernelImageForDevice", 700: "cudaErrorIllegalAddress",
+              701: "cudaErrorLaunchOutOfResources", 715: "cudaErrorIllegalInstruction",
+              716: "cudaErrorMisalignedAddress", 719: "cudaErrorLaunchFailure"}
+
+
 def _err_name(rc: int) -> str:
-    try:
-        from torch.cuda import cudart  # noqa: F401
-        return {1: "cudaErrorInvalidValue", 2: "cudaErrorMemoryAllocation", 98: "cudaErrorInvalidDeviceFunction",
-                209: "cudaErrorNoKernelImageForDevice", 700: "cudaErrorIllegalAddress"}.get(rc, "see cuda_runtime_api.h")
-    except Exception:  # noqa: BLE001
-        return "?"
+    return _ERR_NAMES.get(rc, "see cuda_runtime_api.h")
 
 
 # Pointers and streams are passed as plain ints (None for NULL): every entry point declares

@@ -787,8 +787,6 @@ class FullyShardedDataParallel(nn.Module):
 
     def load_full_state_dict(self, sd: dict) -> None:
         """Load a full reference-format state dict (every rank reads the same file)."""
-        from ..checkpoint import _fp32_state_dict  # noqa: F401  (same key mapping)
-
         tmp = {id(s.param): torch.zeros(s.shape, dtype=torch.float32, device=self.device)
                for u in self.units for s in u.segs}
         saved = {}
