@@ -249,6 +249,35 @@ def test_chunked_ce_all_ignored():
     assert torch.count_nonzero(hid.grad) == 0
 
 
+def test_chunked_ce_peak_memory_below_naive():
+    """The logits never exist as an [M, V] fp32 tensor: the native CE's peak allocation during
+    forward + backward stays below half the naive CE's and below one fp32 logits tensor."""
+    _nat()
+    from nuvla_forge_b200.ops import chunked_cross_entropy
+    from nuvla_forge_b200.ops.reference import chunked_cross_entropy_ref
+
+    m, h, v = 4096, 384, 32000
+    g = _gen(11)
+    hid = torch.randn(m, h, generator=g, device=DEV).to(torch.bfloat16).requires_grad_(True)
+    w = (torch.randn(v, h, generator=g, device=DEV) * 0.05).to(torch.bfloat16).requires_grad_(True)
+    tgt = torch.randint(0, v, (m,), generator=g, device=DEV)
+
+    def peak(fn):
+        hid.grad = w.grad = None
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        torch.cuda.reset_peak_memory_stats()
+        base = torch.cuda.memory_allocated()
+        fn().backward()
+        torch.cuda.synchronize()
+        return torch.cuda.max_memory_allocated() - base
+
+    native = peak(lambda: chunked_cross_entropy(hid, w, tgt, chunk_size=1024))
+    naive = peak(lambda: chunked_cross_entropy_ref(hid, w, tgt))
+    assert native < naive / 2, (native, naive)
+    assert native < 0.75 * m * v * 4, native
+
+
 def test_flat_adamw_matches_torch():
     _nat()
     from nuvla_forge_b200.optim.adamw import FlatAdamW
