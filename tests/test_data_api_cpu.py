@@ -89,6 +89,19 @@ def test_report_generator_never_invents_numbers(tmp_path):
         {"model": "tiny", "steps": 4, "rows": [{"batch": 1, "eager_ms": 2.0, "graphed_ms": 1.0, "speedup": 2.0}]}))
     report.main(["--reports", str(tmp_path / "reports"), "--out", str(out)])
     assert "| 1 | 2.00 | 1.00 | 2.00x |" in out.read_text()
+    # kernel microbench: patchify table and the device-only SwiGLU lines come from the JSON
+    (tmp_path / "reports" / "kernels.json").write_text(json.dumps({
+        "device": "dev", "peaks": {"hbm_gbs": 1000.0, "bf16_tflops": 1.0, "source": "test"},
+        "reference_triton": False, "adaln": [], "cross_entropy": [],
+        "swiglu": [{"shape": "8x8", "eager_ms": 3.0, "native_ms": 2.0, "achieved_gb_s": 500.0,
+                    "frac_of_measured_hbm": 0.5, "native_fwd_kernel_ms": 0.25, "native_bwd_kernel_ms": 0.5,
+                    "kernels_gb_s": 900.0, "kernels_frac_of_measured_hbm": 0.9}],
+        "patchify": [{"shape": "1x28x28x3 p14", "eager_ms": 1.0, "native_ms": 0.125, "speedup_vs_eager": 8.0,
+                      "achieved_gb_s": 600.0, "frac_of_measured_hbm": 0.6}]}))
+    report.main(["--reports", str(tmp_path / "reports"), "--out", str(out)])
+    text = out.read_text()
+    assert "forward 0.250 ms + backward 0.500 ms = 900 GB/s, 90% of measured HBM" in text
+    assert "| `1x28x28x3 p14` | 1.000 | 0.125 | 8.00x | 600 | 60% |" in text
 
 
 def test_reference_state_dict_schema():

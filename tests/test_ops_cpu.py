@@ -115,3 +115,28 @@ def test_model_forward_backward_cpu(preset, over):
     grads = [p.grad for p in model.parameters() if p.requires_grad]
     assert sum(g is not None for g in grads) > 0.9 * len(grads)
     assert all(torch.isfinite(g).all() for g in grads if g is not None)
+
+
+def test_norm_rows_view_alignment():
+    """_rows hands the kernels 2-D rows with unit column stride on a 16-byte boundary: aligned
+    tensors pass through untouched, misaligned or strided ones are copied."""
+    from nuvla_forge_b200.ops.norm import _rows
+
+    n = 64
+    t = torch.randn(8, n, dtype=torch.bfloat16)
+    assert _rows(t, n) is t
+    assert _rows(t.view(2, 4, n), n).data_ptr() == t.data_ptr()
+    # a contiguous view that starts 2 bytes into the storage
+    flat = torch.randn(8 * n + 1, dtype=torch.bfloat16)
+    mis = flat[1:].view(8, n)
+    assert mis.is_contiguous() and mis.data_ptr() % 16 != 0
+    got = _rows(mis, n)
+    assert got.data_ptr() % 16 == 0 and got.is_contiguous() and torch.equal(got, mis)
+    # a column slice of a wider tensor: unit stride, rows 16-byte aligned -> read in place
+    wide = torch.randn(8, 3 * n, dtype=torch.bfloat16)
+    mid = wide[:, n:2 * n]
+    assert _rows(mid, n).data_ptr() == mid.data_ptr()
+    # a transposed view: copied into packed rows
+    tr = torch.randn(n, 8, dtype=torch.bfloat16).t()
+    got = _rows(tr, n)
+    assert got.stride() == (n, 1) and torch.equal(got, tr)
