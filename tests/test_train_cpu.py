@@ -36,12 +36,13 @@ def test_train_cli_writes_report(tmp_path):
 
     stats = main(["--model-config", "tiny", "--steps", "1", "--warmup-steps", "0", "--batch-size", "1",
                   "--num-workers", "0", "--out", str(tmp_path), "--tag", "cpu", "--save-every", "1",
-                  "--ckpt-dir", str(tmp_path / "ck")])
+                  "--ckpt-dir", str(tmp_path / "ck"), "--grad-checkpoint-blocks", "fusion,dit"])
     rep = json.loads((tmp_path / "train-cpu.json").read_text())
     for k in ("step_ms", "n_steps", "samples_per_sec", "world_size", "global_batch", "flags", "model",
               "exposed_comm_ms"):
         assert k in rep, k
     assert stats["n_steps"] == 1 and rep["world_size"] == 1
+    assert rep["flags"]["grad_checkpoint_blocks"] == "fusion,dit"
     ck = torch.load(tmp_path / "ck" / "step-0000001.pt", weights_only=False)
     assert ck["step"] == 1 and "encoder.patch.weight" in ck["model"]
     assert os.path.getsize(tmp_path / "ck" / "step-0000001.pt") > 1e6
