@@ -8,7 +8,7 @@ import torch
 from _mp import run_ranks
 
 
-def _config1(rank, world):
+def _config1(rank, world, ckpt=False):
     from nuvla_forge_b200.data import SampleSpec, SyntheticBatchSource
     from nuvla_forge_b200.models import NuVLAConfig
     from nuvla_forge_b200.parallel.dist import DistInfo
@@ -16,7 +16,7 @@ def _config1(rank, world):
 
     cfg = NuVLAConfig.preset("tiny", fused=False)
     info = DistInfo(rank, world, rank, torch.device("cpu"), "gloo")
-    tr = Trainer(cfg, info, grad_accum=2, no_sync_accum=True, bf16=False, seed=0)
+    tr = Trainer(cfg, info, grad_accum=2, no_sync_accum=True, bf16=False, seed=0, grad_checkpoint=ckpt)
     src = SyntheticBatchSource(SampleSpec.for_model(cfg), 2, seed=0, rank=rank, world=world, pin=False)
     losses = [float(tr.step([src.batch(2 * s), src.batch(2 * s + 1)])) for s in range(2)]
     return {"losses": losses, "master": tr.model.space.master[:4096].clone(), "params": tr.num_parameters()}
@@ -29,6 +29,17 @@ def test_config1_gloo_world2_replicas_agree():
     assert torch.equal(a["master"], b["master"])
     assert all(l == l and l > 0 for l in a["losses"] + b["losses"])
     assert 20e6 < a["params"] < 40e6
+
+
+def test_config1_gloo_world2_activation_checkpointing_matches():
+    """DDP over gloo with every block stack recomputed in backward trains like the plain run."""
+    plain = run_ranks(_config1, 2, timeout_s=120, join_s=600)
+    ckpt = run_ranks(_config1, 2, args=("all",), timeout_s=120, join_s=600)
+    assert all(st == "ok" for st, _ in list(plain.values()) + list(ckpt.values())), (plain, ckpt)
+    for r in (0, 1):
+        torch.testing.assert_close(ckpt[r][1]["master"], plain[r][1]["master"], rtol=1e-5, atol=1e-6)
+        for a, b in zip(ckpt[r][1]["losses"], plain[r][1]["losses"]):
+            assert abs(a - b) <= 1e-5 * max(1.0, abs(b)), (a, b)
 
 
 def test_train_cli_writes_report(tmp_path):
